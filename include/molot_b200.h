@@ -1,0 +1,183 @@
+/* molot_b200 — B200 (sm_100a) decode attention behind a plain C ABI.
+ *
+ * Drop-in replacement for the decode-attention path of Molot
+ * (include/molot/attn.h and its call site in include/molot/forward.h).  All
+ * arithmetic is FP32.  Every entry point returns an int status (MOLOT_OK or
+ * a negative MOLOT_ERR_*) and never throws across the ABI.
+ *
+ * Conventions
+ *   - "host" entry points take host pointers, copy to the current CUDA
+ *     device, run, copy back and synchronise: outputs are ready on return,
+ *     as with the reference's functions.
+ *   - "_dev" / handle entry points take device pointers and a cudaStream_t
+ *     (passed as void*, NULL = legacy default stream); they are
+ *     stream-ordered and return once the work is enqueued.
+ *   - Calls that share a scratch workspace (the per-device default one, or a
+ *     handle's own) must be ordered on one stream.
+ *   - K/V base pointers must be 16-byte aligned and K/V strides multiples of
+ *     4 floats (the kernels stream rows with TMA bulk copies); head_dim must
+ *     be 64, 128 or 256 and nq/nkv in {1,2,4,8,16,32} (256: up to 16).
+ */
+#ifndef MOLOT_B200_H
+#define MOLOT_B200_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOLOT_B200_ABI_VERSION 1
+
+enum molot_status {
+  MOLOT_OK = 0,
+  MOLOT_ERR_INVALID = -1,     /* bad argument (sizes, null, alignment) */
+  MOLOT_ERR_CUDA = -2,        /* CUDA runtime error; see molot_last_error() */
+  MOLOT_ERR_NOMEM = -3,       /* device allocation failed */
+  MOLOT_ERR_CACHE_FULL = -4,  /* forward.h:570 "KV cache full" */
+  MOLOT_ERR_CACHE_EMPTY = -5, /* forward.h:580 "shared KV empty" */
+  MOLOT_ERR_UNSUPPORTED = -6, /* head_dim / group size not instantiated */
+  MOLOT_ERR_TIMEOUT = -7,     /* a bounded device-side wait expired */
+  MOLOT_ERR_NO_DEVICE = -8    /* no CUDA device */
+};
+
+/* Human-readable text for a status code. */
+const char* molot_status_string(int status);
+/* Detail of the last error on the calling thread (CUDA error text etc.). */
+const char* molot_last_error(void);
+/* Reads (and clears when `clear` != 0) the device-side status word of the
+ * current device's default workspace; synchronises the device.  Returns
+ * MOLOT_OK or MOLOT_ERR_TIMEOUT. */
+int molot_device_status(int clear);
+
+/* ------------------------------------------------------------------------
+ * attn.h drop-ins: host buffers, synchronous ("ready on return").
+ * The ThreadPool& parameter of the reference is replaced by the current
+ * CUDA device.
+ * ---------------------------------------------------------------------- */
+
+/* Replaces molot::attn_decode_gqa_cache (attn.h:125-177): Q [nq][qhd],
+ * K/V [n][nkv*qhd] slot-major (attn.h:122-124), O [nq][qhd].  Slots
+ * [max(0, pos_cur-window+1), n) are attended when window > 0, all n
+ * otherwise (attn.h:137); an empty range yields zeros, as the reference. */
+int molot_attn_decode_gqa_cache(const float* Q, const float* K, const float* V, float* O, int nq,
+                                int nkv, int n, int qhd, float scale, int pos_cur, int window);
+
+/* Replaces molot::attn_decode_gqa (attn.h:111-120): K/V [nkv][n][d]. */
+int molot_attn_decode_gqa(const float* Q, const float* K, const float* V, float* O, int nq,
+                          int nkv, int n, int d, float scale);
+
+/* Replaces molot::attn_decode_gqa_win (attn.h:178-187): K/V [nkv][n][d]. */
+int molot_attn_decode_gqa_win(const float* Q, const float* K, const float* V, float* O, int nq,
+                              int nkv, int n, int d, float scale, int pos_cur, int window);
+
+/* Replaces molot::attn_decode_head_win (attn.h:57-101): one head, K/V [n][d]. */
+int molot_attn_decode_head_win(const float* Q, const float* K, const float* V, float* out, int n,
+                               int d, float scale, int pos_cur, int window);
+
+/* Replaces molot::attn_decode_head (attn.h:104-107). */
+int molot_attn_decode_head(const float* Q, const float* K, const float* V, float* out, int n,
+                           int d, float scale);
+
+/* Replaces molot::rope_apply (attn.h:19-28) on a host vector of `d` floats
+ * (NEOX half-split pairs), computed on the device. */
+int molot_rope_apply(float* x, int d, int pos, const float* inv_freq);
+
+/* Replaces molot::rope_inv_freq (attn.h:31-33): out[i] = 1/base^(2i/d).
+ * Host-side table set-up (not on the per-token path). */
+int molot_rope_inv_freq(float base, int d, float* out);
+
+/* ------------------------------------------------------------------------
+ * Device-pointer, stream-ordered forms.
+ * ---------------------------------------------------------------------- */
+
+/* Decode attention over any strided contiguous cache: slot t of kv head g at
+ * K + t*stride_t + g*stride_h (elements).  [n][nkv*d] (attn.h:125) is
+ * stride_t = nkv*d, stride_h = d; [nkv][n][d] (attn.h:111) is stride_t = d,
+ * stride_h = n*d.  Uses the current device's default workspace. */
+int molot_attn_decode_strided_dev(const float* Q, const float* K, const float* V, float* O,
+                                  int nq, int nkv, int n, int d, long long stride_t,
+                                  long long stride_h, float scale, int pos_cur, int window,
+                                  void* stream);
+
+/* forward.h:554-575 on device buffers for a [cap][nkv*d] cache: q (nq heads)
+ * and k (nkv heads) get per-head weighted RMSNorm when q_norm / k_norm are
+ * non-null, then NEOX RoPE at `pos` when freq ([d/2]) is non-null; v gets a
+ * plain RMSNorm over all nkv*d values when v_norm != 0.  The rotated q goes
+ * to q_out; k and v are written to slot `slot` of kc / vc. */
+int molot_norm_rope_append_dev(const float* q, const float* k, const float* v, float* q_out,
+                               const float* q_norm, const float* k_norm, int v_norm, float eps,
+                               const float* freq, int pos, float* kc, float* vc, int slot,
+                               int nq, int nkv, int d, void* stream);
+
+/* ------------------------------------------------------------------------
+ * KV cache handle: replaces Runner::KVC (forward.h:48-51) and its up-front
+ * allocation (forward.h:103-110).  Per layer, K and V are [cap][nkv*hd]
+ * FP32 in HBM (256-byte aligned), with a host-side slot count n.
+ * ---------------------------------------------------------------------- */
+typedef struct molot_kv_cache molot_kv_cache;
+
+int molot_kv_create(int n_layers, int nkv, int hd, int cap, molot_kv_cache** out);
+void molot_kv_destroy(molot_kv_cache* kv);
+int molot_kv_length(const molot_kv_cache* kv, int layer);
+int molot_kv_set_length(molot_kv_cache* kv, int layer, int n);
+int molot_kv_layer_data(molot_kv_cache* kv, int layer, float** k, float** v);
+
+/* Copies nrows rows of K and V (each [nrows][nkv*hd], host or device
+ * memory) into slots [slot0, slot0+nrows) of `layer`, stream-ordered; the
+ * bulk write a prefill performs (forward.h:370-392).  Does not change n. */
+int molot_kv_write(molot_kv_cache* kv, int layer, int slot0, int nrows, const float* k,
+                   const float* v, void* stream);
+
+/* forward.h:554-575 for a KV-owning layer: normalise/rotate q into q_out,
+ * normalise/rotate k and (v_norm) v and append them at slot n, n++.
+ * MOLOT_ERR_CACHE_FULL when n == cap (forward.h:570). */
+int molot_attn_append_rope(molot_kv_cache* kv, int layer, const float* q, const float* k,
+                           const float* v, float* q_out, const float* q_norm,
+                           const float* k_norm, int v_norm, float eps, const float* freq,
+                           int pos, int nq, void* stream);
+
+/* forward.h:578-590: attention of q (already rotated) over the cache of
+ * `src_layer` (the layer itself, or its shared-KV source, model.h:565-583)
+ * with its current length.  MOLOT_ERR_CACHE_EMPTY when that length is 0
+ * (forward.h:580). */
+int molot_attn_decode(molot_kv_cache* kv, int src_layer, const float* q, float* o, int nq,
+                      float scale, int pos_cur, int window, void* stream);
+
+/* Synchronises the handle's stream work and reports device-side timeouts. */
+int molot_kv_check(molot_kv_cache* kv, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Paged, batched decode (continuous batching; no counterpart in the
+ * reference, which specifies but does not implement paging,
+ * DESIGN.md:47-48,103 / README.md:113-114 of the reference).
+ * Pools: K and V each [num_pages][nkv][page_size][d] FP32; page_size a
+ * multiple of 16.  block_table [B][max_pages] int32 (device).
+ * ---------------------------------------------------------------------- */
+typedef struct molot_paged_plan molot_paged_plan;
+
+/* A plan fixes the batch shape for one decode step (all layers): sequence
+ * lengths (host array, slots already containing the new token), optional
+ * positions (host, NULL = length-1) and the window.  It owns its scratch. */
+int molot_paged_plan_create(molot_paged_plan** out);
+void molot_paged_plan_destroy(molot_paged_plan* plan);
+int molot_paged_plan_build(molot_paged_plan* plan, int B, int nq, int nkv, int d,
+                           const int* seq_lens, const int* positions, int window, void* stream);
+
+/* Attention for every sequence of the plan: Q, O [B][nq][d] device. */
+int molot_paged_decode(molot_paged_plan* plan, const float* Q, float* O, const float* k_pool,
+                       const float* v_pool, const int* block_table, int max_pages,
+                       int page_size, float scale, void* stream);
+
+/* forward.h:554-575 for a batch: each sequence's new k/v go to slot
+ * seq_lens[b]-1 of its pages; q is normalised/rotated into q_out. */
+int molot_paged_append(molot_paged_plan* plan, const float* q, const float* k, const float* v,
+                       float* q_out, const float* q_norm, const float* k_norm, int v_norm,
+                       float eps, const float* freq, float* k_pool, float* v_pool,
+                       const int* block_table, int max_pages, int page_size, void* stream);
+
+/* Synchronises and reports device-side timeouts of the plan's launches. */
+int molot_paged_check(molot_paged_plan* plan, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOLOT_B200_H */

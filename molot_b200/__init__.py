@@ -1,0 +1,369 @@
+"""molot_b200: B200-native decode attention with the reference's attn.h API.
+
+Python view of the C ABI in ``include/molot_b200.h`` (``libmolot_b200.so``,
+built in-tree by ``python -m molot_b200.build``).  Names, argument meaning
+and error behaviour mirror the reference's functions
+(include/molot/attn.h, the attention segment of include/molot/forward.h):
+
+* host drop-ins on numpy arrays, synchronous:
+  ``attn_decode_gqa_cache``, ``attn_decode_gqa``, ``attn_decode_gqa_win``,
+  ``attn_decode_head``, ``attn_decode_head_win``, ``rope_apply``,
+  ``rope_inv_freq``;
+* stream-ordered device forms on torch CUDA tensors:
+  ``decode_strided``, ``norm_rope_append``;
+* ``KVCache`` (forward.h's per-layer KVC, HBM-resident) with
+  ``append_rope`` / ``decode``;
+* ``PagedPlan`` for batched decode over 16-token pages.
+
+torch is used only to hold device memory and streams.  There is no CPU
+fallback: importing this package fails loudly when the library is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libmolot_b200.so")
+HEADER = os.path.join(os.path.dirname(PKG), "include", "molot_b200.h")
+
+OK = 0
+ERR_INVALID = -1
+ERR_CUDA = -2
+ERR_NOMEM = -3
+ERR_CACHE_FULL = -4
+ERR_CACHE_EMPTY = -5
+ERR_UNSUPPORTED = -6
+ERR_TIMEOUT = -7
+ERR_NO_DEVICE = -8
+
+
+class MolotError(RuntimeError):
+    """A non-zero status from the C ABI (the reference throws
+    std::runtime_error in the same places, forward.h:570,580)."""
+
+    def __init__(self, status: int, text: str, detail: str):
+        super().__init__(f"molot_b200 status {status} ({text}): {detail}")
+        self.status = status
+
+
+if not os.path.isfile(LIB_PATH):
+    raise ImportError(
+        f"molot_b200: CUDA library not built ({LIB_PATH} missing); "
+        "run `python -m molot_b200.build` -- there is no CPU fallback")
+
+_lib = ctypes.CDLL(LIB_PATH)
+
+_p = ctypes.c_void_p
+_i = ctypes.c_int
+_f = ctypes.c_float
+_ll = ctypes.c_longlong
+_pp = ctypes.POINTER(ctypes.c_void_p)
+
+
+def _decl(name, args, res=_i):
+    fn = getattr(_lib, name)
+    fn.argtypes = args
+    fn.restype = res
+    return fn
+
+
+_decl("molot_status_string", [_i], ctypes.c_char_p)
+_decl("molot_last_error", [], ctypes.c_char_p)
+_decl("molot_device_status", [_i])
+_decl("molot_attn_decode_gqa_cache", [_p, _p, _p, _p, _i, _i, _i, _i, _f, _i, _i])
+_decl("molot_attn_decode_gqa", [_p, _p, _p, _p, _i, _i, _i, _i, _f])
+_decl("molot_attn_decode_gqa_win", [_p, _p, _p, _p, _i, _i, _i, _i, _f, _i, _i])
+_decl("molot_attn_decode_head_win", [_p, _p, _p, _p, _i, _i, _f, _i, _i])
+_decl("molot_attn_decode_head", [_p, _p, _p, _p, _i, _i, _f])
+_decl("molot_rope_apply", [_p, _i, _i, _p])
+_decl("molot_rope_inv_freq", [_f, _i, _p])
+_decl("molot_attn_decode_strided_dev", [_p, _p, _p, _p, _i, _i, _i, _i, _ll, _ll, _f, _i, _i, _p])
+_decl("molot_norm_rope_append_dev",
+      [_p, _p, _p, _p, _p, _p, _i, _f, _p, _i, _p, _p, _i, _i, _i, _i, _p])
+_decl("molot_kv_create", [_i, _i, _i, _i, _pp])
+_decl("molot_kv_destroy", [_p], None)
+_decl("molot_kv_length", [_p, _i])
+_decl("molot_kv_set_length", [_p, _i, _i])
+_decl("molot_kv_layer_data", [_p, _i, _pp, _pp])
+_decl("molot_kv_write", [_p, _i, _i, _i, _p, _p, _p])
+_decl("molot_attn_append_rope", [_p, _i, _p, _p, _p, _p, _p, _p, _i, _f, _p, _i, _i, _p])
+_decl("molot_attn_decode", [_p, _i, _p, _p, _i, _f, _i, _i, _p])
+_decl("molot_kv_check", [_p, _p])
+_decl("molot_paged_plan_create", [_pp])
+_decl("molot_paged_plan_destroy", [_p], None)
+_decl("molot_paged_plan_build", [_p, _i, _i, _i, _i, _p, _p, _i, _p])
+_decl("molot_paged_decode", [_p, _p, _p, _p, _p, _p, _i, _i, _f, _p])
+_decl("molot_paged_append", [_p, _p, _p, _p, _p, _p, _p, _i, _f, _p, _p, _p, _p, _i, _i, _p])
+_decl("molot_paged_check", [_p, _p])
+
+
+def library():
+    """The loaded ctypes library (for callers binding extra symbols)."""
+    return _lib
+
+
+def header_symbols(path: str = HEADER) -> list[str]:
+    """Every function the public header declares."""
+    text = open(path).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(molot_[a-z0-9_]+)\s*\(", text)))
+
+
+def status_string(status: int) -> str:
+    return _lib.molot_status_string(status).decode()
+
+
+def last_error() -> str:
+    return _lib.molot_last_error().decode()
+
+
+def check(status: int) -> None:
+    if status != OK:
+        raise MolotError(status, status_string(status), last_error())
+
+
+# ------------------------------------------------------------------ helpers
+
+def _host_f32(a) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    return a
+
+
+def _ptr(a) -> int | None:
+    if a is None:
+        return None
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    if hasattr(a, "data_ptr"):  # torch tensor
+        if not a.is_contiguous():
+            raise ValueError("tensor must be contiguous")
+        return a.data_ptr()
+    return int(a)
+
+
+def _stream_ptr(stream) -> int | None:
+    if stream is None:
+        try:
+            import torch
+            return torch.cuda.current_stream().cuda_stream
+        except Exception:  # pragma: no cover - torch absent
+            return None
+    if hasattr(stream, "cuda_stream"):
+        return stream.cuda_stream
+    return int(stream)
+
+
+def _check_cuda_tensor(t, name):
+    if not (hasattr(t, "is_cuda") and t.is_cuda):
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype.__repr__() != "torch.float32" and str(t.dtype) != "torch.float32":
+        raise ValueError(f"{name} must be float32")
+
+
+class _CudaArray:
+    """Minimal __cuda_array_interface__ exporter used to view library-owned
+    device memory as a torch tensor without copying."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {
+            "data": (ptr, False), "shape": tuple(shape), "typestr": typestr, "version": 3,
+            "strides": None,
+        }
+
+
+# ------------------------------------------------------------------ host drop-ins
+
+def attn_decode_gqa_cache(Q, K, V, nq, nkv, n, qhd, scale, pos_cur, window) -> np.ndarray:
+    """attn.h:125-177 on host arrays: Q [nq*qhd], K/V [n][nkv*qhd] -> O [nq][qhd]."""
+    Q, K, V = _host_f32(Q), _host_f32(K), _host_f32(V)
+    O = np.zeros((nq, qhd), np.float32)
+    check(_lib.molot_attn_decode_gqa_cache(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), nq, nkv, n, qhd,
+                                           scale, pos_cur, window))
+    return O
+
+
+def attn_decode_gqa(Q, K, V, nq, nkv, n, d, scale) -> np.ndarray:
+    """attn.h:111-120: K/V [nkv][n][d]."""
+    Q, K, V = _host_f32(Q), _host_f32(K), _host_f32(V)
+    O = np.zeros((nq, d), np.float32)
+    check(_lib.molot_attn_decode_gqa(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), nq, nkv, n, d, scale))
+    return O
+
+
+def attn_decode_gqa_win(Q, K, V, nq, nkv, n, d, scale, pos_cur, window) -> np.ndarray:
+    """attn.h:178-187: K/V [nkv][n][d], sliding window."""
+    Q, K, V = _host_f32(Q), _host_f32(K), _host_f32(V)
+    O = np.zeros((nq, d), np.float32)
+    check(_lib.molot_attn_decode_gqa_win(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), nq, nkv, n, d, scale,
+                                         pos_cur, window))
+    return O
+
+
+def attn_decode_head_win(Q, K, V, n, d, scale, pos_cur, window) -> np.ndarray:
+    """attn.h:57-101: one head, K/V [n][d]."""
+    Q, K, V = _host_f32(Q), _host_f32(K), _host_f32(V)
+    out = np.zeros(d, np.float32)
+    check(_lib.molot_attn_decode_head_win(_ptr(Q), _ptr(K), _ptr(V), _ptr(out), n, d, scale,
+                                          pos_cur, window))
+    return out
+
+
+def attn_decode_head(Q, K, V, n, d, scale) -> np.ndarray:
+    """attn.h:104-107."""
+    Q, K, V = _host_f32(Q), _host_f32(K), _host_f32(V)
+    out = np.zeros(d, np.float32)
+    check(_lib.molot_attn_decode_head(_ptr(Q), _ptr(K), _ptr(V), _ptr(out), n, d, scale))
+    return out
+
+
+def rope_apply(x, d, pos, inv_freq) -> np.ndarray:
+    """attn.h:19-28 on one head vector (returns the rotated copy)."""
+    x = _host_f32(x).copy()
+    f = _host_f32(inv_freq)
+    check(_lib.molot_rope_apply(_ptr(x), d, pos, _ptr(f)))
+    return x
+
+
+def rope_inv_freq(base, d) -> np.ndarray:
+    """attn.h:31-33."""
+    out = np.zeros(d // 2, np.float32)
+    check(_lib.molot_rope_inv_freq(base, d, _ptr(out)))
+    return out
+
+
+def device_status(clear: bool = True) -> int:
+    """Device-side status of the default workspace (0 or ERR_TIMEOUT)."""
+    return _lib.molot_device_status(1 if clear else 0)
+
+
+# ------------------------------------------------------------------ device forms
+
+def decode_strided(Q, K, V, O, nq, nkv, n, d, stride_t, stride_h, scale, pos_cur, window,
+                   stream=None) -> None:
+    """Stream-ordered decode over a strided contiguous cache (torch tensors)."""
+    check(_lib.molot_attn_decode_strided_dev(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), nq, nkv, n, d,
+                                             stride_t, stride_h, scale, pos_cur, window,
+                                             _stream_ptr(stream)))
+
+
+def norm_rope_append(q, k, v, q_out, q_norm, k_norm, v_norm, eps, freq, pos, kc, vc, slot, nq,
+                     nkv, d, stream=None) -> None:
+    """forward.h:554-575 on device tensors for a [cap][nkv*d] cache."""
+    check(_lib.molot_norm_rope_append_dev(_ptr(q), _ptr(k), _ptr(v), _ptr(q_out), _ptr(q_norm),
+                                          _ptr(k_norm), int(v_norm), eps, _ptr(freq), pos,
+                                          _ptr(kc), _ptr(vc), slot, nq, nkv, d,
+                                          _stream_ptr(stream)))
+
+
+class KVCache:
+    """HBM-resident per-layer KV cache (replaces forward.h's Runner::KVC)."""
+
+    def __init__(self, n_layers: int, nkv: int, hd: int, cap: int):
+        h = ctypes.c_void_p()
+        check(_lib.molot_kv_create(n_layers, nkv, hd, cap, ctypes.byref(h)))
+        self._h = h
+        self.n_layers, self.nkv, self.hd, self.cap = n_layers, nkv, hd, cap
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.molot_kv_destroy(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    def length(self, layer: int) -> int:
+        r = _lib.molot_kv_length(self._h, layer)
+        if r < 0:
+            check(r)
+        return r
+
+    def set_length(self, layer: int, n: int) -> None:
+        check(_lib.molot_kv_set_length(self._h, layer, n))
+
+    def layer_ptrs(self, layer: int) -> tuple[int, int]:
+        k = ctypes.c_void_p()
+        v = ctypes.c_void_p()
+        check(_lib.molot_kv_layer_data(self._h, layer, ctypes.byref(k), ctypes.byref(v)))
+        return k.value, v.value
+
+    def layer_tensors(self, layer: int):
+        """(K, V) torch views [cap][nkv][hd] of the layer's device memory."""
+        import torch
+        kp, vp = self.layer_ptrs(layer)
+        shape = (self.cap, self.nkv, self.hd)
+        return (torch.as_tensor(_CudaArray(kp, shape), device="cuda"),
+                torch.as_tensor(_CudaArray(vp, shape), device="cuda"))
+
+    def write(self, layer: int, slot0: int, k, v, stream=None) -> None:
+        rows = k.shape[0]
+        check(_lib.molot_kv_write(self._h, layer, slot0, rows, _ptr(k), _ptr(v),
+                                  _stream_ptr(stream)))
+
+    def append_rope(self, layer, q, k, v, q_out, q_norm=None, k_norm=None, v_norm=False,
+                    eps=1e-6, freq=None, pos=0, nq=None, stream=None) -> None:
+        nq = nq if nq is not None else q.numel() // self.hd
+        check(_lib.molot_attn_append_rope(self._h, layer, _ptr(q), _ptr(k), _ptr(v), _ptr(q_out),
+                                          _ptr(q_norm), _ptr(k_norm), int(v_norm), eps,
+                                          _ptr(freq), pos, nq, _stream_ptr(stream)))
+
+    def decode(self, src_layer, q, o, scale, pos_cur, window=0, nq=None, stream=None) -> None:
+        nq = nq if nq is not None else q.numel() // self.hd
+        check(_lib.molot_attn_decode(self._h, src_layer, _ptr(q), _ptr(o), nq, scale, pos_cur,
+                                     window, _stream_ptr(stream)))
+
+    def check(self, stream=None) -> None:
+        check(_lib.molot_kv_check(self._h, _stream_ptr(stream)))
+
+
+class PagedPlan:
+    """Batch shape of one decode step over a paged pool (see molot_b200.h)."""
+
+    def __init__(self):
+        h = ctypes.c_void_p()
+        check(_lib.molot_paged_plan_create(ctypes.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.molot_paged_plan_destroy(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def build(self, nq, nkv, d, seq_lens, positions=None, window=0, stream=None) -> None:
+        sl = np.ascontiguousarray(seq_lens, dtype=np.int32)
+        pos = None if positions is None else np.ascontiguousarray(positions, dtype=np.int32)
+        self._keep = (sl, pos)
+        check(_lib.molot_paged_plan_build(self._h, sl.size, nq, nkv, d, _ptr(sl), _ptr(pos),
+                                          window, _stream_ptr(stream)))
+
+    def decode(self, Q, O, k_pool, v_pool, block_table, page_size, scale, stream=None) -> None:
+        check(_lib.molot_paged_decode(self._h, _ptr(Q), _ptr(O), _ptr(k_pool), _ptr(v_pool),
+                                      _ptr(block_table), block_table.shape[1], page_size, scale,
+                                      _stream_ptr(stream)))
+
+    def append(self, q, k, v, q_out, k_pool, v_pool, block_table, page_size, q_norm=None,
+               k_norm=None, v_norm=False, eps=1e-6, freq=None, stream=None) -> None:
+        check(_lib.molot_paged_append(self._h, _ptr(q), _ptr(k), _ptr(v), _ptr(q_out),
+                                      _ptr(q_norm), _ptr(k_norm), int(v_norm), eps, _ptr(freq),
+                                      _ptr(k_pool), _ptr(v_pool), _ptr(block_table),
+                                      block_table.shape[1], page_size, _stream_ptr(stream)))
+
+    def check(self, stream=None) -> None:
+        check(_lib.molot_paged_check(self._h, _stream_ptr(stream)))

@@ -1,0 +1,864 @@
+// C ABI of molot_b200 (include/molot_b200.h): argument checking, scratch
+// workspaces, kernel dispatch, the KV-cache handle and paged plans.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "append.cuh"
+#include "decode.cuh"
+#include "molot_b200.h"
+
+namespace molot {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(e == cudaErrorMemoryAllocation ? MOLOT_ERR_NOMEM : MOLOT_ERR_CUDA,
+              std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define MOLOT_CUDA(call)                                 \
+  do {                                                   \
+    cudaError_t e_ = (call);                             \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call);  \
+  } while (0)
+
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per bounded wait
+constexpr int kMaxPartialFloats = 4096 + 2 * 32;           // G*D + 2G upper bound
+
+int current_device(int* dev) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0)
+    return fail(MOLOT_ERR_NO_DEVICE, "no CUDA device visible");
+  MOLOT_CUDA(cudaGetDevice(dev));
+  return MOLOT_OK;
+}
+
+int sm_count(int dev) {
+  static std::mutex mu;
+  static std::vector<int> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  if ((int)cache.size() <= dev) cache.resize(dev + 1, 0);
+  if (!cache[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = v > 0 ? v : 1;
+  }
+  return cache[dev];
+}
+
+// ------------------------------------------------------------- workspace
+
+// Device scratch owned by one ordered stream of calls: split-KV partials,
+// per-segment tickets (zero between launches), the device status word and
+// plan arrays.  Grows only; growth synchronises the device.
+struct Workspace {
+  int device = -1;
+  float* partials = nullptr;
+  size_t partials_cap = 0;
+  int* counters = nullptr;
+  size_t counters_cap = 0;
+  int* status = nullptr;
+  int* plan = nullptr;
+  size_t plan_cap = 0;
+
+  ~Workspace() { release(); }
+  void release() {
+    if (device < 0) return;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    cudaFree(partials);
+    cudaFree(counters);
+    cudaFree(status);
+    cudaFree(plan);
+    if (prev >= 0) cudaSetDevice(prev);
+    partials = nullptr;
+    counters = nullptr;
+    status = nullptr;
+    plan = nullptr;
+    partials_cap = counters_cap = plan_cap = 0;
+  }
+
+  int ensure(int dev, size_t partial_floats, size_t ncounters, size_t plan_ints) {
+    if (device >= 0 && device != dev)
+      return fail(MOLOT_ERR_INVALID, "workspace used on a different device than it was made on");
+    device = dev;
+    const bool grow = partial_floats > partials_cap || ncounters > counters_cap ||
+                      plan_ints > plan_cap || !status;
+    if (!grow) return MOLOT_OK;
+    MOLOT_CUDA(cudaDeviceSynchronize());
+    if (!status) {
+      MOLOT_CUDA(cudaMalloc(&status, 256));
+      MOLOT_CUDA(cudaMemset(status, 0, 256));
+    }
+    if (partial_floats > partials_cap) {
+      cudaFree(partials);
+      partials = nullptr;
+      const size_t cap = std::max(partial_floats, (size_t)2 * sm_count(dev) * kMaxPartialFloats);
+      MOLOT_CUDA(cudaMalloc(&partials, cap * sizeof(float)));
+      partials_cap = cap;
+    }
+    if (ncounters > counters_cap) {
+      cudaFree(counters);
+      counters = nullptr;
+      const size_t cap = std::max<size_t>(ncounters, 4096);
+      MOLOT_CUDA(cudaMalloc(&counters, cap * sizeof(int)));
+      MOLOT_CUDA(cudaMemset(counters, 0, cap * sizeof(int)));
+      counters_cap = cap;
+    }
+    if (plan_ints > plan_cap) {
+      cudaFree(plan);
+      plan = nullptr;
+      const size_t cap = std::max<size_t>(plan_ints, 4096);
+      MOLOT_CUDA(cudaMalloc(&plan, cap * sizeof(int)));
+      plan_cap = cap;
+    }
+    return MOLOT_OK;
+  }
+
+  int check(cudaStream_t st, bool clear) {
+    if (!status) return MOLOT_OK;
+    int h = 0;
+    MOLOT_CUDA(cudaMemcpyAsync(&h, status, sizeof(int), cudaMemcpyDeviceToHost, st));
+    MOLOT_CUDA(cudaStreamSynchronize(st));
+    if (h != 0) {
+      if (clear) {
+        MOLOT_CUDA(cudaMemsetAsync(status, 0, sizeof(int), st));
+        // A launch that gave up may have left tickets behind.
+        MOLOT_CUDA(cudaMemsetAsync(counters, 0, counters_cap * sizeof(int), st));
+        MOLOT_CUDA(cudaStreamSynchronize(st));
+      }
+      return fail(MOLOT_ERR_TIMEOUT, h == kDevErrConsumerTimeout
+                                         ? "device wait for a KV tile timed out"
+                                         : "device wait for a free KV stage timed out");
+    }
+    return MOLOT_OK;
+  }
+};
+
+// ------------------------------------------------------------- dispatch
+
+struct KernelRef {
+  const void* fn = nullptr;
+  int smem = 0;
+};
+
+template <int D, int GS, int HS>
+KernelRef decode_ref() {
+  return {reinterpret_cast<const void*>(&gqa_decode_kernel<D, GS, HS>), DecodeSmem<D, GS>::kTotal};
+}
+
+bool pick_decode(int D, int G, KernelRef* k) {
+  switch (D) {
+    case 64:
+      switch (G) {
+        case 1: *k = decode_ref<64, 1, 1>(); return true;
+        case 2: *k = decode_ref<64, 2, 1>(); return true;
+        case 4: *k = decode_ref<64, 4, 1>(); return true;
+        case 8: *k = decode_ref<64, 8, 1>(); return true;
+        case 16: *k = decode_ref<64, 8, 2>(); return true;
+        case 32: *k = decode_ref<64, 8, 4>(); return true;
+      }
+      return false;
+    case 128:
+      switch (G) {
+        case 1: *k = decode_ref<128, 1, 1>(); return true;
+        case 2: *k = decode_ref<128, 2, 1>(); return true;
+        case 4: *k = decode_ref<128, 4, 1>(); return true;
+        case 8: *k = decode_ref<128, 4, 2>(); return true;
+        case 16: *k = decode_ref<128, 4, 4>(); return true;
+        case 32: *k = decode_ref<128, 4, 8>(); return true;
+      }
+      return false;
+    case 256:
+      switch (G) {
+        case 1: *k = decode_ref<256, 1, 1>(); return true;
+        case 2: *k = decode_ref<256, 2, 1>(); return true;
+        case 4: *k = decode_ref<256, 2, 2>(); return true;
+        case 8: *k = decode_ref<256, 2, 4>(); return true;
+        case 16: *k = decode_ref<256, 2, 8>(); return true;
+      }
+      return false;
+  }
+  return false;
+}
+
+const void* pick_append(int D) {
+  switch (D) {
+    case 64: return reinterpret_cast<const void*>(&norm_rope_append_kernel<64>);
+    case 128: return reinterpret_cast<const void*>(&norm_rope_append_kernel<128>);
+    case 256: return reinterpret_cast<const void*>(&norm_rope_append_kernel<256>);
+  }
+  return nullptr;
+}
+
+int prepare_kernel(const KernelRef& k, int dev) {
+  // The dynamic shared-memory opt-in is per function and device.
+  static std::mutex mu;
+  static std::vector<std::pair<const void*, int>> done;
+  std::lock_guard<std::mutex> lk(mu);
+  for (auto& p : done)
+    if (p.first == k.fn && p.second == dev) return MOLOT_OK;
+  MOLOT_CUDA(cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem));
+  done.emplace_back(k.fn, dev);
+  return MOLOT_OK;
+}
+
+int launch(const void* fn, dim3 grid, dim3 block, int smem, cudaStream_t st, void* arg) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = nullptr;
+  cfg.numAttrs = 0;
+  void* args[] = {arg};
+  MOLOT_CUDA(cudaLaunchKernelExC(&cfg, fn, args));
+  return MOLOT_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int window_start(int pos_cur, int window) {
+  return (window > 0 && pos_cur - window + 1 > 0) ? pos_cur - window + 1 : 0;
+}
+
+int check_shape(int nq, int nkv, int d, KernelRef* k) {
+  if (nq <= 0 || nkv <= 0 || d <= 0) return fail(MOLOT_ERR_INVALID, "nq, nkv and d must be > 0");
+  if (nq % nkv) return fail(MOLOT_ERR_INVALID, "nq must be a multiple of nkv");
+  if (!pick_decode(d, nq / nkv, k))
+    return fail(MOLOT_ERR_UNSUPPORTED, "head_dim / group size combination not built: d=" +
+                                           std::to_string(d) +
+                                           " group=" + std::to_string(nq / nkv));
+  return MOLOT_OK;
+}
+
+// Single-sequence decode over a strided contiguous cache.
+int decode_uniform(Workspace& ws, const float* Q, float* O, const float* K, const float* V,
+                   int nq, int nkv, int n, int d, long long stride_t, long long stride_h,
+                   float scale, int pos_cur, int window, cudaStream_t st) {
+  KernelRef k;
+  int rc = check_shape(nq, nkv, d, &k);
+  if (rc) return rc;
+  if (!Q || !O || !K || !V) return fail(MOLOT_ERR_INVALID, "null pointer");
+  if (n < 0) return fail(MOLOT_ERR_INVALID, "n must be >= 0");
+  if (!aligned16(K) || !aligned16(V) || (stride_t & 3) || (stride_h & 3))
+    return fail(MOLOT_ERR_INVALID, "K/V must be 16-byte aligned with strides multiple of 4 floats");
+  int dev;
+  if ((rc = current_device(&dev))) return rc;
+  const int t0 = window_start(pos_cur, window);
+  if (n <= t0) {  // empty range: the reference leaves zeros (attn.h:163)
+    MOLOT_CUDA(cudaMemsetAsync(O, 0, sizeof(float) * (size_t)nq * d, st));
+    return MOLOT_OK;
+  }
+  const int blo = t0 / kBlk;
+  const int nblk = (n + kBlk - 1) / kBlk - blo;
+  const long long NB = (long long)nkv * nblk;
+  const int grid = (int)std::min<long long>(NB, sm_count(dev));
+  const int G = nq / nkv;
+  if ((rc = ws.ensure(dev, (size_t)2 * grid * (G * d + 2 * G), nkv, 0))) return rc;
+  if ((rc = prepare_kernel(k, dev))) return rc;
+  DecodeArgs a = {};
+  a.Q = Q;
+  a.q_bstride = (long long)nq * d;
+  a.O = O;
+  a.o_bstride = (long long)nq * d;
+  a.K = K;
+  a.V = V;
+  a.kv_bstride = 0;
+  a.stride_t = stride_t;
+  a.stride_h = stride_h;
+  a.block_table = nullptr;
+  a.nkv = nkv;
+  a.G = G;
+  a.scale = scale;
+  a.uniform = 1;
+  a.n = n;
+  a.t0 = t0;
+  a.S = nkv;
+  a.NB = NB;
+  a.nblk_u = nblk;
+  a.blo_u = blo;
+  a.partials = ws.partials;
+  a.counters = ws.counters;
+  a.status = ws.status;
+  a.timeout_ns = kWaitLimitNs;
+  return launch(k.fn, dim3(grid), dim3(kDecodeThreads), k.smem, st, &a);
+}
+
+int append_launch(const AppendArgs& a, int d, int B, cudaStream_t st) {
+  const void* fn = pick_append(d);
+  if (!fn) return fail(MOLOT_ERR_UNSUPPORTED, "head_dim not built: " + std::to_string(d));
+  const int heads = a.nq + a.nkv;
+  AppendArgs copy = a;
+  return launch(fn, dim3((heads + kAppendWarps - 1) / kAppendWarps, B), dim3(kAppendWarps * 32), 0,
+                st, &copy);
+}
+
+// ------------------------------------------------------------- host-call context
+
+// Per-device state behind the synchronous host-buffer drop-ins.
+struct HostCtx {
+  std::mutex mu;
+  int device = -1;
+  cudaStream_t stream = nullptr;
+  Workspace ws;
+  float* buf = nullptr;
+  size_t buf_cap = 0;  // floats
+
+  int init(int dev) {
+    if (device == dev) return MOLOT_OK;
+    device = dev;
+    MOLOT_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    return MOLOT_OK;
+  }
+  int reserve(size_t floats) {
+    if (floats <= buf_cap) return MOLOT_OK;
+    if (buf) cudaFree(buf);
+    buf = nullptr;
+    buf_cap = 0;
+    MOLOT_CUDA(cudaMalloc(&buf, floats * sizeof(float)));
+    buf_cap = floats;
+    return MOLOT_OK;
+  }
+};
+
+HostCtx& host_ctx(int dev) {
+  static std::mutex mu;
+  static std::vector<HostCtx*> ctxs;
+  std::lock_guard<std::mutex> lk(mu);
+  if ((int)ctxs.size() <= dev) ctxs.resize(dev + 1, nullptr);
+  if (!ctxs[dev]) ctxs[dev] = new HostCtx();  // lives until process exit
+  return *ctxs[dev];
+}
+
+size_t round4(size_t x) { return (x + 63) & ~size_t(63); }
+
+// Copies Q/K/V in, runs decode_uniform over the staged copy, copies O out.
+int host_decode(const float* Q, const float* K, const float* V, float* O, int nq, int nkv, int n,
+                int d, bool head_major, float scale, int pos_cur, int window) {
+  if (!Q || !K || !V || !O) return fail(MOLOT_ERR_INVALID, "null pointer");
+  if (n < 0 || nq <= 0 || nkv <= 0 || d <= 0)
+    return fail(MOLOT_ERR_INVALID, "sizes must be positive");
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  HostCtx& c = host_ctx(dev);
+  std::lock_guard<std::mutex> lk(c.mu);
+  if ((rc = c.init(dev))) return rc;
+  const size_t qn = (size_t)nq * d, kvn = (size_t)n * nkv * d;
+  const size_t oq = 0, ok = round4(qn), ov = ok + round4(kvn), oo = ov + round4(kvn);
+  if ((rc = c.reserve(oo + round4(qn)))) return rc;
+  float* dq = c.buf + oq;
+  float* dk = c.buf + ok;
+  float* dv = c.buf + ov;
+  float* dout = c.buf + oo;
+  MOLOT_CUDA(cudaMemcpyAsync(dq, Q, qn * 4, cudaMemcpyHostToDevice, c.stream));
+  if (kvn) {
+    MOLOT_CUDA(cudaMemcpyAsync(dk, K, kvn * 4, cudaMemcpyHostToDevice, c.stream));
+    MOLOT_CUDA(cudaMemcpyAsync(dv, V, kvn * 4, cudaMemcpyHostToDevice, c.stream));
+  }
+  const long long st_t = head_major ? d : (long long)nkv * d;
+  const long long st_h = head_major ? (long long)n * d : d;
+  rc = decode_uniform(c.ws, dq, dout, dk, dv, nq, nkv, n, d, st_t, st_h, scale, pos_cur, window,
+                      c.stream);
+  if (rc) return rc;
+  MOLOT_CUDA(cudaMemcpyAsync(O, dout, qn * 4, cudaMemcpyDeviceToHost, c.stream));
+  MOLOT_CUDA(cudaStreamSynchronize(c.stream));
+  return c.ws.check(c.stream, true);
+}
+
+}  // namespace
+}  // namespace molot
+
+using namespace molot;
+
+// ===================================================================== C ABI
+
+struct molot_kv_cache {
+  int device = -1;
+  int n_layers = 0, nkv = 0, hd = 0, cap = 0;
+  size_t layer_floats = 0;  // per K (or V) of one layer, padded
+  float* base = nullptr;
+  std::vector<int> len;
+  Workspace ws;
+};
+
+struct molot_paged_plan {
+  int device = -1;
+  Workspace ws;
+  int* h_plan = nullptr;  // pinned staging
+  size_t h_cap = 0;
+  cudaEvent_t uploaded = nullptr;
+  bool built = false;
+  int B = 0, nq = 0, nkv = 0, d = 0, window = 0, grid = 0, S = 0;
+  long long NB = 0;
+  // offsets (ints) into ws.plan
+  size_t o_n = 0, o_t0 = 0, o_pos = 0, o_slot = 0, o_prefix = 0, o_cta = 0;
+  std::vector<int> h_n, h_t0, h_pos, h_slot, h_prefix, h_cta;
+  bool all_empty = false;
+};
+
+extern "C" {
+
+const char* molot_status_string(int status) {
+  switch (status) {
+    case MOLOT_OK: return "ok";
+    case MOLOT_ERR_INVALID: return "invalid argument";
+    case MOLOT_ERR_CUDA: return "CUDA error";
+    case MOLOT_ERR_NOMEM: return "out of device memory";
+    case MOLOT_ERR_CACHE_FULL: return "KV cache full";
+    case MOLOT_ERR_CACHE_EMPTY: return "shared KV empty";
+    case MOLOT_ERR_UNSUPPORTED: return "unsupported shape";
+    case MOLOT_ERR_TIMEOUT: return "device wait timed out";
+    case MOLOT_ERR_NO_DEVICE: return "no CUDA device";
+  }
+  return "unknown status";
+}
+
+const char* molot_last_error(void) { return g_last_error.c_str(); }
+
+int molot_device_status(int clear) {
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  HostCtx& c = host_ctx(dev);
+  std::lock_guard<std::mutex> lk(c.mu);
+  if ((rc = c.init(dev))) return rc;
+  MOLOT_CUDA(cudaDeviceSynchronize());
+  return c.ws.check(c.stream, clear != 0);
+}
+
+// ---------------------------------------------------------------- drop-ins
+
+int molot_attn_decode_gqa_cache(const float* Q, const float* K, const float* V, float* O, int nq,
+                                int nkv, int n, int qhd, float scale, int pos_cur, int window) {
+  return host_decode(Q, K, V, O, nq, nkv, n, qhd, false, scale, pos_cur, window);
+}
+
+int molot_attn_decode_gqa(const float* Q, const float* K, const float* V, float* O, int nq,
+                          int nkv, int n, int d, float scale) {
+  // attn.h:106: the full causal prefix (window 0).
+  return host_decode(Q, K, V, O, nq, nkv, n, d, true, scale, n > 0 ? n : 0, 0);
+}
+
+int molot_attn_decode_gqa_win(const float* Q, const float* K, const float* V, float* O, int nq,
+                              int nkv, int n, int d, float scale, int pos_cur, int window) {
+  return host_decode(Q, K, V, O, nq, nkv, n, d, true, scale, pos_cur, window);
+}
+
+int molot_attn_decode_head_win(const float* Q, const float* K, const float* V, float* out, int n,
+                               int d, float scale, int pos_cur, int window) {
+  return host_decode(Q, K, V, out, 1, 1, n, d, true, scale, pos_cur, window);
+}
+
+int molot_attn_decode_head(const float* Q, const float* K, const float* V, float* out, int n,
+                           int d, float scale) {
+  return host_decode(Q, K, V, out, 1, 1, n, d, true, scale, n > 0 ? n : 0, 0);
+}
+
+int molot_rope_apply(float* x, int d, int pos, const float* inv_freq) {
+  if (!x || !inv_freq || d <= 0 || (d & 1)) return fail(MOLOT_ERR_INVALID, "bad rope arguments");
+  if (!pick_append(d)) return fail(MOLOT_ERR_UNSUPPORTED, "head_dim not built");
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  HostCtx& c = host_ctx(dev);
+  std::lock_guard<std::mutex> lk(c.mu);
+  if ((rc = c.init(dev))) return rc;
+  if ((rc = c.reserve(round4(d) + round4(d / 2)))) return rc;
+  float* dx = c.buf;
+  float* df = c.buf + round4(d);
+  MOLOT_CUDA(cudaMemcpyAsync(dx, x, (size_t)d * 4, cudaMemcpyHostToDevice, c.stream));
+  MOLOT_CUDA(cudaMemcpyAsync(df, inv_freq, (size_t)(d / 2) * 4, cudaMemcpyHostToDevice, c.stream));
+  AppendArgs a = {};
+  a.q_in = dx;
+  a.q_out = dx;
+  a.freq = df;
+  a.nq = 1;
+  a.nkv = 0;
+  a.pos = pos;
+  if ((rc = append_launch(a, d, 1, c.stream))) return rc;
+  MOLOT_CUDA(cudaMemcpyAsync(x, dx, (size_t)d * 4, cudaMemcpyDeviceToHost, c.stream));
+  MOLOT_CUDA(cudaStreamSynchronize(c.stream));
+  return MOLOT_OK;
+}
+
+int molot_rope_inv_freq(float base, int d, float* out) {
+  if (!out || d <= 0) return fail(MOLOT_ERR_INVALID, "bad rope_inv_freq arguments");
+  for (int i = 0; i < d / 2; ++i) out[i] = 1.0f / std::pow(base, (2.0f * (float)i) / (float)d);
+  return MOLOT_OK;
+}
+
+// ---------------------------------------------------------------- device forms
+
+int molot_attn_decode_strided_dev(const float* Q, const float* K, const float* V, float* O,
+                                  int nq, int nkv, int n, int d, long long stride_t,
+                                  long long stride_h, float scale, int pos_cur, int window,
+                                  void* stream) {
+  KernelRef k;
+  int dev, rc;
+  if ((rc = check_shape(nq, nkv, d, &k))) return rc;
+  if ((rc = current_device(&dev))) return rc;
+  HostCtx& c = host_ctx(dev);
+  std::lock_guard<std::mutex> lk(c.mu);
+  return decode_uniform(c.ws, Q, O, K, V, nq, nkv, n, d, stride_t, stride_h, scale, pos_cur,
+                        window, (cudaStream_t)stream);
+}
+
+int molot_norm_rope_append_dev(const float* q, const float* k, const float* v, float* q_out,
+                               const float* q_norm, const float* k_norm, int v_norm, float eps,
+                               const float* freq, int pos, float* kc, float* vc, int slot,
+                               int nq, int nkv, int d, void* stream) {
+  if (!q || !k || !v || !q_out || !kc || !vc) return fail(MOLOT_ERR_INVALID, "null pointer");
+  if (nq <= 0 || nkv <= 0 || slot < 0) return fail(MOLOT_ERR_INVALID, "bad sizes");
+  AppendArgs a = {};
+  a.q_in = q;
+  a.k_in = k;
+  a.v_in = v;
+  a.q_out = q_out;
+  a.q_norm = q_norm;
+  a.k_norm = k_norm;
+  a.v_norm = v_norm;
+  a.eps = eps;
+  a.freq = freq;
+  a.nq = nq;
+  a.nkv = nkv;
+  a.pos = pos;
+  a.slot = slot;
+  a.K = kc;
+  a.V = vc;
+  a.stride_t = (long long)nkv * d;
+  a.stride_h = d;
+  return append_launch(a, d, 1, (cudaStream_t)stream);
+}
+
+// ---------------------------------------------------------------- KV cache handle
+
+int molot_kv_create(int n_layers, int nkv, int hd, int cap, molot_kv_cache** out) {
+  if (!out) return fail(MOLOT_ERR_INVALID, "null out");
+  *out = nullptr;
+  if (n_layers <= 0 || nkv <= 0 || hd <= 0 || cap <= 0)
+    return fail(MOLOT_ERR_INVALID, "sizes must be positive");
+  if (!pick_append(hd)) return fail(MOLOT_ERR_UNSUPPORTED, "head_dim not built");
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  auto* kv = new molot_kv_cache();
+  kv->device = dev;
+  kv->n_layers = n_layers;
+  kv->nkv = nkv;
+  kv->hd = hd;
+  kv->cap = cap;
+  kv->layer_floats = ((size_t)cap * nkv * hd + 63) & ~size_t(63);  // 256-byte aligned layers
+  kv->len.assign(n_layers, 0);
+  cudaError_t e = cudaMalloc(&kv->base, kv->layer_floats * 2 * n_layers * sizeof(float));
+  if (e != cudaSuccess) {
+    delete kv;
+    return cuda_fail(e, "cudaMalloc(kv cache)");
+  }
+  *out = kv;
+  return MOLOT_OK;
+}
+
+void molot_kv_destroy(molot_kv_cache* kv) {
+  if (!kv) return;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(kv->device);
+  cudaDeviceSynchronize();
+  cudaFree(kv->base);
+  kv->ws.release();
+  if (prev >= 0) cudaSetDevice(prev);
+  delete kv;
+}
+
+int molot_kv_length(const molot_kv_cache* kv, int layer) {
+  if (!kv || layer < 0 || layer >= kv->n_layers) return fail(MOLOT_ERR_INVALID, "bad layer");
+  return kv->len[layer];
+}
+
+int molot_kv_set_length(molot_kv_cache* kv, int layer, int n) {
+  if (!kv || layer < 0 || layer >= kv->n_layers || n < 0 || n > kv->cap)
+    return fail(MOLOT_ERR_INVALID, "bad layer or length");
+  kv->len[layer] = n;
+  return MOLOT_OK;
+}
+
+int molot_kv_layer_data(molot_kv_cache* kv, int layer, float** k, float** v) {
+  if (!kv || layer < 0 || layer >= kv->n_layers) return fail(MOLOT_ERR_INVALID, "bad layer");
+  if (k) *k = kv->base + (size_t)(2 * layer) * kv->layer_floats;
+  if (v) *v = kv->base + (size_t)(2 * layer + 1) * kv->layer_floats;
+  return MOLOT_OK;
+}
+
+int molot_kv_write(molot_kv_cache* kv, int layer, int slot0, int nrows, const float* k,
+                   const float* v, void* stream) {
+  if (!kv || layer < 0 || layer >= kv->n_layers) return fail(MOLOT_ERR_INVALID, "bad layer");
+  if (!k || !v || slot0 < 0 || nrows < 0 || slot0 + nrows > kv->cap)
+    return fail(MOLOT_ERR_INVALID, "rows outside the cache");
+  float *kc, *vc;
+  molot_kv_layer_data(kv, layer, &kc, &vc);
+  const size_t row = (size_t)kv->nkv * kv->hd;
+  cudaStream_t st = (cudaStream_t)stream;
+  MOLOT_CUDA(cudaMemcpyAsync(kc + slot0 * row, k, nrows * row * sizeof(float), cudaMemcpyDefault, st));
+  MOLOT_CUDA(cudaMemcpyAsync(vc + slot0 * row, v, nrows * row * sizeof(float), cudaMemcpyDefault, st));
+  return MOLOT_OK;
+}
+
+int molot_attn_append_rope(molot_kv_cache* kv, int layer, const float* q, const float* k,
+                           const float* v, float* q_out, const float* q_norm,
+                           const float* k_norm, int v_norm, float eps, const float* freq,
+                           int pos, int nq, void* stream) {
+  if (!kv || layer < 0 || layer >= kv->n_layers) return fail(MOLOT_ERR_INVALID, "bad layer");
+  if (kv->len[layer] >= kv->cap) return fail(MOLOT_ERR_CACHE_FULL, "fwd: KV cache full");
+  float *kc, *vc;
+  molot_kv_layer_data(kv, layer, &kc, &vc);
+  int rc = molot_norm_rope_append_dev(q, k, v, q_out, q_norm, k_norm, v_norm, eps, freq, pos, kc,
+                                      vc, kv->len[layer], nq, kv->nkv, kv->hd, stream);
+  if (rc) return rc;
+  kv->len[layer]++;
+  return MOLOT_OK;
+}
+
+int molot_attn_decode(molot_kv_cache* kv, int src_layer, const float* q, float* o, int nq,
+                      float scale, int pos_cur, int window, void* stream) {
+  if (!kv || src_layer < 0 || src_layer >= kv->n_layers)
+    return fail(MOLOT_ERR_INVALID, "bad layer");
+  const int n = kv->len[src_layer];
+  if (n == 0) return fail(MOLOT_ERR_CACHE_EMPTY, "fwd: shared KV empty");
+  float *kc, *vc;
+  molot_kv_layer_data(kv, src_layer, &kc, &vc);
+  return decode_uniform(kv->ws, q, o, kc, vc, nq, kv->nkv, n, kv->hd, (long long)kv->nkv * kv->hd,
+                        kv->hd, scale, pos_cur, window, (cudaStream_t)stream);
+}
+
+int molot_kv_check(molot_kv_cache* kv, void* stream) {
+  if (!kv) return fail(MOLOT_ERR_INVALID, "null handle");
+  MOLOT_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  MOLOT_CUDA(cudaGetLastError());
+  return kv->ws.check((cudaStream_t)stream, true);
+}
+
+// ---------------------------------------------------------------- paged plans
+
+int molot_paged_plan_create(molot_paged_plan** out) {
+  if (!out) return fail(MOLOT_ERR_INVALID, "null out");
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  auto* p = new molot_paged_plan();
+  p->device = dev;
+  cudaError_t e = cudaEventCreateWithFlags(&p->uploaded, cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    delete p;
+    return cuda_fail(e, "cudaEventCreate");
+  }
+  *out = p;
+  return MOLOT_OK;
+}
+
+void molot_paged_plan_destroy(molot_paged_plan* p) {
+  if (!p) return;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(p->device);
+  cudaDeviceSynchronize();
+  if (p->h_plan) cudaFreeHost(p->h_plan);
+  if (p->uploaded) cudaEventDestroy(p->uploaded);
+  p->ws.release();
+  if (prev >= 0) cudaSetDevice(prev);
+  delete p;
+}
+
+int molot_paged_plan_build(molot_paged_plan* p, int B, int nq, int nkv, int d,
+                           const int* seq_lens, const int* positions, int window, void* stream) {
+  if (!p || !seq_lens || B <= 0) return fail(MOLOT_ERR_INVALID, "bad plan arguments");
+  KernelRef k;
+  int rc = check_shape(nq, nkv, d, &k);
+  if (rc) return rc;
+  const int S = B * nkv;
+  p->h_n.assign(seq_lens, seq_lens + B);
+  p->h_t0.resize(B);
+  p->h_pos.resize(B);
+  p->h_slot.resize(B);
+  p->h_prefix.resize(S + 1);
+  long long NB = 0;
+  for (int b = 0; b < B; ++b) {
+    const int n = seq_lens[b];
+    if (n < 0) return fail(MOLOT_ERR_INVALID, "negative sequence length");
+    const int pos = positions ? positions[b] : n - 1;
+    const int t0 = window_start(pos, window);
+    p->h_pos[b] = pos;
+    p->h_slot[b] = n - 1;
+    p->h_t0[b] = t0;
+    const int nblk = n > t0 ? (n + kBlk - 1) / kBlk - t0 / kBlk : 0;
+    for (int g = 0; g < nkv; ++g) {
+      p->h_prefix[b * nkv + g] = (int)NB;
+      NB += nblk;
+    }
+  }
+  p->h_prefix[S] = (int)NB;
+  if (NB >= (1ll << 31)) return fail(MOLOT_ERR_INVALID, "batch too large");
+  int dev;
+  if ((rc = current_device(&dev))) return rc;
+  if (dev != p->device) return fail(MOLOT_ERR_INVALID, "plan used on another device");
+  const int grid = (int)std::max<long long>(1, std::min<long long>(NB, sm_count(dev)));
+  p->h_cta.resize(grid);
+  {
+    int s = 0;
+    for (int c = 0; c < grid; ++c) {
+      const long long start = (long long)c * NB / grid;
+      while (s < S && p->h_prefix[s + 1] <= start) ++s;
+      p->h_cta[c] = std::min(s, S - 1);
+    }
+  }
+  p->B = B;
+  p->nq = nq;
+  p->nkv = nkv;
+  p->d = d;
+  p->window = window;
+  p->grid = grid;
+  p->S = S;
+  p->NB = NB;
+  p->all_empty = NB == 0;
+  // layout of the uploaded plan
+  p->o_n = 0;
+  p->o_t0 = p->o_n + B;
+  p->o_pos = p->o_t0 + B;
+  p->o_slot = p->o_pos + B;
+  p->o_prefix = p->o_slot + B;
+  p->o_cta = p->o_prefix + S + 1;
+  const size_t total = p->o_cta + grid;
+  const int G = nq / nkv;
+  if ((rc = p->ws.ensure(dev, (size_t)2 * grid * (G * d + 2 * G), S, total))) return rc;
+  if (p->h_cap < total) {
+    if (p->h_plan) {
+      MOLOT_CUDA(cudaEventSynchronize(p->uploaded));
+      cudaFreeHost(p->h_plan);
+      p->h_plan = nullptr;
+    }
+    MOLOT_CUDA(cudaMallocHost(&p->h_plan, total * sizeof(int)));
+    p->h_cap = total;
+  } else if (p->built) {
+    MOLOT_CUDA(cudaEventSynchronize(p->uploaded));  // staging still being read?
+  }
+  std::memcpy(p->h_plan + p->o_n, p->h_n.data(), B * sizeof(int));
+  std::memcpy(p->h_plan + p->o_t0, p->h_t0.data(), B * sizeof(int));
+  std::memcpy(p->h_plan + p->o_pos, p->h_pos.data(), B * sizeof(int));
+  std::memcpy(p->h_plan + p->o_slot, p->h_slot.data(), B * sizeof(int));
+  std::memcpy(p->h_plan + p->o_prefix, p->h_prefix.data(), (S + 1) * sizeof(int));
+  std::memcpy(p->h_plan + p->o_cta, p->h_cta.data(), grid * sizeof(int));
+  cudaStream_t st = (cudaStream_t)stream;
+  MOLOT_CUDA(cudaMemcpyAsync(p->ws.plan, p->h_plan, total * sizeof(int), cudaMemcpyHostToDevice, st));
+  MOLOT_CUDA(cudaEventRecord(p->uploaded, st));
+  p->built = true;
+  return MOLOT_OK;
+}
+
+int molot_paged_decode(molot_paged_plan* p, const float* Q, float* O, const float* k_pool,
+                       const float* v_pool, const int* block_table, int max_pages,
+                       int page_size, float scale, void* stream) {
+  if (!p || !p->built) return fail(MOLOT_ERR_INVALID, "plan not built");
+  if (!Q || !O || !k_pool || !v_pool || !block_table) return fail(MOLOT_ERR_INVALID, "null pointer");
+  if (page_size <= 0 || page_size % kBlk) return fail(MOLOT_ERR_INVALID, "page_size must be a multiple of 16");
+  if (!aligned16(k_pool) || !aligned16(v_pool)) return fail(MOLOT_ERR_INVALID, "pools must be 16-byte aligned");
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  if (dev != p->device) return fail(MOLOT_ERR_INVALID, "plan used on another device");
+  KernelRef k;
+  if ((rc = check_shape(p->nq, p->nkv, p->d, &k))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  // Sequences with an empty attended range produce zeros (attn.h:163).
+  bool any_empty = false;
+  for (int b = 0; b < p->B; ++b) any_empty |= p->h_n[b] <= p->h_t0[b];
+  if (any_empty) {
+    for (int b = 0; b < p->B; ++b)
+      if (p->h_n[b] <= p->h_t0[b])
+        MOLOT_CUDA(cudaMemsetAsync(O + (size_t)b * p->nq * p->d, 0, sizeof(float) * p->nq * p->d, st));
+  }
+  if (p->all_empty) return MOLOT_OK;
+  if ((rc = prepare_kernel(k, dev))) return rc;
+  DecodeArgs a = {};
+  a.Q = Q;
+  a.q_bstride = (long long)p->nq * p->d;
+  a.O = O;
+  a.o_bstride = (long long)p->nq * p->d;
+  a.K = k_pool;
+  a.V = v_pool;
+  a.block_table = block_table;
+  a.bt_stride = max_pages;
+  a.page_size = page_size;
+  a.page_stride = (long long)p->nkv * page_size * p->d;
+  a.page_hstride = (long long)page_size * p->d;
+  a.nkv = p->nkv;
+  a.G = p->nq / p->nkv;
+  a.scale = scale;
+  a.uniform = 0;
+  a.seq_n = p->ws.plan + p->o_n;
+  a.seq_t0 = p->ws.plan + p->o_t0;
+  a.seg_prefix = p->ws.plan + p->o_prefix;
+  a.cta_seg = p->ws.plan + p->o_cta;
+  a.S = p->S;
+  a.NB = p->NB;
+  a.partials = p->ws.partials;
+  a.counters = p->ws.counters;
+  a.status = p->ws.status;
+  a.timeout_ns = kWaitLimitNs;
+  return launch(k.fn, dim3(p->grid), dim3(kDecodeThreads), k.smem, st, &a);
+}
+
+int molot_paged_append(molot_paged_plan* p, const float* q, const float* k, const float* v,
+                       float* q_out, const float* q_norm, const float* k_norm, int v_norm,
+                       float eps, const float* freq, float* k_pool, float* v_pool,
+                       const int* block_table, int max_pages, int page_size, void* stream) {
+  if (!p || !p->built) return fail(MOLOT_ERR_INVALID, "plan not built");
+  if (!q || !k || !v || !q_out || !k_pool || !v_pool || !block_table)
+    return fail(MOLOT_ERR_INVALID, "null pointer");
+  if (page_size <= 0 || page_size % kBlk) return fail(MOLOT_ERR_INVALID, "page_size must be a multiple of 16");
+  for (int b = 0; b < p->B; ++b)
+    if (p->h_n[b] <= 0) return fail(MOLOT_ERR_INVALID, "append needs seq_lens >= 1");
+  AppendArgs a = {};
+  a.q_in = q;
+  a.q_bstride = (long long)p->nq * p->d;
+  a.k_in = k;
+  a.v_in = v;
+  a.kv_in_bstride = (long long)p->nkv * p->d;
+  a.q_out = q_out;
+  a.qo_bstride = (long long)p->nq * p->d;
+  a.q_norm = q_norm;
+  a.k_norm = k_norm;
+  a.v_norm = v_norm;
+  a.eps = eps;
+  a.freq = freq;
+  a.nq = p->nq;
+  a.nkv = p->nkv;
+  a.seq_pos = p->ws.plan + p->o_pos;
+  a.seq_slot = p->ws.plan + p->o_slot;
+  a.K = k_pool;
+  a.V = v_pool;
+  a.block_table = block_table;
+  a.bt_stride = max_pages;
+  a.page_size = page_size;
+  a.page_stride = (long long)p->nkv * page_size * p->d;
+  a.page_hstride = (long long)page_size * p->d;
+  return append_launch(a, p->d, p->B, (cudaStream_t)stream);
+}
+
+int molot_paged_check(molot_paged_plan* p, void* stream) {
+  if (!p) return fail(MOLOT_ERR_INVALID, "null plan");
+  MOLOT_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  MOLOT_CUDA(cudaGetLastError());
+  return p->ws.check((cudaStream_t)stream, true);
+}
+
+}  // extern "C"

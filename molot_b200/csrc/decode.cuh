@@ -1,0 +1,552 @@
+// Split-KV GQA decode attention for sm_100a (flash-decoding, FP32, no tensor
+// cores: batch-1 decode is a bandwidth-bound GEMV).
+//
+// Work decomposition
+//   A *segment* is one (sequence b, kv head g) pair; its KV rows are the
+//   slots [t0_b, n_b) (t0 > 0 for sliding-window layers, attn.h:137).  Slots
+//   are grouped into 16-token *blocks* in absolute slot numbering (block k =
+//   slots [16k, 16k+16), so a block never straddles a 16-token page).  All
+//   segments' blocks are laid end to end (s = b*nkv + g) and the grid's CTAs
+//   take equal contiguous block ranges: CTA c owns [c*NB/grid, (c+1)*NB/grid).
+//   A segment that lies inside one CTA is finished there; one that spans CTAs
+//   leaves a partial (running max, sum, unnormalised output) per CTA, and the
+//   last CTA to finish it (atomic ticket) merges the partials.
+//
+// CTA structure (one CTA per SM, 8 consumer warps + 1 producer warp)
+//   The producer streams tiles of 4 quarters x QR rows of K and V into a ring
+//   of STAGES shared-memory stages with TMA bulk copies (one copy per quarter
+//   when its rows are contiguous in HBM, one per row otherwise), signalling an
+//   mbarrier with the byte count.  Quarters sit 32 bytes apart from one
+//   another so the four 8-lane row groups of a warp read distinct banks.
+//   A consumer warp works on 4 rows at once, 8 lanes per row: lane l of a row
+//   group owns head dimensions {16m + l, 16m + l + 8}, i.e. exactly the two
+//   accumulator lanes l and l+8 of the reference's 16-wide FMA dot
+//   (gemm.h:17-28).  Each lane runs those two fused-multiply-add chains in
+//   the reference's order and the row group finishes with the reference's
+//   reduction tree (l+8 locally, then xor 4, 2, 1), so every QK score is
+//   bit-identical to dot_fp32_avx512(q, k) * scale (attn.h:144).
+//   Softmax is an exp2-based online softmax per row group; row groups, warps
+//   and CTAs are merged with the usual (max, sum) rescaling.
+//   The same lanes then accumulate p * V for their dimensions.
+#pragma once
+#include <cuda_runtime.h>
+#include <math_constants.h>
+
+#include <cstdint>
+
+#include "ptx.cuh"
+
+namespace molot {
+
+constexpr int kBlk = 16;            // partition granularity (tokens)
+constexpr int kConsumerWarps = 8;
+// Three warpgroups: two of consumers, one whose first warp is the producer.
+constexpr int kDecodeThreads = (kConsumerWarps + 4) * 32;
+// Register split after launch (384 threads x 168 registers = 64512):
+// consumers 256 x 232 + producer group 128 x 40 = 64512.
+constexpr int kConsumerRegs = 232;
+constexpr int kProducerRegs = 40;
+static_assert(2 * 128 * kConsumerRegs + 128 * kProducerRegs <= kDecodeThreads * 168,
+              "register split exceeds the launch allocation");
+constexpr int kQuarterPadBytes = 32;
+
+// Status codes written into the device status word.
+constexpr int kDevErrConsumerTimeout = 1;
+constexpr int kDevErrProducerTimeout = 2;
+
+struct DecodeArgs {
+  // Query / output: head h of sequence b at Q + b*q_bstride + h*D.
+  const float* Q;
+  long long q_bstride;
+  float* O;
+  long long o_bstride;
+  // Keys / values, contiguous form: slot t of kv head g of sequence b at
+  // base + b*kv_bstride + t*stride_t + g*stride_h.
+  const float* K;
+  const float* V;
+  long long kv_bstride, stride_t, stride_h;
+  // Paged form (block_table != nullptr): slot t of sequence b lives in page
+  // p = block_table[b*bt_stride + t/page_size], row t%page_size, at
+  // base + p*page_stride + g*page_hstride + (t%page_size)*D.
+  const int* block_table;
+  int bt_stride, page_size;
+  long long page_stride, page_hstride;
+  int nkv, G;
+  float scale;
+  // Segments.
+  int uniform;  // 1: all segments share n / t0 below (single sequence)
+  int n, t0;
+  const int* seq_n;       // planned: [B]
+  const int* seq_t0;      // planned: [B]
+  const int* seg_prefix;  // planned: [S+1] global block offset of segment s
+  const int* cta_seg;     // planned: [grid] segment holding the CTA's first block
+  int S;
+  long long NB;
+  int nblk_u, blo_u;  // uniform: blocks per segment and first block index
+  // Scratch.
+  float* partials;  // [2*grid][G*D + 2*G]
+  int* counters;    // [S], zero between launches
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+template <int D>
+struct TileShape {
+  static constexpr int QR = (D > 128) ? 8 : 16;          // rows per quarter
+  static constexpr int T = 4 * QR;                       // rows per tile
+  static constexpr int TB = T / kBlk;                    // blocks per tile
+  static constexpr int QB = QR * D * 4;                  // quarter bytes
+  static constexpr int QSTRIDE = QB + kQuarterPadBytes;  // quarter pitch (bytes)
+  static constexpr int KQ = 4 * QSTRIDE;                 // K (or V) part of a stage
+  static constexpr int STAGE = 2 * KQ;
+  static constexpr int STAGES_RAW = 204800 / STAGE;  // ~200 KB of ring
+  static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
+};
+
+template <int D, int GS>
+struct DecodeSmem {
+  using TS = TileShape<D>;
+  static constexpr int kStageBytes = TS::STAGES * TS::STAGE;
+  static constexpr int kMergeO = kConsumerWarps * GS * D * 4;
+  static constexpr int kMergeML = kConsumerWarps * GS * 2 * 4;
+  static constexpr int kBars = 2 * TS::STAGES * 8;
+  static constexpr int kTotal = kStageBytes + kMergeO + kMergeML + kBars + 16;
+};
+
+__device__ __forceinline__ long long cta_of_block(long long x, long long NB, int grid) {
+  // Largest c with floor(c*NB/grid) <= x.
+  return ((x + 1) * grid + NB - 1) / NB - 1;
+}
+
+struct SegView {
+  int b, g, n, t0, blo;
+  long long gbeg, gend;
+};
+
+__device__ __forceinline__ SegView seg_view(const DecodeArgs& a, int s) {
+  SegView v;
+  v.b = s / a.nkv;
+  v.g = s - v.b * a.nkv;
+  if (a.uniform) {
+    v.n = a.n;
+    v.t0 = a.t0;
+    v.gbeg = (long long)s * a.nblk_u;
+    v.gend = v.gbeg + a.nblk_u;
+    v.blo = a.blo_u;
+  } else {
+    v.n = __ldg(a.seq_n + v.b);
+    v.t0 = __ldg(a.seq_t0 + v.b);
+    v.gbeg = __ldg(a.seg_prefix + s);
+    v.gend = __ldg(a.seg_prefix + s + 1);
+    v.blo = v.t0 / kBlk;
+  }
+  return v;
+}
+
+__device__ __forceinline__ int first_seg_of_cta(const DecodeArgs& a, int c) {
+  if (a.uniform) return (int)(((long long)c * a.NB / gridDim.x) / a.nblk_u);
+  return __ldg(a.cta_seg + c);
+}
+
+__device__ __forceinline__ void raise_status(const DecodeArgs& a, volatile int* abort_flag,
+                                             int code) {
+  *abort_flag = 1;
+  atomicCAS(a.status, 0, code);
+}
+
+template <int D, int GS, int HS>
+__global__ void __launch_bounds__(kDecodeThreads, 1)
+    gqa_decode_kernel(const __grid_constant__ DecodeArgs a) {
+  using TS = TileShape<D>;
+  using SM = DecodeSmem<D, GS>;
+  constexpr int QR = TS::QR;
+  constexpr int STAGES = TS::STAGES;
+  constexpr int WPS = kConsumerWarps / HS;  // warps per head set
+  constexpr int R = QR / WPS;               // rows per warp per quarter per tile
+  constexpr int RC = R < 4 ? R : 4;         // rows per online-softmax update
+  constexpr int DV = D / 16;
+  constexpr float L2E = 1.4426950408889634f;
+  static_assert(kConsumerWarps % HS == 0, "head sets must divide the consumer warps");
+  static_assert(QR % WPS == 0 && R >= 1, "rows per quarter must divide among warps");
+  static_assert(D % 16 == 0, "head dim must be a multiple of 16");
+  static_assert(R % RC == 0, "row chunks must tile the rows");
+
+  extern __shared__ __align__(128) unsigned char smem[];
+  unsigned char* stages = smem;
+  float* merge_o = reinterpret_cast<float*>(smem + SM::kStageBytes);
+  float* merge_ml = reinterpret_cast<float*>(smem + SM::kStageBytes + SM::kMergeO);
+  uint64_t* full_bar =
+      reinterpret_cast<uint64_t*>(smem + SM::kStageBytes + SM::kMergeO + SM::kMergeML);
+  uint64_t* empty_bar = full_bar + STAGES;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty_bar + STAGES);
+  volatile int* ticket_sm = abort_flag + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      ptx::mbar_init(full_bar + i, 1);
+      ptx::mbar_init(empty_bar + i, kConsumerWarps);
+    }
+    *abort_flag = 0;
+    *ticket_sm = 0;
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+
+  const int grid = gridDim.x;
+  const long long cbeg = (long long)blockIdx.x * a.NB / grid;
+  const long long cend = (long long)(blockIdx.x + 1) * a.NB / grid;
+  const int s_first = first_seg_of_cta(a, blockIdx.x);
+
+  if (warp >= kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    ptx::setmaxnreg_dec<kProducerRegs>();
+    if (warp != kConsumerWarps) return;
+    const uint64_t pol = ptx::policy_evict_first();
+    const bool rows_contig = (a.block_table != nullptr) || (a.stride_t == D);
+    int it = 0;
+    long long pos = cbeg;
+    int s = s_first;
+    while (pos < cend) {
+      const SegView sv = seg_view(a, s);
+      const long long pend = sv.gend < cend ? sv.gend : cend;
+      if (pend > pos) {
+        const int lb = sv.blo + (int)(pos - sv.gbeg);
+        const int le = sv.blo + (int)(pend - sv.gbeg);
+        const int pt0 = max(sv.t0, lb * kBlk);
+        const int pt1 = min(sv.n, le * kBlk);
+        for (int blk = lb; blk < le; blk += TS::TB, ++it) {
+          const int stage = it % STAGES;
+          if (it >= STAGES && !*abort_flag) {
+            if (!ptx::mbar_wait_bounded(empty_bar + stage, ((it / STAGES) - 1) & 1,
+                                        a.timeout_ns)) {
+              if (lane == 0) raise_status(a, abort_flag, kDevErrProducerTimeout);
+            }
+          }
+          __syncwarp();
+          const int tok0 = blk * kBlk;
+          int qa[4], qn[4];
+          uint32_t bytes = 0;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int lo = max(tok0 + q * QR, pt0);
+            const int hi = min(tok0 + (q + 1) * QR, pt1);
+            qa[q] = lo;
+            qn[q] = hi > lo ? hi - lo : 0;
+            bytes += (uint32_t)qn[q] * D * 4u * 2u;
+          }
+          if (*abort_flag) {
+            // Consumers skip waits once aborted; complete the phase without data.
+            if (lane == 0) ptx::mbar_arrive(full_bar + stage);
+            continue;
+          }
+          if (lane == 0) ptx::mbar_arrive_expect_tx(full_bar + stage, bytes);
+          __syncwarp();
+          unsigned char* st_base = stages + (size_t)stage * TS::STAGE;
+          if (rows_contig) {
+            if (lane < 8) {
+              const int q = lane & 3;
+              const int kv = lane >> 2;
+              if (qn[q] > 0) {
+                const float* base = kv ? a.V : a.K;
+                const float* src;
+                if (a.block_table) {
+                  const int p =
+                      __ldg(a.block_table + (long long)sv.b * a.bt_stride + qa[q] / a.page_size);
+                  src = base + (long long)p * a.page_stride + (long long)sv.g * a.page_hstride +
+                        (long long)(qa[q] % a.page_size) * D;
+                } else {
+                  src = base + (long long)sv.b * a.kv_bstride + (long long)qa[q] * a.stride_t +
+                        (long long)sv.g * a.stride_h;
+                }
+                unsigned char* dst = st_base + kv * TS::KQ + q * TS::QSTRIDE +
+                                     (qa[q] - (tok0 + q * QR)) * D * 4;
+                ptx::bulk_g2s(dst, src, (uint32_t)qn[q] * D * 4u, full_bar + stage, pol);
+              }
+            }
+          } else {
+            for (int idx = lane; idx < 2 * 4 * QR; idx += 32) {
+              const int kv = idx / (4 * QR);
+              const int rem = idx - kv * 4 * QR;
+              const int q = rem / QR;
+              const int r = rem - q * QR;
+              const int t = tok0 + q * QR + r;
+              if (t >= qa[q] && t < qa[q] + qn[q]) {
+                const float* base = kv ? a.V : a.K;
+                const float* src = base + (long long)sv.b * a.kv_bstride +
+                                   (long long)t * a.stride_t + (long long)sv.g * a.stride_h;
+                unsigned char* dst = st_base + kv * TS::KQ + q * TS::QSTRIDE + r * D * 4;
+                ptx::bulk_g2s(dst, src, (uint32_t)D * 4u, full_bar + stage, pol);
+              }
+            }
+          }
+        }
+      }
+      pos = pend > pos ? pend : pos;
+      ++s;
+    }
+    // Drain: every issued stage must have landed before the CTA may exit.
+    if (lane == 0) {
+      const int first = it > STAGES ? it - STAGES : 0;
+      for (int j = first; j < it; ++j) {
+        if (!ptx::mbar_wait_bounded(full_bar + (j % STAGES), (j / STAGES) & 1, a.timeout_ns)) {
+          raise_status(a, abort_flag, kDevErrProducerTimeout);
+          break;
+        }
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  ptx::setmaxnreg_inc<kConsumerRegs>();
+  const int set = warp / WPS;  // head set of this warp
+  const int wi = warp - set * WPS;
+  const int grp = lane >> 3;   // row group == quarter read
+  const int l8 = lane & 7;
+  const int ctid = threadIdx.x;  // 0..255
+
+  float q[GS][2 * DV];
+  float o[GS][2 * DV];
+  float m[GS], l[GS];
+
+  int it = 0;
+  long long pos = cbeg;
+  int s = s_first;
+  while (pos < cend) {
+    const SegView sv = seg_view(a, s);
+    const long long pend = sv.gend < cend ? sv.gend : cend;
+    if (pend > pos) {
+      const int lb = sv.blo + (int)(pos - sv.gbeg);
+      const int le = sv.blo + (int)(pend - sv.gbeg);
+      const int pt0 = max(sv.t0, lb * kBlk);
+      const int pt1 = min(sv.n, le * kBlk);
+      const bool whole = (pos == sv.gbeg) && (pend == sv.gend);
+      const int head0 = sv.g * a.G + set * GS;  // first query head of this warp's set
+
+      {
+        const float* qb = a.Q + (long long)sv.b * a.q_bstride + (long long)head0 * D + l8;
+#pragma unroll
+        for (int h = 0; h < GS; ++h) {
+#pragma unroll
+          for (int mm = 0; mm < DV; ++mm) {
+            q[h][2 * mm] = __ldg(qb + h * D + 16 * mm);
+            q[h][2 * mm + 1] = __ldg(qb + h * D + 16 * mm + 8);
+            o[h][2 * mm] = 0.f;
+            o[h][2 * mm + 1] = 0.f;
+          }
+          m[h] = -CUDART_INF_F;
+          l[h] = 0.f;
+        }
+      }
+
+      for (int blk = lb; blk < le; blk += TS::TB, ++it) {
+        const int stage = it % STAGES;
+        if (!*abort_flag) {
+          if (!ptx::mbar_wait_bounded(full_bar + stage, (it / STAGES) & 1, a.timeout_ns)) {
+            if (lane == 0) raise_status(a, abort_flag, kDevErrConsumerTimeout);
+          }
+        }
+        __syncwarp();
+        if (!*abort_flag) {
+          const float* kq = reinterpret_cast<const float*>(stages + (size_t)stage * TS::STAGE +
+                                                           grp * TS::QSTRIDE) + l8;
+          const float* vq = reinterpret_cast<const float*>(
+                                stages + (size_t)stage * TS::STAGE + TS::KQ + grp * TS::QSTRIDE) +
+                            l8;
+          const int tok_base = blk * kBlk + grp * QR + wi * R;
+#pragma unroll
+          for (int r0 = 0; r0 < R; r0 += RC) {
+            float sc[RC][GS];
+            bool ok[RC];
+#pragma unroll
+            for (int r = 0; r < RC; ++r) {
+              const int tok = tok_base + r0 + r;
+              ok[r] = tok >= pt0 && tok < pt1;
+              const float* kr = kq + (wi * R + r0 + r) * D;
+              float a0[GS], a1[GS];
+#pragma unroll
+              for (int h = 0; h < GS; ++h) {
+                a0[h] = 0.f;
+                a1[h] = 0.f;
+              }
+#pragma unroll
+              for (int mm = 0; mm < DV; ++mm) {
+                const float k0 = kr[16 * mm];
+                const float k1 = kr[16 * mm + 8];
+#pragma unroll
+                for (int h = 0; h < GS; ++h) {
+                  a0[h] = __fmaf_rn(q[h][2 * mm], k0, a0[h]);
+                  a1[h] = __fmaf_rn(q[h][2 * mm + 1], k1, a1[h]);
+                }
+              }
+              // The reference's _mm512_reduce_add_ps tree: lanes l and l+8
+              // (held by this lane), then l^4, l^2, l^1 within the row group.
+#pragma unroll
+              for (int h = 0; h < GS; ++h) {
+                float t = __fadd_rn(a0[h], a1[h]);
+                t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 4));
+                t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
+                t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 1));
+                sc[r][h] = ok[r] ? __fmul_rn(t, a.scale) : -CUDART_INF_F;
+              }
+            }
+            // Online softmax update (state per row group).
+            bool grow = false;
+            float mnew[GS];
+#pragma unroll
+            for (int h = 0; h < GS; ++h) {
+              float mc = sc[0][h];
+#pragma unroll
+              for (int r = 1; r < RC; ++r) mc = fmaxf(mc, sc[r][h]);
+              mnew[h] = fmaxf(m[h], mc);
+              grow |= mnew[h] > m[h];
+            }
+            if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+              for (int h = 0; h < GS; ++h) {
+                const float alpha = mnew[h] > m[h] ? exp2f((m[h] - mnew[h]) * L2E) : 1.f;
+                l[h] *= alpha;
+#pragma unroll
+                for (int i = 0; i < 2 * DV; ++i) o[h][i] *= alpha;
+                m[h] = mnew[h];
+              }
+            }
+            float p[RC][GS];
+#pragma unroll
+            for (int r = 0; r < RC; ++r) {
+#pragma unroll
+              for (int h = 0; h < GS; ++h) {
+                p[r][h] = ok[r] ? exp2f((sc[r][h] - m[h]) * L2E) : 0.f;
+                l[h] += p[r][h];
+              }
+            }
+#pragma unroll
+            for (int r = 0; r < RC; ++r) {
+              const float* vr = vq + (wi * R + r0 + r) * D;
+#pragma unroll
+              for (int mm = 0; mm < DV; ++mm) {
+                const float v0 = ok[r] ? vr[16 * mm] : 0.f;
+                const float v1 = ok[r] ? vr[16 * mm + 8] : 0.f;
+#pragma unroll
+                for (int h = 0; h < GS; ++h) {
+                  o[h][2 * mm] = __fmaf_rn(p[r][h], v0, o[h][2 * mm]);
+                  o[h][2 * mm + 1] = __fmaf_rn(p[r][h], v1, o[h][2 * mm + 1]);
+                }
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(empty_bar + stage);
+      }
+
+      // ---- finalize the piece: merge 4 row groups, then warps, then CTAs.
+#pragma unroll
+      for (int off = 8; off <= 16; off <<= 1) {
+#pragma unroll
+        for (int h = 0; h < GS; ++h) {
+          const float mo = __shfl_xor_sync(0xffffffffu, m[h], off);
+          const float lo = __shfl_xor_sync(0xffffffffu, l[h], off);
+          const float M = fmaxf(m[h], mo);
+          const float fs = (m[h] == -CUDART_INF_F) ? 0.f : exp2f((m[h] - M) * L2E);
+          const float fo = (mo == -CUDART_INF_F) ? 0.f : exp2f((mo - M) * L2E);
+          l[h] = l[h] * fs + lo * fo;
+#pragma unroll
+          for (int i = 0; i < 2 * DV; ++i) {
+            const float ov = __shfl_xor_sync(0xffffffffu, o[h][i], off);
+            o[h][i] = o[h][i] * fs + ov * fo;
+          }
+          m[h] = M;
+        }
+      }
+      if (lane < 8) {
+#pragma unroll
+        for (int h = 0; h < GS; ++h) {
+          float* dst = merge_o + ((size_t)warp * GS + h) * D + l8;
+#pragma unroll
+          for (int mm = 0; mm < DV; ++mm) {
+            dst[16 * mm] = o[h][2 * mm];
+            dst[16 * mm + 8] = o[h][2 * mm + 1];
+          }
+          if (lane == 0) {
+            merge_ml[(warp * GS + h) * 2] = m[h];
+            merge_ml[(warp * GS + h) * 2 + 1] = l[h];
+          }
+        }
+      }
+      ptx::named_bar_sync(1, kConsumerWarps * 32);
+
+      const int G = a.G;
+      const int psz = G * D + 2 * G;
+      const int slot = 2 * blockIdx.x + (pos == cbeg ? 0 : 1);
+      float* part = a.partials + (size_t)slot * psz;
+      float* out_seg = a.O + (long long)sv.b * a.o_bstride + (long long)sv.g * G * D;
+      for (int idx = ctid; idx < G * D; idx += kConsumerWarps * 32) {
+        const int hl = idx / D;
+        const int j = idx - hl * D;
+        const int st = hl / GS;
+        const int hh = hl - st * GS;
+        float M = -CUDART_INF_F;
+#pragma unroll
+        for (int w = 0; w < WPS; ++w) M = fmaxf(M, merge_ml[((st * WPS + w) * GS + hh) * 2]);
+        float L = 0.f, acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < WPS; ++w) {
+          const int ww = st * WPS + w;
+          const float mw = merge_ml[(ww * GS + hh) * 2];
+          const float f = (mw == -CUDART_INF_F) ? 0.f : exp2f((mw - M) * L2E);
+          L += merge_ml[(ww * GS + hh) * 2 + 1] * f;
+          acc += merge_o[((size_t)ww * GS + hh) * D + j] * f;
+        }
+        if (whole) {
+          out_seg[idx] = acc / L;
+        } else {
+          part[idx] = acc;
+          if (j == 0) {
+            part[G * D + hl] = M;
+            part[G * D + G + hl] = L;
+          }
+        }
+      }
+      if (!whole) __threadfence();
+      ptx::named_bar_sync(1, kConsumerWarps * 32);
+
+      if (!whole) {
+        const long long cf = cta_of_block(sv.gbeg, a.NB, grid);
+        const long long cl = cta_of_block(sv.gend - 1, a.NB, grid);
+        if (ctid == 0) *ticket_sm = atomicAdd(a.counters + s, 1);
+        ptx::named_bar_sync(1, kConsumerWarps * 32);
+        if (*ticket_sm == (int)(cl - cf)) {
+          __threadfence();
+          for (int idx = ctid; idx < G * D; idx += kConsumerWarps * 32) {
+            const int hl = idx / D;
+            float M = -CUDART_INF_F;
+            for (long long c = cf; c <= cl; ++c) {
+              const int sl = 2 * (int)c + (first_seg_of_cta(a, (int)c) == s ? 0 : 1);
+              M = fmaxf(M, __ldcg(a.partials + (size_t)sl * psz + G * D + hl));
+            }
+            float L = 0.f, acc = 0.f;
+            for (long long c = cf; c <= cl; ++c) {
+              const int sl = 2 * (int)c + (first_seg_of_cta(a, (int)c) == s ? 0 : 1);
+              const float* pp = a.partials + (size_t)sl * psz;
+              const float mc = __ldcg(pp + G * D + hl);
+              const float f = (mc == -CUDART_INF_F) ? 0.f : exp2f((mc - M) * L2E);
+              L += __ldcg(pp + G * D + G + hl) * f;
+              acc += __ldcg(pp + idx) * f;
+            }
+            out_seg[idx] = acc / L;
+          }
+          if (ctid == 0) a.counters[s] = 0;
+        }
+        ptx::named_bar_sync(1, kConsumerWarps * 32);
+      }
+    }
+    pos = pend > pos ? pend : pos;
+    ++s;
+  }
+}
+
+}  // namespace molot

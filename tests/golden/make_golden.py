@@ -1,0 +1,138 @@
+"""Generates the golden fixtures in this directory from the reference itself.
+
+    python tests/golden/make_golden.py
+
+Runs the reference's own decode-attention headers (compiled unchanged into
+oracle/_ref/libmolot_ref.so by oracle/Makefile) on seeded N(0,1) inputs and
+stores inputs and outputs as .npz files.  tests/test_oracle.py pins the C
+restatement in oracle/attn_oracle.c against them; nothing at run time needs
+the reference tree.
+
+Cases follow the reference's own checks (bench/bench.cc:186-234: attention
+head at n=512, d=128 with inputs scaled by 0.2; vector exp on 16 fixed
+inputs) and the forward-path function attn_decode_gqa_cache at small sizes
+covering GQA grouping, the sliding window, head_dim 64/128/256, scale 1 and
+1/sqrt(d), plus the per-token prologue (QK RMSNorm, V norm, RoPE, append).
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+import oracle  # noqa: E402
+
+# (name, nq, nkv, n, d, scale, pos_cur, window, seed)
+ATTN_CASES = [
+    ("gqa4_n300_d128", 8, 2, 300, 128, 128 ** -0.5, 299, 0, 11),
+    ("mha_n45_d64_win16", 4, 4, 45, 64, 0.125, 44, 16, 12),
+    ("gqa2_n70_d256_scale1", 8, 4, 70, 256, 1.0, 69, 0, 13),
+    ("gqa4_n33_d128_tail", 32, 8, 33, 128, 128 ** -0.5, 32, 0, 14),
+    ("gqa8_n200_d128_win1", 8, 1, 200, 128, 128 ** -0.5, 199, 1, 15),
+    ("gqa4_n17_d128_winbig", 4, 1, 17, 128, 0.3, 16, 1024, 16),
+    ("empty_window", 4, 2, 10, 64, 0.125, 40, 8, 17),
+]
+
+
+def attn_cases():
+    out = {}
+    for name, nq, nkv, n, d, scale, pos, window, seed in ATTN_CASES:
+        rng = np.random.default_rng(seed)
+        Q = rng.standard_normal((nq, d)).astype(np.float32)
+        K = rng.standard_normal((n, nkv * d)).astype(np.float32)
+        V = rng.standard_normal((n, nkv * d)).astype(np.float32)
+        O = oracle.attn_decode_gqa_cache(Q, K, V, nq, nkv, n, d, scale, pos, window, impl="ref",
+                                         nthreads=4)
+        out[name] = dict(Q=Q, K=K, V=V, O=O,
+                         params=np.array([nq, nkv, n, d, pos, window], np.int64),
+                         scale=np.float32(scale))
+    return out
+
+
+def head_case():
+    """bench.cc:186-218 shape: one head, n=512, d=128, N(0,1)*0.2."""
+    rng = np.random.default_rng(1234)
+    n, d = 512, 128
+    Q = (rng.standard_normal(d) * 0.2).astype(np.float32)
+    K = (rng.standard_normal((n, d)) * 0.2).astype(np.float32)
+    V = (rng.standard_normal((n, d)) * 0.2).astype(np.float32)
+    lib = oracle.ref()
+    O = np.zeros(d, np.float32)
+    lib.ref_attn_decode_head(Q.ctypes.data, K.ctypes.data, V.ctypes.data, O.ctypes.data, n, d,
+                             np.float32(1.0 / np.sqrt(d)))
+    return dict(Q=Q, K=K, V=V, O=O)
+
+
+def exp_case():
+    """bench.cc:220-234 inputs."""
+    x = np.array([-87.0, -20.0, -10.0, -5.0, -3.0, -2.0, -1.5, -1.0, -0.75, -0.5, -0.25, -0.1,
+                  -0.01, 0.0, 1.0, 50.0], np.float32)
+    return dict(x=x, y=oracle.exp_taylor(x, impl="ref"))
+
+
+def norm_rope_case():
+    rng = np.random.default_rng(21)
+    out = {}
+    for d, base, pos in ((128, 1e4, 4096), (128, 5e5, 16384), (256, 1e6, 32768), (64, 1e4, 7)):
+        x = rng.standard_normal(d).astype(np.float32)
+        w = rng.standard_normal(d).astype(np.float32)
+        inv = oracle.rope_inv_freq(base, d, impl="ref")
+        out[f"d{d}_pos{pos}"] = dict(
+            x=x, w=w, inv_freq=inv, pos=np.int64(pos), base=np.float32(base),
+            rmsnorm=oracle.rmsnorm(x, w, 1e-6, impl="ref"),
+            rmsnorm_plain=oracle.rmsnorm_plain(x, 1e-6, impl="ref"),
+            rope=oracle.rope_apply(x, d, pos, inv, impl="ref"))
+    return out
+
+
+def layer_step_case():
+    """forward.h:554-590 for a gemma-style layer: QK-norm, V-norm, RoPE."""
+    rng = np.random.default_rng(31)
+    nq, nkv, hd, n0, cap = 8, 4, 256, 40, 48
+    kc = np.zeros((cap, nkv * hd), np.float32)
+    vc = np.zeros((cap, nkv * hd), np.float32)
+    kc[:n0] = rng.standard_normal((n0, nkv * hd))
+    vc[:n0] = rng.standard_normal((n0, nkv * hd))
+    q = rng.standard_normal(nq * hd).astype(np.float32)
+    k = rng.standard_normal(nkv * hd).astype(np.float32)
+    v = rng.standard_normal(nkv * hd).astype(np.float32)
+    qn = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kn = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    freq = oracle.rope_inv_freq(1e4, hd, impl="ref")
+    inputs = dict(q=q.copy(), k=k.copy(), v=v.copy(), kc=kc.copy(), vc=vc.copy(), q_norm=qn,
+                  k_norm=kn, freq=freq)
+    st, n1, out = oracle.attn_layer_step(q, k, v, qn, kn, 1, 1e-6, freq, n0, kc, vc, n0,
+                                         (nq, hd), nq, nkv, hd, 1.0, 16, impl="ref", nthreads=4)
+    assert st == 0 and n1 == n0 + 1
+    return dict(**inputs, params=np.array([nq, nkv, hd, n0, cap, 16], np.int64),
+                out=out, q_rot=q, k_row=kc[n0].copy(), v_row=vc[n0].copy())
+
+
+def main():
+    if oracle.ref() is None:
+        raise SystemExit("reference shim not available (needs the reference tree and AVX-512)")
+    flat = {}
+    for name, case in attn_cases().items():
+        for k, v in case.items():
+            flat[f"{name}/{k}"] = v
+    np.savez_compressed(os.path.join(HERE, "attn_gqa_cache.npz"), **flat)
+    np.savez_compressed(os.path.join(HERE, "attn_head_bench.npz"), **head_case())
+    np.savez_compressed(os.path.join(HERE, "exp16.npz"), **exp_case())
+    flat = {}
+    for name, case in norm_rope_case().items():
+        for k, v in case.items():
+            flat[f"{name}/{k}"] = v
+    np.savez_compressed(os.path.join(HERE, "norm_rope.npz"), **flat)
+    np.savez_compressed(os.path.join(HERE, "layer_step.npz"), **layer_step_case())
+    for f in sorted(os.listdir(HERE)):
+        if f.endswith(".npz"):
+            print(f, os.path.getsize(os.path.join(HERE, f)))
+
+
+if __name__ == "__main__":
+    main()
