@@ -239,9 +239,9 @@ def run_molot(args, cfg):
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
     for layer in range(L):
-        kt, vt = cache.layer_tensors(layer)
-        kt[:ctx].normal_(generator=gen)
-        vt[:ctx].normal_(generator=gen)
+        kt, vt = cache.layer_tensors(layer)  # head-major [nkv][cap][hd]
+        kt[:, :ctx].normal_(generator=gen)
+        vt[:, :ctx].normal_(generator=gen)
     q_raw = torch.randn((L, nq * d), device=dev, generator=gen)
     k_raw = torch.randn((L, nkv * d), device=dev, generator=gen)
     v_raw = torch.randn((L, nkv * d), device=dev, generator=gen)

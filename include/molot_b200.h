@@ -110,8 +110,11 @@ int molot_norm_rope_append_dev(const float* q, const float* k, const float* v, f
 
 /* ------------------------------------------------------------------------
  * KV cache handle: replaces Runner::KVC (forward.h:48-51) and its up-front
- * allocation (forward.h:103-110).  Per layer, K and V are [cap][nkv*hd]
- * FP32 in HBM (256-byte aligned), with a host-side slot count n.
+ * allocation (forward.h:103-110).  Per layer, K and V are FP32 in HBM,
+ * 256-byte aligned, laid out head-major [nkv][cap][hd] (each kv head's slots
+ * contiguous, so the decode kernel streams whole 16-slot blocks with single
+ * TMA copies), with a host-side slot count n.  Rows enter in the
+ * reference's [slot][nkv*hd] order through molot_kv_write / append.
  * ---------------------------------------------------------------------- */
 typedef struct molot_kv_cache molot_kv_cache;
 

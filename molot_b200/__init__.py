@@ -299,10 +299,11 @@ class KVCache:
         return k.value, v.value
 
     def layer_tensors(self, layer: int):
-        """(K, V) torch views [cap][nkv][hd] of the layer's device memory."""
+        """(K, V) torch views [nkv][cap][hd] (head-major) of the layer's
+        device memory."""
         import torch
         kp, vp = self.layer_ptrs(layer)
-        shape = (self.cap, self.nkv, self.hd)
+        shape = (self.nkv, self.cap, self.hd)
         return (torch.as_tensor(_CudaArray(kp, shape), device="cuda"),
                 torch.as_tensor(_CudaArray(vp, shape), device="cuda"))
 

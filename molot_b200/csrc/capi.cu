@@ -270,7 +270,7 @@ int decode_uniform(Workspace& ws, const float* Q, float* O, const float* K, cons
   const long long NB = (long long)nkv * nblk;
   const int grid = (int)std::min<long long>(NB, sm_count(dev));
   const int G = nq / nkv;
-  if ((rc = ws.ensure(dev, (size_t)2 * grid * (G * d + 2 * G), nkv, 0))) return rc;
+  if ((rc = ws.ensure(dev, (size_t)2 * grid * partial_record_floats(G, d), nkv, 0))) return rc;
   if ((rc = prepare_kernel(k, dev))) return rc;
   DecodeArgs a = {};
   a.Q = Q;
@@ -517,10 +517,14 @@ int molot_attn_decode_strided_dev(const float* Q, const float* K, const float* V
                         window, (cudaStream_t)stream);
 }
 
-int molot_norm_rope_append_dev(const float* q, const float* k, const float* v, float* q_out,
-                               const float* q_norm, const float* k_norm, int v_norm, float eps,
-                               const float* freq, int pos, float* kc, float* vc, int slot,
-                               int nq, int nkv, int d, void* stream) {
+namespace molot {
+namespace {
+// The per-token prologue into a strided single-sequence cache: slot `slot`
+// of kv head g lives at kc + slot*stride_t + g*stride_h.
+int append_strided(const float* q, const float* k, const float* v, float* q_out,
+                   const float* q_norm, const float* k_norm, int v_norm, float eps,
+                   const float* freq, int pos, float* kc, float* vc, int slot, int nq, int nkv,
+                   int d, long long stride_t, long long stride_h, cudaStream_t st) {
   if (!q || !k || !v || !q_out || !kc || !vc) return fail(MOLOT_ERR_INVALID, "null pointer");
   if (nq <= 0 || nkv <= 0 || slot < 0) return fail(MOLOT_ERR_INVALID, "bad sizes");
   AppendArgs a = {};
@@ -539,9 +543,19 @@ int molot_norm_rope_append_dev(const float* q, const float* k, const float* v, f
   a.slot = slot;
   a.K = kc;
   a.V = vc;
-  a.stride_t = (long long)nkv * d;
-  a.stride_h = d;
-  return append_launch(a, d, 1, (cudaStream_t)stream);
+  a.stride_t = stride_t;
+  a.stride_h = stride_h;
+  return append_launch(a, d, 1, st);
+}
+}  // namespace
+}  // namespace molot
+
+int molot_norm_rope_append_dev(const float* q, const float* k, const float* v, float* q_out,
+                               const float* q_norm, const float* k_norm, int v_norm, float eps,
+                               const float* freq, int pos, float* kc, float* vc, int slot,
+                               int nq, int nkv, int d, void* stream) {
+  return append_strided(q, k, v, q_out, q_norm, k_norm, v_norm, eps, freq, pos, kc, vc, slot, nq,
+                        nkv, d, (long long)nkv * d, d, (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------- KV cache handle
@@ -607,12 +621,20 @@ int molot_kv_write(molot_kv_cache* kv, int layer, int slot0, int nrows, const fl
   if (!kv || layer < 0 || layer >= kv->n_layers) return fail(MOLOT_ERR_INVALID, "bad layer");
   if (!k || !v || slot0 < 0 || nrows < 0 || slot0 + nrows > kv->cap)
     return fail(MOLOT_ERR_INVALID, "rows outside the cache");
+  if (nrows == 0) return MOLOT_OK;
   float *kc, *vc;
   molot_kv_layer_data(kv, layer, &kc, &vc);
-  const size_t row = (size_t)kv->nkv * kv->hd;
+  // [nrows][nkv*hd] rows in, [nkv][cap][hd] head-major cache out: one
+  // strided copy per kv head.
+  const size_t hd = kv->hd, src_pitch = (size_t)kv->nkv * hd * sizeof(float);
   cudaStream_t st = (cudaStream_t)stream;
-  MOLOT_CUDA(cudaMemcpyAsync(kc + slot0 * row, k, nrows * row * sizeof(float), cudaMemcpyDefault, st));
-  MOLOT_CUDA(cudaMemcpyAsync(vc + slot0 * row, v, nrows * row * sizeof(float), cudaMemcpyDefault, st));
+  for (int g = 0; g < kv->nkv; ++g) {
+    const size_t off = (size_t)g * kv->cap * hd + (size_t)slot0 * hd;
+    MOLOT_CUDA(cudaMemcpy2DAsync(kc + off, hd * sizeof(float), k + g * hd, src_pitch,
+                                 hd * sizeof(float), nrows, cudaMemcpyDefault, st));
+    MOLOT_CUDA(cudaMemcpy2DAsync(vc + off, hd * sizeof(float), v + g * hd, src_pitch,
+                                 hd * sizeof(float), nrows, cudaMemcpyDefault, st));
+  }
   return MOLOT_OK;
 }
 
@@ -624,8 +646,9 @@ int molot_attn_append_rope(molot_kv_cache* kv, int layer, const float* q, const 
   if (kv->len[layer] >= kv->cap) return fail(MOLOT_ERR_CACHE_FULL, "fwd: KV cache full");
   float *kc, *vc;
   molot_kv_layer_data(kv, layer, &kc, &vc);
-  int rc = molot_norm_rope_append_dev(q, k, v, q_out, q_norm, k_norm, v_norm, eps, freq, pos, kc,
-                                      vc, kv->len[layer], nq, kv->nkv, kv->hd, stream);
+  int rc = append_strided(q, k, v, q_out, q_norm, k_norm, v_norm, eps, freq, pos, kc, vc,
+                          kv->len[layer], nq, kv->nkv, kv->hd, kv->hd, (long long)kv->cap * kv->hd,
+                          (cudaStream_t)stream);
   if (rc) return rc;
   kv->len[layer]++;
   return MOLOT_OK;
@@ -639,8 +662,8 @@ int molot_attn_decode(molot_kv_cache* kv, int src_layer, const float* q, float* 
   if (n == 0) return fail(MOLOT_ERR_CACHE_EMPTY, "fwd: shared KV empty");
   float *kc, *vc;
   molot_kv_layer_data(kv, src_layer, &kc, &vc);
-  return decode_uniform(kv->ws, q, o, kc, vc, nq, kv->nkv, n, kv->hd, (long long)kv->nkv * kv->hd,
-                        kv->hd, scale, pos_cur, window, (cudaStream_t)stream);
+  return decode_uniform(kv->ws, q, o, kc, vc, nq, kv->nkv, n, kv->hd, kv->hd,
+                        (long long)kv->cap * kv->hd, scale, pos_cur, window, (cudaStream_t)stream);
 }
 
 int molot_kv_check(molot_kv_cache* kv, void* stream) {
@@ -740,7 +763,7 @@ int molot_paged_plan_build(molot_paged_plan* p, int B, int nq, int nkv, int d,
   p->o_cta = p->o_prefix + S + 1;
   const size_t total = p->o_cta + grid;
   const int G = nq / nkv;
-  if ((rc = p->ws.ensure(dev, (size_t)2 * grid * (G * d + 2 * G), S, total))) return rc;
+  if ((rc = p->ws.ensure(dev, (size_t)2 * grid * partial_record_floats(G, d), S, total))) return rc;
   if (p->h_cap < total) {
     if (p->h_plan) {
       MOLOT_CUDA(cudaEventSynchronize(p->uploaded));

@@ -107,11 +107,21 @@ template <int D, int GS>
 struct DecodeSmem {
   using TS = TileShape<D>;
   static constexpr int kStageBytes = TS::STAGES * TS::STAGE;
-  static constexpr int kMergeO = kConsumerWarps * GS * D * 4;
+  // per-warp outputs for the CTA merge; reused as [256][6] scratch by the
+  // cross-CTA combine
+  static constexpr int kMergeO =
+      4 * (kConsumerWarps * GS * D > 6 * kConsumerWarps * 32 ? kConsumerWarps * GS * D
+                                                             : 6 * kConsumerWarps * 32);
   static constexpr int kMergeML = kConsumerWarps * GS * 2 * 4;
   static constexpr int kBars = 2 * TS::STAGES * 8;
   static constexpr int kTotal = kStageBytes + kMergeO + kMergeML + kBars + 16;
 };
+
+// Floats of one partial record: o[G][D], then m[G], l[G]; padded to a
+// multiple of 4 so each record starts 16-byte aligned (float4 reads).
+__host__ __device__ constexpr int partial_record_floats(int G, int D) {
+  return (G * D + 2 * G + 3) & ~3;
+}
 
 __device__ __forceinline__ long long cta_of_block(long long x, long long NB, int grid) {
   // Largest c with floor(c*NB/grid) <= x.
@@ -480,7 +490,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       ptx::named_bar_sync(1, kConsumerWarps * 32);
 
       const int G = a.G;
-      const int psz = G * D + 2 * G;
+      const int psz = partial_record_floats(G, D);
       const int slot = 2 * blockIdx.x + (pos == cbeg ? 0 : 1);
       float* part = a.partials + (size_t)slot * psz;
       float* out_seg = a.O + (long long)sv.b * a.o_bstride + (long long)sv.g * G * D;
@@ -520,24 +530,92 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         if (ctid == 0) *ticket_sm = atomicAdd(a.counters + s, 1);
         ptx::named_bar_sync(1, kConsumerWarps * 32);
         if (*ticket_sm == (int)(cl - cf)) {
+          // Last CTA of the segment: merge the nc partials.  Every CTA after
+          // the first starts inside this segment (slot 0); the first keeps it
+          // in slot 0 only if its own range starts here too.
           __threadfence();
-          for (int idx = ctid; idx < G * D; idx += kConsumerWarps * 32) {
-            const int hl = idx / D;
+          const int nc = (int)(cl - cf + 1);
+          const int slot_first =
+              2 * (int)cf + (((long long)cf * a.NB / grid) >= sv.gbeg ? 0 : 1);
+          const int nchunk = G * D / 4;  // float4 chunks of o[G][D]
+          const int csplit = max(1, (kConsumerWarps * 32) / nchunk);
+          float* red = merge_o;  // [task][6] scratch, merge buffer is free now
+          for (int task = ctid; task < nchunk * csplit; task += kConsumerWarps * 32) {
+            const int chunk = task % nchunk;
+            const int part_i = task / nchunk;
+            const int hl = (chunk * 4) / D;
+            float M = -CUDART_INF_F, L = 0.f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int k0 = part_i; k0 < nc; k0 += 4 * csplit) {
+              float mc[4], lc[4];
+              float4 oc[4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int k = k0 + u * csplit;
+                if (k < nc) {
+                  const int sl = k == 0 ? slot_first : 2 * ((int)cf + k);
+                  const float* pp = a.partials + (size_t)sl * psz;
+                  mc[u] = __ldcg(pp + G * D + hl);
+                  lc[u] = __ldcg(pp + G * D + G + hl);
+                  oc[u] = __ldcg(reinterpret_cast<const float4*>(pp) + chunk);
+                } else {
+                  mc[u] = -CUDART_INF_F;
+                  lc[u] = 0.f;
+                  oc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+              }
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const float Mn = fmaxf(M, mc[u]);
+                const float fa = (M == -CUDART_INF_F) ? 0.f : exp2f((M - Mn) * L2E);
+                const float fb = (mc[u] == -CUDART_INF_F) ? 0.f : exp2f((mc[u] - Mn) * L2E);
+                L = L * fa + lc[u] * fb;
+                acc.x = acc.x * fa + oc[u].x * fb;
+                acc.y = acc.y * fa + oc[u].y * fb;
+                acc.z = acc.z * fa + oc[u].z * fb;
+                acc.w = acc.w * fa + oc[u].w * fb;
+                M = Mn;
+              }
+            }
+            if (csplit == 1) {
+              // This thread saw every partial of the chunk.
+              float* dst = out_seg + chunk * 4;
+              dst[0] = acc.x / L;
+              dst[1] = acc.y / L;
+              dst[2] = acc.z / L;
+              dst[3] = acc.w / L;
+            } else {
+              // csplit > 1 means nchunk * csplit <= 256: the task index fits
+              // the [256][6] scratch.
+              float* r = red + (size_t)task * 6;
+              r[0] = M;
+              r[1] = L;
+              r[2] = acc.x;
+              r[3] = acc.y;
+              r[4] = acc.z;
+              r[5] = acc.w;
+            }
+          }
+          ptx::named_bar_sync(1, kConsumerWarps * 32);
+          for (int chunk = ctid; csplit > 1 && chunk < nchunk; chunk += kConsumerWarps * 32) {
             float M = -CUDART_INF_F;
-            for (long long c = cf; c <= cl; ++c) {
-              const int sl = 2 * (int)c + (first_seg_of_cta(a, (int)c) == s ? 0 : 1);
-              M = fmaxf(M, __ldcg(a.partials + (size_t)sl * psz + G * D + hl));
+            for (int p = 0; p < csplit; ++p) M = fmaxf(M, red[(size_t)(p * nchunk + chunk) * 6]);
+            float L = 0.f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int p = 0; p < csplit; ++p) {
+              const float* r = red + (size_t)(p * nchunk + chunk) * 6;
+              const float f = (r[0] == -CUDART_INF_F) ? 0.f : exp2f((r[0] - M) * L2E);
+              L += r[1] * f;
+              acc.x += r[2] * f;
+              acc.y += r[3] * f;
+              acc.z += r[4] * f;
+              acc.w += r[5] * f;
             }
-            float L = 0.f, acc = 0.f;
-            for (long long c = cf; c <= cl; ++c) {
-              const int sl = 2 * (int)c + (first_seg_of_cta(a, (int)c) == s ? 0 : 1);
-              const float* pp = a.partials + (size_t)sl * psz;
-              const float mc = __ldcg(pp + G * D + hl);
-              const float f = (mc == -CUDART_INF_F) ? 0.f : exp2f((mc - M) * L2E);
-              L += __ldcg(pp + G * D + G + hl) * f;
-              acc += __ldcg(pp + idx) * f;
-            }
-            out_seg[idx] = acc / L;
+            float* dst = out_seg + chunk * 4;
+            dst[0] = acc.x / L;
+            dst[1] = acc.y / L;
+            dst[2] = acc.z / L;
+            dst[3] = acc.w / L;
           }
           if (ctid == 0) a.counters[s] = 0;
         }
