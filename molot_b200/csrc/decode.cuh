@@ -164,6 +164,110 @@ __device__ __forceinline__ void raise_status(const DecodeArgs& a, volatile int* 
   atomicCAS(a.status, 0, code);
 }
 
+constexpr float kLog2e = 1.4426950408889634f;
+// Lazy rescaling: the running maximum (log2 units) is only raised when a
+// score exceeds it by more than this, so weights stay <= 2^8 while the
+// accumulators are rescaled rarely.  Every merge uses the stored maxima,
+// so the result does not depend on when rescales happened.
+constexpr float kLazyLog2 = 8.0f;
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// One chunk of RC rows of a row group: QK scores in the reference's
+// accumulation order, lazy online-softmax update, p * V accumulation.
+// kr / vr point at this lane's first element of the chunk's first K / V row
+// in shared memory; rows are D floats apart.  FULL: every row is valid.
+template <int D, int GS, int RC, bool FULL>
+__device__ __forceinline__ void process_rows(const float* kr, const float* vr, int tok, int pt0,
+                                             int pt1, float scale, float (&q)[GS][D / 8],
+                                             float (&o)[GS][D / 8], float (&m2)[GS],
+                                             float (&l)[GS]) {
+  constexpr int DV = D / 16;
+  float sc[RC][GS];
+  bool ok[RC];
+#pragma unroll
+  for (int r = 0; r < RC; ++r) {
+    ok[r] = FULL || (tok + r >= pt0 && tok + r < pt1);
+    const float* k = kr + r * D;
+    float a0[GS], a1[GS];
+#pragma unroll
+    for (int h = 0; h < GS; ++h) {
+      a0[h] = 0.f;
+      a1[h] = 0.f;
+    }
+#pragma unroll
+    for (int mm = 0; mm < DV; ++mm) {
+      const float k0 = k[16 * mm];
+      const float k1 = k[16 * mm + 8];
+#pragma unroll
+      for (int h = 0; h < GS; ++h) {
+        a0[h] = __fmaf_rn(q[h][2 * mm], k0, a0[h]);
+        a1[h] = __fmaf_rn(q[h][2 * mm + 1], k1, a1[h]);
+      }
+    }
+    // The reference's _mm512_reduce_add_ps tree: lanes l and l+8 (held by
+    // this lane), then l^4, l^2, l^1 within the row group.
+#pragma unroll
+    for (int h = 0; h < GS; ++h) {
+      float t = __fadd_rn(a0[h], a1[h]);
+      t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 4));
+      t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
+      t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 1));
+      const float s = __fmul_rn(t, scale);  // == dot_fp32_avx512(q, k) * scale
+      sc[r][h] = ok[r] ? s : -CUDART_INF_F;
+    }
+  }
+  bool need_any = false;
+  float mc2[GS];
+#pragma unroll
+  for (int h = 0; h < GS; ++h) {
+    float mc = sc[0][h];
+#pragma unroll
+    for (int r = 1; r < RC; ++r) mc = fmaxf(mc, sc[r][h]);
+    mc2[h] = mc * kLog2e;
+    need_any |= mc2[h] > m2[h] + kLazyLog2;
+  }
+  if (__any_sync(0xffffffffu, need_any)) {
+#pragma unroll
+    for (int h = 0; h < GS; ++h) {
+      const bool need = mc2[h] > m2[h] + kLazyLog2;
+      const float alpha = need ? ex2(m2[h] - mc2[h]) : 1.f;
+      l[h] *= alpha;
+#pragma unroll
+      for (int i = 0; i < 2 * DV; ++i) o[h][i] *= alpha;
+      m2[h] = need ? mc2[h] : m2[h];
+    }
+  }
+  float p[RC][GS];
+#pragma unroll
+  for (int r = 0; r < RC; ++r) {
+#pragma unroll
+    for (int h = 0; h < GS; ++h) {
+      const float e = ex2(__fmaf_rn(sc[r][h], kLog2e, -m2[h]));
+      p[r][h] = FULL ? e : (ok[r] ? e : 0.f);
+      l[h] += p[r][h];
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < RC; ++r) {
+    const float* v = vr + r * D;
+#pragma unroll
+    for (int mm = 0; mm < DV; ++mm) {
+      const float v0 = FULL ? v[16 * mm] : (ok[r] ? v[16 * mm] : 0.f);
+      const float v1 = FULL ? v[16 * mm + 8] : (ok[r] ? v[16 * mm + 8] : 0.f);
+#pragma unroll
+      for (int h = 0; h < GS; ++h) {
+        o[h][2 * mm] = __fmaf_rn(p[r][h], v0, o[h][2 * mm]);
+        o[h][2 * mm + 1] = __fmaf_rn(p[r][h], v1, o[h][2 * mm + 1]);
+      }
+    }
+  }
+}
+
 template <int D, int GS, int HS>
 __global__ void __launch_bounds__(kDecodeThreads, 1)
     gqa_decode_kernel(const __grid_constant__ DecodeArgs a) {
@@ -175,7 +279,6 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   constexpr int R = QR / WPS;               // rows per warp per quarter per tile
   constexpr int RC = R < 4 ? R : 4;         // rows per online-softmax update
   constexpr int DV = D / 16;
-  constexpr float L2E = 1.4426950408889634f;
   static_assert(kConsumerWarps % HS == 0, "head sets must divide the consumer warps");
   static_assert(QR % WPS == 0 && R >= 1, "rows per quarter must divide among warps");
   static_assert(D % 16 == 0, "head dim must be a multiple of 16");
@@ -367,86 +470,19 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
                                 stages + (size_t)stage * TS::STAGE + TS::KQ + grp * TS::QSTRIDE) +
                             l8;
           const int tok_base = blk * kBlk + grp * QR + wi * R;
+          // Only a piece's first and last tiles can hold rows outside
+          // [pt0, pt1); the rest take the predicate-free path.
+          const bool full = blk * kBlk >= pt0 && blk * kBlk + TS::T <= pt1;
+          if (full) {
 #pragma unroll
-          for (int r0 = 0; r0 < R; r0 += RC) {
-            float sc[RC][GS];
-            bool ok[RC];
+            for (int r0 = 0; r0 < R; r0 += RC)
+              process_rows<D, GS, RC, true>(kq + (wi * R + r0) * D, vq + (wi * R + r0) * D,
+                                            tok_base + r0, pt0, pt1, a.scale, q, o, m, l);
+          } else {
 #pragma unroll
-            for (int r = 0; r < RC; ++r) {
-              const int tok = tok_base + r0 + r;
-              ok[r] = tok >= pt0 && tok < pt1;
-              const float* kr = kq + (wi * R + r0 + r) * D;
-              float a0[GS], a1[GS];
-#pragma unroll
-              for (int h = 0; h < GS; ++h) {
-                a0[h] = 0.f;
-                a1[h] = 0.f;
-              }
-#pragma unroll
-              for (int mm = 0; mm < DV; ++mm) {
-                const float k0 = kr[16 * mm];
-                const float k1 = kr[16 * mm + 8];
-#pragma unroll
-                for (int h = 0; h < GS; ++h) {
-                  a0[h] = __fmaf_rn(q[h][2 * mm], k0, a0[h]);
-                  a1[h] = __fmaf_rn(q[h][2 * mm + 1], k1, a1[h]);
-                }
-              }
-              // The reference's _mm512_reduce_add_ps tree: lanes l and l+8
-              // (held by this lane), then l^4, l^2, l^1 within the row group.
-#pragma unroll
-              for (int h = 0; h < GS; ++h) {
-                float t = __fadd_rn(a0[h], a1[h]);
-                t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 4));
-                t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
-                t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 1));
-                sc[r][h] = ok[r] ? __fmul_rn(t, a.scale) : -CUDART_INF_F;
-              }
-            }
-            // Online softmax update (state per row group).
-            bool grow = false;
-            float mnew[GS];
-#pragma unroll
-            for (int h = 0; h < GS; ++h) {
-              float mc = sc[0][h];
-#pragma unroll
-              for (int r = 1; r < RC; ++r) mc = fmaxf(mc, sc[r][h]);
-              mnew[h] = fmaxf(m[h], mc);
-              grow |= mnew[h] > m[h];
-            }
-            if (__any_sync(0xffffffffu, grow)) {
-#pragma unroll
-              for (int h = 0; h < GS; ++h) {
-                const float alpha = mnew[h] > m[h] ? exp2f((m[h] - mnew[h]) * L2E) : 1.f;
-                l[h] *= alpha;
-#pragma unroll
-                for (int i = 0; i < 2 * DV; ++i) o[h][i] *= alpha;
-                m[h] = mnew[h];
-              }
-            }
-            float p[RC][GS];
-#pragma unroll
-            for (int r = 0; r < RC; ++r) {
-#pragma unroll
-              for (int h = 0; h < GS; ++h) {
-                p[r][h] = ok[r] ? exp2f((sc[r][h] - m[h]) * L2E) : 0.f;
-                l[h] += p[r][h];
-              }
-            }
-#pragma unroll
-            for (int r = 0; r < RC; ++r) {
-              const float* vr = vq + (wi * R + r0 + r) * D;
-#pragma unroll
-              for (int mm = 0; mm < DV; ++mm) {
-                const float v0 = ok[r] ? vr[16 * mm] : 0.f;
-                const float v1 = ok[r] ? vr[16 * mm + 8] : 0.f;
-#pragma unroll
-                for (int h = 0; h < GS; ++h) {
-                  o[h][2 * mm] = __fmaf_rn(p[r][h], v0, o[h][2 * mm]);
-                  o[h][2 * mm + 1] = __fmaf_rn(p[r][h], v1, o[h][2 * mm + 1]);
-                }
-              }
-            }
+            for (int r0 = 0; r0 < R; r0 += RC)
+              process_rows<D, GS, RC, false>(kq + (wi * R + r0) * D, vq + (wi * R + r0) * D,
+                                             tok_base + r0, pt0, pt1, a.scale, q, o, m, l);
           }
         }
         __syncwarp();
@@ -461,8 +497,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
           const float mo = __shfl_xor_sync(0xffffffffu, m[h], off);
           const float lo = __shfl_xor_sync(0xffffffffu, l[h], off);
           const float M = fmaxf(m[h], mo);
-          const float fs = (m[h] == -CUDART_INF_F) ? 0.f : exp2f((m[h] - M) * L2E);
-          const float fo = (mo == -CUDART_INF_F) ? 0.f : exp2f((mo - M) * L2E);
+          const float fs = (m[h] == -CUDART_INF_F) ? 0.f : ex2(m[h] - M);
+          const float fo = (mo == -CUDART_INF_F) ? 0.f : ex2(mo - M);
           l[h] = l[h] * fs + lo * fo;
 #pragma unroll
           for (int i = 0; i < 2 * DV; ++i) {
@@ -507,7 +543,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         for (int w = 0; w < WPS; ++w) {
           const int ww = st * WPS + w;
           const float mw = merge_ml[(ww * GS + hh) * 2];
-          const float f = (mw == -CUDART_INF_F) ? 0.f : exp2f((mw - M) * L2E);
+          const float f = (mw == -CUDART_INF_F) ? 0.f : ex2(mw - M);
           L += merge_ml[(ww * GS + hh) * 2 + 1] * f;
           acc += merge_o[((size_t)ww * GS + hh) * D + j] * f;
         }
@@ -546,11 +582,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
             const int hl = (chunk * 4) / D;
             float M = -CUDART_INF_F, L = 0.f;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int k0 = part_i; k0 < nc; k0 += 4 * csplit) {
-              float mc[4], lc[4];
-              float4 oc[4];
+            for (int k0 = part_i; k0 < nc; k0 += 8 * csplit) {
+              float mc[8], lc[8];
+              float4 oc[8];
 #pragma unroll
-              for (int u = 0; u < 4; ++u) {
+              for (int u = 0; u < 8; ++u) {
                 const int k = k0 + u * csplit;
                 if (k < nc) {
                   const int sl = k == 0 ? slot_first : 2 * ((int)cf + k);
@@ -565,10 +601,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
                 }
               }
 #pragma unroll
-              for (int u = 0; u < 4; ++u) {
+              for (int u = 0; u < 8; ++u) {
                 const float Mn = fmaxf(M, mc[u]);
-                const float fa = (M == -CUDART_INF_F) ? 0.f : exp2f((M - Mn) * L2E);
-                const float fb = (mc[u] == -CUDART_INF_F) ? 0.f : exp2f((mc[u] - Mn) * L2E);
+                const float fa = (M == -CUDART_INF_F) ? 0.f : ex2(M - Mn);
+                const float fb = (mc[u] == -CUDART_INF_F) ? 0.f : ex2(mc[u] - Mn);
                 L = L * fa + lc[u] * fb;
                 acc.x = acc.x * fa + oc[u].x * fb;
                 acc.y = acc.y * fa + oc[u].y * fb;
@@ -604,7 +640,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int p = 0; p < csplit; ++p) {
               const float* r = red + (size_t)(p * nchunk + chunk) * 6;
-              const float f = (r[0] == -CUDART_INF_F) ? 0.f : exp2f((r[0] - M) * L2E);
+              const float f = (r[0] == -CUDART_INF_F) ? 0.f : ex2(r[0] - M);
               L += r[1] * f;
               acc.x += r[2] * f;
               acc.y += r[3] * f;
