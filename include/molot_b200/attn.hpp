@@ -1,0 +1,112 @@
+// C++ drop-in for the reference's decode-attention header
+// (include/molot/attn.h) and its KV cache (Runner::KVC, forward.h:48-51),
+// backed by the molot_b200 C ABI (include/molot_b200.h).
+//
+// Same function names and argument meaning as the reference, in namespace
+// molot_b200.  The reference's trailing ThreadPool& becomes the CUDA device
+// current on the calling thread; results are ready on return, as in the
+// reference.  Errors throw std::runtime_error, matching the places where the
+// reference's forward pass throws (forward.h:570, 580); bad arguments, which
+// the reference does not check, throw too instead of reading out of bounds.
+#pragma once
+
+#include <stdexcept>
+#include <string>
+
+#include "molot_b200.h"
+
+namespace molot_b200 {
+
+inline void check(int status) {
+  if (status != MOLOT_OK)
+    throw std::runtime_error(std::string("molot_b200: ") + molot_status_string(status) + ": " +
+                             molot_last_error());
+}
+
+// attn.h:19-28
+inline void rope_apply(float* x, int d, int pos, const float* inv_freq) {
+  check(molot_rope_apply(x, d, pos, inv_freq));
+}
+
+// attn.h:31-33
+inline void rope_inv_freq(float base, int d, float* out) {
+  check(molot_rope_inv_freq(base, d, out));
+}
+
+// attn.h:57-101
+inline void attn_decode_head_win(const float* Q, const float* K, const float* V, float* out,
+                                 int n, int d, float scale, int pos_cur, int window) {
+  check(molot_attn_decode_head_win(Q, K, V, out, n, d, scale, pos_cur, window));
+}
+
+// attn.h:104-107
+inline void attn_decode_head(const float* Q, const float* K, const float* V, float* out, int n,
+                             int d, float scale) {
+  check(molot_attn_decode_head(Q, K, V, out, n, d, scale));
+}
+
+// attn.h:111-120
+inline void attn_decode_gqa(const float* Q, const float* K, const float* V, float* O, int nq,
+                            int nkv, int n, int d, float scale) {
+  check(molot_attn_decode_gqa(Q, K, V, O, nq, nkv, n, d, scale));
+}
+
+// attn.h:125-177
+inline void attn_decode_gqa_cache(const float* Q, const float* K, const float* V, float* O,
+                                  int nq, int nkv, int n, int qhd, float scale, int pos_cur,
+                                  int window) {
+  check(molot_attn_decode_gqa_cache(Q, K, V, O, nq, nkv, n, qhd, scale, pos_cur, window));
+}
+
+// attn.h:178-187
+inline void attn_decode_gqa_win(const float* Q, const float* K, const float* V, float* O, int nq,
+                                int nkv, int n, int d, float scale, int pos_cur, int window) {
+  check(molot_attn_decode_gqa_win(Q, K, V, O, nq, nkv, n, d, scale, pos_cur, window));
+}
+
+// HBM-resident replacement for Runner::KVC: one handle for all layers.
+// Device pointers in, device pointers out; stream-ordered (stream = a
+// cudaStream_t, nullptr = legacy default stream).
+class KVCache {
+ public:
+  KVCache(int n_layers, int nkv, int hd, int cap) : nkv_(nkv), hd_(hd), cap_(cap) {
+    check(molot_kv_create(n_layers, nkv, hd, cap, &h_));
+  }
+  ~KVCache() { molot_kv_destroy(h_); }
+  KVCache(const KVCache&) = delete;
+  KVCache& operator=(const KVCache&) = delete;
+
+  int n(int layer) const {
+    int r = molot_kv_length(h_, layer);
+    if (r < 0) check(r);
+    return r;
+  }
+  int cap() const { return cap_; }
+  void set_n(int layer, int n) { check(molot_kv_set_length(h_, layer, n)); }
+  // Prefill-style bulk write of rows [slot0, slot0+nrows) ([nrows][nkv*hd]).
+  void write(int layer, int slot0, int nrows, const float* k, const float* v,
+             void* stream = nullptr) {
+    check(molot_kv_write(h_, layer, slot0, nrows, k, v, stream));
+  }
+  // forward.h:554-575: norms + RoPE on the new token, append at slot n.
+  void append_rope(int layer, const float* q, const float* k, const float* v, float* q_out,
+                   const float* q_norm, const float* k_norm, bool v_norm, float eps,
+                   const float* freq, int pos, int nq, void* stream = nullptr) {
+    check(molot_attn_append_rope(h_, layer, q, k, v, q_out, q_norm, k_norm, v_norm ? 1 : 0, eps,
+                                 freq, pos, nq, stream));
+  }
+  // forward.h:578-590: attention over the cache of src_layer.
+  void decode(int src_layer, const float* q, float* o, int nq, float scale, int pos_cur,
+              int window, void* stream = nullptr) {
+    check(molot_attn_decode(h_, src_layer, q, o, nq, scale, pos_cur, window, stream));
+  }
+  // Synchronise and surface device-side wait timeouts.
+  void sync(void* stream = nullptr) { check(molot_kv_check(h_, stream)); }
+  molot_kv_cache* handle() { return h_; }
+
+ private:
+  molot_kv_cache* h_ = nullptr;
+  int nkv_, hd_, cap_;
+};
+
+}  // namespace molot_b200
