@@ -98,6 +98,21 @@ int molot_attn_decode_strided_dev(const float* Q, const float* K, const float* V
                                   long long stride_h, float scale, int pos_cur, int window,
                                   void* stream);
 
+/* No counterpart in the reference: molot_attn_decode_strided_dev for callers
+ * that cannot allocate device memory (their host runtime owns every device
+ * allocation, or a cudaMalloc on first use would synchronise the device).
+ * Same arguments and results, but the split-KV scratch is a fixed ~1.4 MB
+ * array inside the library (held by every GPU that loads it) instead of a
+ * workspace allocated on first use.  Limits: head_dim 64/128/256, group
+ * nq/nkv 1/2/4/8 with group*head_dim <= 1024, nkv <= 256; larger requests
+ * return MOLOT_ERR_UNSUPPORTED.  The first call on a device sets up the
+ * scratch address (make it before any stream capture).  All calls share the
+ * scratch: calls that overlap on the GPU race, so order them on one stream. */
+int molot_attn_decode_strided_noalloc(const float* Q, const float* K, const float* V, float* O,
+                                      int nq, int nkv, int n, int d, long long stride_t,
+                                      long long stride_h, float scale, int pos_cur, int window,
+                                      void* stream);
+
 /* forward.h:554-575 on device buffers for a [cap][nkv*d] cache: q (nq heads)
  * and k (nkv heads) get per-head weighted RMSNorm when q_norm / k_norm are
  * non-null, then NEOX RoPE at `pos` when freq ([d/2]) is non-null; v gets a

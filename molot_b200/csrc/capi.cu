@@ -382,6 +382,11 @@ int host_decode(const float* Q, const float* K, const float* V, float* O, int nq
 }
 
 }  // namespace
+
+// Lets other translation units of the library report through
+// molot_last_error().
+int set_last_error(int code, const char* msg) { return fail(code, msg); }
+
 }  // namespace molot
 
 using namespace molot;

@@ -1,0 +1,205 @@
+// molot_attn_decode_strided_noalloc: the strided single-sequence decode for
+// callers that cannot allocate device memory.
+//
+// Some embedders run inside a host runtime that owns every device
+// allocation (a custom caching allocator, a memory pool sized at start-up,
+// or a region where cudaMalloc would synchronise the device and stall other
+// streams), so a library call that allocates its own scratch on first use
+// is not acceptable to them.  This entry point allocates nothing: the split-KV
+// partial records, the per-head tickets and the status word live in one
+// file-scope __device__ array of fixed size (kNoAllocScratchBytes, about
+// 1.4 MB).  Every GPU on which the library's code is loaded holds that
+// array until the process exits.
+//
+// Limits: head_dim in {64, 128, 256}, group size nq/nkv in {1, 2, 4, 8} with
+// group * head_dim <= 1024, nkv <= 256, and at most kNoAllocMaxGrid CTAs.
+// Larger requests are rejected with MOLOT_ERR_UNSUPPORTED.
+//
+// All calls share the one array, and it keeps what the last call left in it:
+// each call clears the tickets and the status word (cudaMemsetAsync on the
+// array, which allocates nothing) before its launch.  Calls whose work
+// overlaps on the GPU -- different streams, or different host threads
+// without ordering -- race on the array; order them on one stream.
+//
+// Set-up: on the first call on a device, with that device current, the
+// array's device address is fetched once with cudaGetSymbolAddress (the
+// array's name is only a host-side stand-in in host code) and cached; make
+// that first call before any stream capture.
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+
+#include "decode.cuh"
+#include "molot_b200.h"
+
+namespace molot {
+
+int set_last_error(int code, const char* msg);
+
+namespace {
+
+constexpr int kNoAllocMaxGrid = 160;                      // >= 148 SMs of a B200
+constexpr int kNoAllocMaxGroupDim = 1024;                 // G * head_dim
+constexpr int kNoAllocMaxRecord = kNoAllocMaxGroupDim + 64;  // floats, >= partial_record_floats
+constexpr int kNoAllocMaxSegments = 256;                  // nkv
+constexpr size_t kNoAllocPartialBytes = 2ull * kNoAllocMaxGrid * kNoAllocMaxRecord * 4;
+constexpr size_t kNoAllocCounterBytes = kNoAllocMaxSegments * 4;
+constexpr size_t kNoAllocStatusBytes = 256;
+constexpr size_t kNoAllocScratchBytes =
+    kNoAllocPartialBytes + kNoAllocCounterBytes + kNoAllocStatusBytes;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device (set-up once).
+int scratch_for(int dev, unsigned char** out) {
+  if (dev < 0 || dev >= kMaxDevices)
+    return set_last_error(MOLOT_ERR_UNSUPPORTED, "device index beyond the no-alloc table");
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return set_last_error(MOLOT_ERR_CUDA, (std::string("cudaGetSymbolAddress(no-alloc scratch): ") +
+                                             cudaGetErrorString(e)).c_str());
+    g_scratch_addr[dev] = p;
+  }
+  *out = static_cast<unsigned char*>(g_scratch_addr[dev]);
+  return MOLOT_OK;
+}
+
+struct Kernel {
+  const void* fn;
+  int smem;
+};
+
+template <int D, int GS, int HS>
+Kernel kernel_of() {
+  return {reinterpret_cast<const void*>(&gqa_decode_kernel<D, GS, HS>), DecodeSmem<D, GS>::kTotal};
+}
+
+bool pick(int d, int g, Kernel* k) {
+  switch (d) {
+    case 64:
+      switch (g) {
+        case 1: *k = kernel_of<64, 1, 1>(); return true;
+        case 2: *k = kernel_of<64, 2, 1>(); return true;
+        case 4: *k = kernel_of<64, 4, 1>(); return true;
+        case 8: *k = kernel_of<64, 8, 1>(); return true;
+      }
+      return false;
+    case 128:
+      switch (g) {
+        case 1: *k = kernel_of<128, 1, 1>(); return true;
+        case 2: *k = kernel_of<128, 2, 1>(); return true;
+        case 4: *k = kernel_of<128, 4, 1>(); return true;
+        case 8: *k = kernel_of<128, 4, 2>(); return true;
+      }
+      return false;
+    case 256:
+      switch (g) {
+        case 1: *k = kernel_of<256, 1, 1>(); return true;
+        case 2: *k = kernel_of<256, 2, 1>(); return true;
+        case 4: *k = kernel_of<256, 2, 2>(); return true;
+      }
+      return false;
+  }
+  return false;
+}
+
+int cuda_err(cudaError_t e, const char* what) {
+  return set_last_error(MOLOT_ERR_CUDA, (std::string(what) + ": " + cudaGetErrorString(e)).c_str());
+}
+
+}  // namespace
+}  // namespace molot
+
+using namespace molot;
+
+extern "C" int molot_attn_decode_strided_noalloc(const float* Q, const float* K, const float* V,
+                                                 float* O, int nq, int nkv, int n, int d,
+                                                 long long stride_t, long long stride_h,
+                                                 float scale, int pos_cur, int window,
+                                                 void* stream) {
+  if (!Q || !K || !V || !O) return set_last_error(MOLOT_ERR_INVALID, "null pointer");
+  if (nq <= 0 || nkv <= 0 || d <= 0 || n < 0 || nq % nkv)
+    return set_last_error(MOLOT_ERR_INVALID, "bad sizes (nq must be a positive multiple of nkv)");
+  const int G = nq / nkv;
+  Kernel k;
+  if (nkv > kNoAllocMaxSegments || G * d > kNoAllocMaxGroupDim || !pick(d, G, &k))
+    return set_last_error(MOLOT_ERR_UNSUPPORTED,
+                          "no-alloc decode supports head_dim 64/128/256, group 1/2/4/8 with "
+                          "group*head_dim <= 1024 and nkv <= 256");
+  if ((reinterpret_cast<uintptr_t>(K) & 15) || (reinterpret_cast<uintptr_t>(V) & 15) ||
+      (stride_t & 3) || (stride_h & 3))
+    return set_last_error(MOLOT_ERR_INVALID,
+                          "K/V must be 16-byte aligned with strides multiple of 4 floats");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_err(e, "cudaGetDevice");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int t0 = (window > 0 && pos_cur - window + 1 > 0) ? pos_cur - window + 1 : 0;
+  if (n <= t0) {  // empty attended range: zeros, as the reference (attn.h:163)
+    e = cudaMemsetAsync(O, 0, sizeof(float) * (size_t)nq * d, st);
+    return e == cudaSuccess ? MOLOT_OK : cuda_err(e, "cudaMemsetAsync(O)");
+  }
+  unsigned char* scratch = nullptr;
+  int rc = scratch_for(dev, &scratch);
+  if (rc) return rc;
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_err(e, "cudaDeviceGetAttribute");
+  const int blo = t0 / kBlk;
+  const int nblk = (n + kBlk - 1) / kBlk - blo;
+  const long long NB = (long long)nkv * nblk;
+  int grid = sms < kNoAllocMaxGrid ? sms : kNoAllocMaxGrid;
+  if (NB < grid) grid = (int)NB;
+  if (partial_record_floats(G, d) > kNoAllocMaxRecord)
+    return set_last_error(MOLOT_ERR_UNSUPPORTED, "partial record exceeds the no-alloc scratch");
+
+  float* partials = reinterpret_cast<float*>(scratch);
+  int* counters = reinterpret_cast<int*>(scratch + kNoAllocPartialBytes);
+  int* status = reinterpret_cast<int*>(scratch + kNoAllocPartialBytes + kNoAllocCounterBytes);
+  // Tickets and status must start at zero; the previous call may have left
+  // them otherwise if it gave up on a wait.
+  e = cudaMemsetAsync(counters, 0, kNoAllocCounterBytes + kNoAllocStatusBytes, st);
+  if (e != cudaSuccess) return cuda_err(e, "cudaMemsetAsync(no-alloc tickets)");
+  e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
+  if (e != cudaSuccess) return cuda_err(e, "cudaFuncSetAttribute");
+
+  DecodeArgs a = {};
+  a.Q = Q;
+  a.q_bstride = (long long)nq * d;
+  a.O = O;
+  a.o_bstride = (long long)nq * d;
+  a.K = K;
+  a.V = V;
+  a.stride_t = stride_t;
+  a.stride_h = stride_h;
+  a.nkv = nkv;
+  a.G = G;
+  a.scale = scale;
+  a.uniform = 1;
+  a.n = n;
+  a.t0 = t0;
+  a.S = nkv;
+  a.NB = NB;
+  a.nblk_u = nblk;
+  a.blo_u = blo;
+  a.partials = partials;
+  a.counters = counters;
+  a.status = status;
+  a.timeout_ns = 2000000000ull;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kDecodeThreads);
+  cfg.dynamicSmemBytes = k.smem;
+  cfg.stream = st;
+  void* args[] = {&a};
+  e = cudaLaunchKernelExC(&cfg, k.fn, args);
+  return e == cudaSuccess ? MOLOT_OK : cuda_err(e, "launch (no-alloc decode)");
+}
