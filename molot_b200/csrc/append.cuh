@@ -14,6 +14,8 @@
 
 #include <cstdint>
 
+#include "ptx.cuh"
+
 namespace molot {
 
 struct AppendArgs {
@@ -76,6 +78,12 @@ __global__ void __launch_bounds__(kAppendWarps * 32)
     norm_rope_append_kernel(const __grid_constant__ AppendArgs a) {
   static_assert(D % 16 == 0, "head dim must be a multiple of 16");
   constexpr int H = D / 2;
+  // Programmatic dependent launch: the next launch (the decode) may start at
+  // once -- it streams only KV rows older than the one written here until it
+  // waits for this grid.  Everything this kernel reads or writes comes after
+  // the wait for the preceding grid.
+  if (threadIdx.x == 0) ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int head = blockIdx.x * kAppendWarps + warp;

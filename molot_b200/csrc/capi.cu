@@ -63,13 +63,13 @@ int sm_count(int dev) {
 // ------------------------------------------------------------- workspace
 
 // Device scratch owned by one ordered stream of calls: split-KV partials,
-// per-segment tickets (zero between launches), the device status word and
-// plan arrays.  Grows only; growth synchronises the device.
+// the device status word and plan arrays.  Grows only; growth synchronises
+// the device.
 struct Workspace {
   int device = -1;
   float* partials = nullptr;
   size_t partials_cap = 0;
-  int* counters = nullptr;
+  int* counters = nullptr;  // per-segment tickets, zero between launches
   size_t counters_cap = 0;
   int* status = nullptr;
   int* plan = nullptr;
@@ -218,14 +218,20 @@ int prepare_kernel(const KernelRef& k, int dev) {
   return MOLOT_OK;
 }
 
+// Every kernel of the library is launched with programmatic stream
+// serialisation: it may start while the preceding kernel drains, and reads
+// what that kernel wrote only after griddepcontrol.wait.
 int launch(const void* fn, dim3 grid, dim3 block, int smem, cudaStream_t st, void* arg) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cfg.attrs = nullptr;
-  cfg.numAttrs = 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   void* args[] = {arg};
   MOLOT_CUDA(cudaLaunchKernelExC(&cfg, fn, args));
   return MOLOT_OK;
@@ -247,10 +253,18 @@ int check_shape(int nq, int nkv, int d, KernelRef* k) {
   return MOLOT_OK;
 }
 
-// Single-sequence decode over a strided contiguous cache.
+// One decode grid; split segments are merged inside it by their last CTA.
+int launch_decode(const KernelRef& k, DecodeArgs& a, cudaStream_t st) {
+  return launch(k.fn, dim3(a.grid), dim3(kDecodeThreads), k.smem, st, &a);
+}
+
+// Single-sequence decode over a strided contiguous cache.  prefetch_old_rows:
+// see DecodeArgs (set only when the preceding launch is the library's append
+// of slot n-1).
 int decode_uniform(Workspace& ws, const float* Q, float* O, const float* K, const float* V,
                    int nq, int nkv, int n, int d, long long stride_t, long long stride_h,
-                   float scale, int pos_cur, int window, cudaStream_t st) {
+                   float scale, int pos_cur, int window, cudaStream_t st,
+                   bool prefetch_old_rows = false) {
   KernelRef k;
   int rc = check_shape(nq, nkv, d, &k);
   if (rc) return rc;
@@ -273,6 +287,8 @@ int decode_uniform(Workspace& ws, const float* Q, float* O, const float* K, cons
   if ((rc = ws.ensure(dev, (size_t)2 * grid * partial_record_floats(G, d), nkv, 0))) return rc;
   if ((rc = prepare_kernel(k, dev))) return rc;
   DecodeArgs a = {};
+  a.grid = grid;
+  a.prefetch_old_rows = prefetch_old_rows ? 1 : 0;
   a.Q = Q;
   a.q_bstride = (long long)nq * d;
   a.O = O;
@@ -297,7 +313,7 @@ int decode_uniform(Workspace& ws, const float* Q, float* O, const float* K, cons
   a.counters = ws.counters;
   a.status = ws.status;
   a.timeout_ns = kWaitLimitNs;
-  return launch(k.fn, dim3(grid), dim3(kDecodeThreads), k.smem, st, &a);
+  return launch_decode(k, a, st);
 }
 
 int append_launch(const AppendArgs& a, int d, int B, cudaStream_t st) {
@@ -400,6 +416,10 @@ struct molot_kv_cache {
   float* base = nullptr;
   std::vector<int> len;
   Workspace ws;
+  // Layer whose newest slot the handle's most recent launch appended (-1 if
+  // the most recent operation was anything else).  A decode of that layer
+  // may stream its older slots before the append has completed.
+  int last_append_layer = -1;
 };
 
 struct molot_paged_plan {
@@ -415,6 +435,8 @@ struct molot_paged_plan {
   size_t o_n = 0, o_t0 = 0, o_pos = 0, o_slot = 0, o_prefix = 0, o_cta = 0;
   std::vector<int> h_n, h_t0, h_pos, h_slot, h_prefix, h_cta;
   bool all_empty = false;
+  // K pool whose newest slots the plan's most recent launch appended.
+  const float* appended_pool = nullptr;
 };
 
 extern "C" {
@@ -611,6 +633,7 @@ int molot_kv_set_length(molot_kv_cache* kv, int layer, int n) {
   if (!kv || layer < 0 || layer >= kv->n_layers || n < 0 || n > kv->cap)
     return fail(MOLOT_ERR_INVALID, "bad layer or length");
   kv->len[layer] = n;
+  kv->last_append_layer = -1;
   return MOLOT_OK;
 }
 
@@ -627,6 +650,7 @@ int molot_kv_write(molot_kv_cache* kv, int layer, int slot0, int nrows, const fl
   if (!k || !v || slot0 < 0 || nrows < 0 || slot0 + nrows > kv->cap)
     return fail(MOLOT_ERR_INVALID, "rows outside the cache");
   if (nrows == 0) return MOLOT_OK;
+  kv->last_append_layer = -1;
   float *kc, *vc;
   molot_kv_layer_data(kv, layer, &kc, &vc);
   // [nrows][nkv*hd] rows in, [nkv][cap][hd] head-major cache out: one
@@ -656,6 +680,7 @@ int molot_attn_append_rope(molot_kv_cache* kv, int layer, const float* q, const 
                           (cudaStream_t)stream);
   if (rc) return rc;
   kv->len[layer]++;
+  kv->last_append_layer = layer;
   return MOLOT_OK;
 }
 
@@ -667,8 +692,11 @@ int molot_attn_decode(molot_kv_cache* kv, int src_layer, const float* q, float* 
   if (n == 0) return fail(MOLOT_ERR_CACHE_EMPTY, "fwd: shared KV empty");
   float *kc, *vc;
   molot_kv_layer_data(kv, src_layer, &kc, &vc);
+  const bool prefetch = kv->last_append_layer == src_layer;
+  kv->last_append_layer = -1;
   return decode_uniform(kv->ws, q, o, kc, vc, nq, kv->nkv, n, kv->hd, kv->hd,
-                        (long long)kv->cap * kv->hd, scale, pos_cur, window, (cudaStream_t)stream);
+                        (long long)kv->cap * kv->hd, scale, pos_cur, window, (cudaStream_t)stream,
+                        prefetch);
 }
 
 int molot_kv_check(molot_kv_cache* kv, void* stream) {
@@ -842,7 +870,13 @@ int molot_paged_decode(molot_paged_plan* p, const float* Q, float* O, const floa
   a.counters = p->ws.counters;
   a.status = p->ws.status;
   a.timeout_ns = kWaitLimitNs;
-  return launch(k.fn, dim3(p->grid), dim3(kDecodeThreads), k.smem, st, &a);
+  a.grid = p->grid;
+  // Older slots were written two or more launches back only when this
+  // plan's most recent launch appended the newest slot of every sequence
+  // (into these very pools).
+  a.prefetch_old_rows = (p->appended_pool == k_pool) ? 1 : 0;
+  p->appended_pool = nullptr;
+  return launch_decode(k, a, st);
 }
 
 int molot_paged_append(molot_paged_plan* p, const float* q, const float* k, const float* v,
@@ -879,7 +913,9 @@ int molot_paged_append(molot_paged_plan* p, const float* q, const float* k, cons
   a.page_size = page_size;
   a.page_stride = (long long)p->nkv * page_size * p->d;
   a.page_hstride = (long long)page_size * p->d;
-  return append_launch(a, p->d, p->B, (cudaStream_t)stream);
+  int rc = append_launch(a, p->d, p->B, (cudaStream_t)stream);
+  p->appended_pool = rc == MOLOT_OK ? k_pool : nullptr;
+  return rc;
 }
 
 int molot_paged_check(molot_paged_plan* p, void* stream) {

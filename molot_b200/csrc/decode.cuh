@@ -83,9 +83,16 @@ struct DecodeArgs {
   int S;
   long long NB;
   int nblk_u, blo_u;  // uniform: blocks per segment and first block index
+  int grid;  // CTAs of the decode grid (the partition is computed from it)
+  // Programmatic dependent launch.  When set, the producer may stream each
+  // segment's slots below its newest one (n-1) before the preceding launch
+  // has completed: they were written two or more launches earlier (the
+  // preceding launch is the append that wrote slot n-1).  When clear, it
+  // waits before its first copy.
+  int prefetch_old_rows;
   // Scratch.
-  float* partials;  // [2*grid][G*D + 2*G]
-  int* counters;    // [S], zero between launches
+  float* partials;  // [2*grid][partial_record_floats(G, D)]
+  int* counters;    // [S] per-segment tickets, zero between launches
   int* status;
   unsigned long long timeout_ns;
 };
@@ -154,7 +161,7 @@ __device__ __forceinline__ SegView seg_view(const DecodeArgs& a, int s) {
 }
 
 __device__ __forceinline__ int first_seg_of_cta(const DecodeArgs& a, int c) {
-  if (a.uniform) return (int)(((long long)c * a.NB / gridDim.x) / a.nblk_u);
+  if (a.uniform) return (int)(((long long)c * a.NB / a.grid) / a.nblk_u);
   return __ldg(a.cta_seg + c);
 }
 
@@ -268,6 +275,102 @@ __device__ __forceinline__ void process_rows(const float* kr, const float* vr, i
   }
 }
 
+// Merge of a split segment's per-CTA partial records (log2-domain max m, sum
+// l, unnormalised o), run by the 256 consumer threads of the CTA that drew
+// the segment's last ticket.  CTAs cf..cl contributed; every CTA after the
+// first starts inside the segment (its slot 0), the first keeps the segment
+// in slot 0 only if its own range starts there too.  Each thread owns a
+// float4 chunk of o[G][D] and a share (csplit) of the partials, issuing up
+// to 16 partials' loads before merging them with online rescaling; shares
+// are folded through `red` ([256][6] floats of shared memory).
+template <int D>
+__device__ __forceinline__ void combine_segment(const DecodeArgs& a, int s, const SegView& sv,
+                                                long long cf, long long cl, float* red, int ctid,
+                                                float* out_seg) {
+  constexpr int kBatch = 16;
+  const int G = a.G;
+  const int psz = partial_record_floats(G, D);
+  const int nc = (int)(cl - cf + 1);
+  const int slot_first = 2 * (int)cf + (((long long)cf * a.NB / a.grid) >= sv.gbeg ? 0 : 1);
+  const int nchunk = G * D / 4;
+  const int csplit = max(1, (kConsumerWarps * 32) / nchunk);
+  for (int task = ctid; task < nchunk * csplit; task += kConsumerWarps * 32) {
+    const int chunk = task % nchunk;
+    const int part_i = task / nchunk;
+    const int hl = (chunk * 4) / D;
+    float M = -CUDART_INF_F, L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k0 = part_i; k0 < nc; k0 += kBatch * csplit) {
+      float mc[kBatch], lc[kBatch];
+      float4 oc[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int k = k0 + u * csplit;
+        if (k < nc) {
+          const int sl = k == 0 ? slot_first : 2 * ((int)cf + k);
+          const float* pp = a.partials + (size_t)sl * psz;
+          mc[u] = __ldcg(pp + G * D + hl);
+          lc[u] = __ldcg(pp + G * D + G + hl);
+          oc[u] = __ldcg(reinterpret_cast<const float4*>(pp) + chunk);
+        } else {
+          mc[u] = -CUDART_INF_F;
+          lc[u] = 0.f;
+          oc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const float Mn = fmaxf(M, mc[u]);
+        const float fa = (M == -CUDART_INF_F) ? 0.f : ex2(M - Mn);
+        const float fb = (mc[u] == -CUDART_INF_F) ? 0.f : ex2(mc[u] - Mn);
+        L = L * fa + lc[u] * fb;
+        acc.x = acc.x * fa + oc[u].x * fb;
+        acc.y = acc.y * fa + oc[u].y * fb;
+        acc.z = acc.z * fa + oc[u].z * fb;
+        acc.w = acc.w * fa + oc[u].w * fb;
+        M = Mn;
+      }
+    }
+    if (csplit == 1) {
+      float* dst = out_seg + chunk * 4;
+      dst[0] = acc.x / L;
+      dst[1] = acc.y / L;
+      dst[2] = acc.z / L;
+      dst[3] = acc.w / L;
+    } else {
+      // csplit > 1 implies nchunk * csplit <= 256: the task fits `red`.
+      float* r = red + (size_t)task * 6;
+      r[0] = M;
+      r[1] = L;
+      r[2] = acc.x;
+      r[3] = acc.y;
+      r[4] = acc.z;
+      r[5] = acc.w;
+    }
+  }
+  ptx::named_bar_sync(1, kConsumerWarps * 32);
+  for (int chunk = ctid; csplit > 1 && chunk < nchunk; chunk += kConsumerWarps * 32) {
+    float M = -CUDART_INF_F;
+    for (int p = 0; p < csplit; ++p) M = fmaxf(M, red[(size_t)(p * nchunk + chunk) * 6]);
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p = 0; p < csplit; ++p) {
+      const float* r = red + (size_t)(p * nchunk + chunk) * 6;
+      const float f = (r[0] == -CUDART_INF_F) ? 0.f : ex2(r[0] - M);
+      L += r[1] * f;
+      acc.x += r[2] * f;
+      acc.y += r[3] * f;
+      acc.z += r[4] * f;
+      acc.w += r[5] * f;
+    }
+    float* dst = out_seg + chunk * 4;
+    dst[0] = acc.x / L;
+    dst[1] = acc.y / L;
+    dst[2] = acc.z / L;
+    dst[3] = acc.w / L;
+  }
+}
+
 template <int D, int GS, int HS>
 __global__ void __launch_bounds__(kDecodeThreads, 1)
     gqa_decode_kernel(const __grid_constant__ DecodeArgs a) {
@@ -303,12 +406,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       ptx::mbar_init(empty_bar + i, kConsumerWarps);
     }
     *abort_flag = 0;
-    *ticket_sm = 0;
     ptx::fence_mbar_init();
   }
   __syncthreads();
 
-  const int grid = gridDim.x;
+  const int grid = a.grid;
   const long long cbeg = (long long)blockIdx.x * a.NB / grid;
   const long long cend = (long long)(blockIdx.x + 1) * a.NB / grid;
   const int s_first = first_seg_of_cta(a, blockIdx.x);
@@ -319,6 +421,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     if (warp != kConsumerWarps) return;
     const uint64_t pol = ptx::policy_evict_first();
     const bool rows_contig = (a.block_table != nullptr) || (a.stride_t == D);
+    bool waited = false;  // griddepcontrol.wait done by this warp
     int it = 0;
     long long pos = cbeg;
     int s = s_first;
@@ -340,6 +443,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
           }
           __syncwarp();
           const int tok0 = blk * kBlk;
+          // Slots written by the immediately preceding launch (the new
+          // token's row) may only be read after that launch has completed.
+          if (!waited && (!a.prefetch_old_rows || min(tok0 + TS::T, pt1) >= sv.n)) {
+            ptx::pdl_wait();
+            waited = true;
+          }
           int qa[4], qn[4];
           uint32_t bytes = 0;
 #pragma unroll
@@ -415,6 +524,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
 
   // -------------------------------------------------------------- consumers
   ptx::setmaxnreg_inc<kConsumerRegs>();
+  // q, the KV row appended just before and the scratch the previous
+  // decode/combine pair used are only touched after the preceding launch
+  // completed.  The trigger comes after that wait: when the next grids
+  // start early, everything up to the launch before this one is complete,
+  // which is what makes a later decode's early reads of older KV rows safe.
+  ptx::pdl_wait();
+  if (threadIdx.x == 0) ptx::pdl_launch_dependents();
   const int set = warp / WPS;  // head set of this warp
   const int wi = warp - set * WPS;
   const int grp = lane >> 3;   // row group == quarter read
@@ -557,102 +673,18 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
           }
         }
       }
-      if (!whole) __threadfence();
+      // Every partial (or output) write of this CTA is issued before the
+      // barrier; the merge buffer is free again after it.
       ptx::named_bar_sync(1, kConsumerWarps * 32);
-
       if (!whole) {
+        // One thread publishes the CTA's partial and takes a ticket; the CTA
+        // that draws the last ticket of the segment merges all partials.
         const long long cf = cta_of_block(sv.gbeg, a.NB, grid);
         const long long cl = cta_of_block(sv.gend - 1, a.NB, grid);
-        if (ctid == 0) *ticket_sm = atomicAdd(a.counters + s, 1);
+        if (ctid == 0) *ticket_sm = ptx::atom_add_acq_rel_gpu(a.counters + s, 1);
         ptx::named_bar_sync(1, kConsumerWarps * 32);
         if (*ticket_sm == (int)(cl - cf)) {
-          // Last CTA of the segment: merge the nc partials.  Every CTA after
-          // the first starts inside this segment (slot 0); the first keeps it
-          // in slot 0 only if its own range starts here too.
-          __threadfence();
-          const int nc = (int)(cl - cf + 1);
-          const int slot_first =
-              2 * (int)cf + (((long long)cf * a.NB / grid) >= sv.gbeg ? 0 : 1);
-          const int nchunk = G * D / 4;  // float4 chunks of o[G][D]
-          const int csplit = max(1, (kConsumerWarps * 32) / nchunk);
-          float* red = merge_o;  // [task][6] scratch, merge buffer is free now
-          for (int task = ctid; task < nchunk * csplit; task += kConsumerWarps * 32) {
-            const int chunk = task % nchunk;
-            const int part_i = task / nchunk;
-            const int hl = (chunk * 4) / D;
-            float M = -CUDART_INF_F, L = 0.f;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int k0 = part_i; k0 < nc; k0 += 8 * csplit) {
-              float mc[8], lc[8];
-              float4 oc[8];
-#pragma unroll
-              for (int u = 0; u < 8; ++u) {
-                const int k = k0 + u * csplit;
-                if (k < nc) {
-                  const int sl = k == 0 ? slot_first : 2 * ((int)cf + k);
-                  const float* pp = a.partials + (size_t)sl * psz;
-                  mc[u] = __ldcg(pp + G * D + hl);
-                  lc[u] = __ldcg(pp + G * D + G + hl);
-                  oc[u] = __ldcg(reinterpret_cast<const float4*>(pp) + chunk);
-                } else {
-                  mc[u] = -CUDART_INF_F;
-                  lc[u] = 0.f;
-                  oc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-              }
-#pragma unroll
-              for (int u = 0; u < 8; ++u) {
-                const float Mn = fmaxf(M, mc[u]);
-                const float fa = (M == -CUDART_INF_F) ? 0.f : ex2(M - Mn);
-                const float fb = (mc[u] == -CUDART_INF_F) ? 0.f : ex2(mc[u] - Mn);
-                L = L * fa + lc[u] * fb;
-                acc.x = acc.x * fa + oc[u].x * fb;
-                acc.y = acc.y * fa + oc[u].y * fb;
-                acc.z = acc.z * fa + oc[u].z * fb;
-                acc.w = acc.w * fa + oc[u].w * fb;
-                M = Mn;
-              }
-            }
-            if (csplit == 1) {
-              // This thread saw every partial of the chunk.
-              float* dst = out_seg + chunk * 4;
-              dst[0] = acc.x / L;
-              dst[1] = acc.y / L;
-              dst[2] = acc.z / L;
-              dst[3] = acc.w / L;
-            } else {
-              // csplit > 1 means nchunk * csplit <= 256: the task index fits
-              // the [256][6] scratch.
-              float* r = red + (size_t)task * 6;
-              r[0] = M;
-              r[1] = L;
-              r[2] = acc.x;
-              r[3] = acc.y;
-              r[4] = acc.z;
-              r[5] = acc.w;
-            }
-          }
-          ptx::named_bar_sync(1, kConsumerWarps * 32);
-          for (int chunk = ctid; csplit > 1 && chunk < nchunk; chunk += kConsumerWarps * 32) {
-            float M = -CUDART_INF_F;
-            for (int p = 0; p < csplit; ++p) M = fmaxf(M, red[(size_t)(p * nchunk + chunk) * 6]);
-            float L = 0.f;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int p = 0; p < csplit; ++p) {
-              const float* r = red + (size_t)(p * nchunk + chunk) * 6;
-              const float f = (r[0] == -CUDART_INF_F) ? 0.f : ex2(r[0] - M);
-              L += r[1] * f;
-              acc.x += r[2] * f;
-              acc.y += r[3] * f;
-              acc.z += r[4] * f;
-              acc.w += r[5] * f;
-            }
-            float* dst = out_seg + chunk * 4;
-            dst[0] = acc.x / L;
-            dst[1] = acc.y / L;
-            dst[2] = acc.z / L;
-            dst[3] = acc.w / L;
-          }
+          combine_segment<D>(a, s, sv, cf, cl, merge_o, ctid, out_seg);
           if (ctid == 0) a.counters[s] = 0;
         }
         ptx::named_bar_sync(1, kConsumerWarps * 32);

@@ -17,7 +17,8 @@
 //
 // All calls share the one array, and it keeps what the last call left in it:
 // each call clears the tickets and the status word (cudaMemsetAsync on the
-// array, which allocates nothing) before its launch.  Calls whose work
+// array, which allocates nothing) before its launch; the partial records are
+// always written before they are read.  Calls whose work
 // overlaps on the GPU -- different streams, or different host threads
 // without ordering -- race on the array; order them on one stream.
 //
@@ -111,6 +112,7 @@ bool pick(int d, int g, Kernel* k) {
   return false;
 }
 
+
 int cuda_err(cudaError_t e, const char* what) {
   return set_last_error(MOLOT_ERR_CUDA, (std::string(what) + ": " + cudaGetErrorString(e)).c_str());
 }
@@ -164,7 +166,7 @@ extern "C" int molot_attn_decode_strided_noalloc(const float* Q, const float* K,
   float* partials = reinterpret_cast<float*>(scratch);
   int* counters = reinterpret_cast<int*>(scratch + kNoAllocPartialBytes);
   int* status = reinterpret_cast<int*>(scratch + kNoAllocPartialBytes + kNoAllocCounterBytes);
-  // Tickets and status must start at zero; the previous call may have left
+  // Tickets and status must start at zero; a previous call may have left
   // them otherwise if it gave up on a wait.
   e = cudaMemsetAsync(counters, 0, kNoAllocCounterBytes + kNoAllocStatusBytes, st);
   if (e != cudaSuccess) return cuda_err(e, "cudaMemsetAsync(no-alloc tickets)");
@@ -194,11 +196,18 @@ extern "C" int molot_attn_decode_strided_noalloc(const float* Q, const float* K,
   a.counters = counters;
   a.status = status;
   a.timeout_ns = 2000000000ull;
+  a.grid = grid;
+  a.prefetch_old_rows = 0;  // the caller's K/V may come from the preceding launch
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kDecodeThreads);
   cfg.dynamicSmemBytes = k.smem;
   cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   void* args[] = {&a};
   e = cudaLaunchKernelExC(&cfg, k.fn, args);
   return e == cudaSuccess ? MOLOT_OK : cuda_err(e, "launch (no-alloc decode)");
