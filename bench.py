@@ -392,10 +392,14 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["molot", "reference"], default="molot")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the layer count (small cases for profiler captures)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.layers > 0:
+        cfg["layers"] = args.layers
     if args.impl == "reference":
         return run_reference(args, cfg)
     return run_molot(args, cfg)
