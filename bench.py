@@ -6,8 +6,10 @@
 Default workload ("cfg2"): one decode step of a 32-layer
 Llama-shaped model at 16k context -- Hq=32, Hkv=8, head_dim=128, 16384 cached
 slots + the new token (n=16385), RoPE theta=5e5.  Per layer the step runs
-the library's public calls: fused QK-norm/RoPE/append (molot_attn_append_rope)
-and split-KV decode (molot_attn_decode) over the HBM-resident cache.  K/V and
+the library's public call molot_attn_step: QK-norm/RoPE of the raw q/k, the
+append of the new row and split-KV decode over the HBM-resident cache, in
+one launch (--path split: molot_attn_append_rope + molot_attn_decode, two
+launches).  K/V and
 q/k/v are seeded N(0,1) synthetic data generated on the device.  The 4.3 GB
 of KV is far larger than L2 (126 MB), so no flush is needed.
 
@@ -249,18 +251,26 @@ def run_molot(args, cfg):
     k_norm = (1 + 0.1 * torch.randn(d, device=dev, generator=gen)).contiguous()
     freq = torch.tensor([1.0 / cfg["theta"] ** (2.0 * i / d) for i in range(d // 2)],
                         dtype=torch.float32, device=dev)
-    q_rot = torch.empty((L, nq * d), device=dev)
+    q_rot = torch.randn((L, nq * d), device=dev, generator=gen)
     out = torch.empty((L, nq * d), device=dev)
     torch.cuda.synchronize()
+
+    fused = args.path == "fused"
 
     def step(qr, kr, vr, o, decode_only=False):
         st = torch.cuda.current_stream()
         for layer in range(L):
-            if not decode_only:
-                cache.set_length(layer, ctx)
+            if decode_only:
+                cache.decode(layer, q_rot[layer], o[layer], scale, ctx, cfg["window"], nq, st)
+                continue
+            cache.set_length(layer, ctx)
+            if fused:
+                cache.step(layer, qr[layer], kr[layer], vr[layer], o[layer], scale, ctx,
+                           cfg["window"], q_norm, k_norm, False, 1e-6, freq, nq, st)
+            else:
                 cache.append_rope(layer, qr[layer], kr[layer], vr[layer], q_rot[layer], q_norm,
                                   k_norm, False, 1e-6, freq, ctx, nq, st)
-            cache.decode(layer, q_rot[layer], o[layer], scale, ctx, cfg["window"], nq, st)
+                cache.decode(layer, q_rot[layer], o[layer], scale, ctx, cfg["window"], nq, st)
 
     def barrier():
         torch.cuda.synchronize()
@@ -312,11 +322,16 @@ def run_molot(args, cfg):
     ms = max_over_ranks(timed(graph.replay, args.steps))
     clk = clocks.stop()
     cache.check(stream)
-    # dominant kernel alone: L back-to-back decode launches per replay
-    for _ in range(args.warmup):
-        dgraph.replay()
-    dec_avg_ms = timed(dgraph.replay, args.steps) / L
-    cache.check(stream)
+    # dominant kernel: with the fused path every launch of the step is one
+    # (prologue + append + decode) kernel, so the step graph times it; the
+    # split path replays L back-to-back decode launches alone.
+    if fused:
+        dec_avg_ms = ms / L
+    else:
+        for _ in range(args.warmup):
+            dgraph.replay()
+        dec_avg_ms = timed(dgraph.replay, args.steps) / L
+        cache.check(stream)
 
     # ---- end-to-end through the public API with host copies (eager calls)
     h_q = torch.randn((L, nq * d), generator=torch.Generator().manual_seed(5)).pin_memory()
@@ -364,11 +379,15 @@ def run_molot(args, cfg):
                     "h2d_bytes_per_step": int(4 * L * (nq + 2 * nkv) * d),
                     "d2h_bytes_per_step": int(4 * L * nq * d),
                     "ms_per_step": round(e2e_ms, 4),
-                    "path": "molot_attn_append_rope + molot_attn_decode per layer, pinned H2D/D2H"},
-            "gpu_launches": 2 * L * args.steps,
+                    "path": (("molot_attn_step" if fused else
+                              "molot_attn_append_rope + molot_attn_decode")
+                             + " per layer, pinned H2D/D2H")},
+            "gpu_launches": (1 if fused else 2) * L * args.steps,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic, "kernel": "gqa_decode_kernel<128,4,1>",
+                         "timed": ("fused step launches (prologue + append + decode)" if fused
+                                   else "decode launches alone"),
                          "peak_source": f"{peak_kind} hbm_gbs",
                          "bytes_per_launch": kv_bytes_layer,
                          "avg_launch_ms": round(dec_avg_ms, 5)},
@@ -392,6 +411,9 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["molot", "reference"], default="molot")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--path", choices=["fused", "split"], default="split",
+                    help="fused: molot_attn_step (one launch per layer); split: "
+                         "molot_attn_append_rope + molot_attn_decode")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (small cases for profiler captures)")
     args = ap.parse_args(argv)

@@ -160,6 +160,18 @@ int molot_attn_append_rope(molot_kv_cache* kv, int layer, const float* q, const 
 int molot_attn_decode(molot_kv_cache* kv, int src_layer, const float* q, float* o, int nq,
                       float scale, int pos_cur, int window, void* stream);
 
+/* forward.h:554-590 for a KV-owning layer in one launch: the raw q (nq
+ * heads) and the new k, v rows get the QK-norm / V-norm / RoPE of
+ * molot_attn_append_rope, the new row is appended at slot n (n++), and the
+ * attention over slots [max(0, pos-window+1), n] is written to o ([nq][hd]).
+ * Same results as molot_attn_append_rope + molot_attn_decode(layer), without
+ * the rotated-q round trip or a second launch.  MOLOT_ERR_CACHE_FULL when
+ * n == cap (forward.h:570). */
+int molot_attn_step(molot_kv_cache* kv, int layer, const float* q, const float* k,
+                    const float* v, const float* q_norm, const float* k_norm, int v_norm,
+                    float eps, const float* freq, int pos, float* o, int nq, float scale,
+                    int window, void* stream);
+
 /* Synchronises the handle's stream work and reports device-side timeouts. */
 int molot_kv_check(molot_kv_cache* kv, void* stream);
 

@@ -93,6 +93,7 @@ _decl("molot_kv_write", [_p, _i, _i, _i, _p, _p, _p])
 _decl("molot_attn_append_rope", [_p, _i, _p, _p, _p, _p, _p, _p, _i, _f, _p, _i, _i, _p])
 _decl("molot_attn_decode", [_p, _i, _p, _p, _i, _f, _i, _i, _p])
 _decl("molot_kv_check", [_p, _p])
+_decl("molot_attn_step", [_p, _i, _p, _p, _p, _p, _p, _i, _f, _p, _i, _p, _i, _f, _i, _p])
 _decl("molot_paged_plan_create", [_pp])
 _decl("molot_paged_plan_destroy", [_p], None)
 _decl("molot_paged_plan_build", [_p, _i, _i, _i, _i, _p, _p, _i, _p])
@@ -318,6 +319,15 @@ class KVCache:
         check(_lib.molot_attn_append_rope(self._h, layer, _ptr(q), _ptr(k), _ptr(v), _ptr(q_out),
                                           _ptr(q_norm), _ptr(k_norm), int(v_norm), eps,
                                           _ptr(freq), pos, nq, _stream_ptr(stream)))
+
+    def step(self, layer, q, k, v, o, scale, pos, window=0, q_norm=None, k_norm=None,
+             v_norm=False, eps=1e-6, freq=None, nq=None, stream=None) -> None:
+        """forward.h:554-590 in one launch: prologue on the raw q/k/v, append
+        at slot n, attention into o."""
+        nq = nq if nq is not None else q.numel() // self.hd
+        check(_lib.molot_attn_step(self._h, layer, _ptr(q), _ptr(k), _ptr(v), _ptr(q_norm),
+                                   _ptr(k_norm), int(v_norm), eps, _ptr(freq), pos, _ptr(o), nq,
+                                   scale, window, _stream_ptr(stream)))
 
     def decode(self, src_layer, q, o, scale, pos_cur, window=0, nq=None, stream=None) -> None:
         nq = nq if nq is not None else q.numel() // self.hd

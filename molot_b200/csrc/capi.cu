@@ -264,7 +264,7 @@ int launch_decode(const KernelRef& k, DecodeArgs& a, cudaStream_t st) {
 int decode_uniform(Workspace& ws, const float* Q, float* O, const float* K, const float* V,
                    int nq, int nkv, int n, int d, long long stride_t, long long stride_h,
                    float scale, int pos_cur, int window, cudaStream_t st,
-                   bool prefetch_old_rows = false) {
+                   bool prefetch_old_rows = false, const DecodeArgs* fused = nullptr) {
   KernelRef k;
   int rc = check_shape(nq, nkv, d, &k);
   if (rc) return rc;
@@ -289,6 +289,19 @@ int decode_uniform(Workspace& ws, const float* Q, float* O, const float* K, cons
   DecodeArgs a = {};
   a.grid = grid;
   a.prefetch_old_rows = prefetch_old_rows ? 1 : 0;
+  if (fused) {  // per-token prologue fused into this launch (slot n-1 is new)
+    a.fused = 1;
+    a.k_raw = fused->k_raw;
+    a.v_raw = fused->v_raw;
+    a.q_norm = fused->q_norm;
+    a.k_norm = fused->k_norm;
+    a.v_norm = fused->v_norm;
+    a.eps = fused->eps;
+    a.freq = fused->freq;
+    a.pos = fused->pos;
+    a.K_w = fused->K_w;
+    a.V_w = fused->V_w;
+  }
   a.Q = Q;
   a.q_bstride = (long long)nq * d;
   a.O = O;
@@ -416,10 +429,36 @@ struct molot_kv_cache {
   float* base = nullptr;
   std::vector<int> len;
   Workspace ws;
-  // Layer whose newest slot the handle's most recent launch appended (-1 if
-  // the most recent operation was anything else).  A decode of that layer
-  // may stream its older slots before the append has completed.
-  int last_append_layer = -1;
+  // The handle's two most recent kernel launches on its stream (index 0 =
+  // latest), which decide whether a decode may stream older KV rows before
+  // griddepcontrol.wait.  An append releases its successor at once; a decode
+  // or step releases it only after its own wait, so when the preceding
+  // launch is decode-type, everything before it is complete.
+  enum Kind { kNone = 0, kAppend = 1, kDecode = 2 };
+  int hist_kind[2] = {kNone, kNone};
+  int hist_layer[2] = {-1, -1};  // layer whose cache that launch wrote
+  void record(int kind, int layer) {
+    hist_kind[1] = hist_kind[0];
+    hist_layer[1] = hist_layer[0];
+    hist_kind[0] = kind;
+    hist_layer[0] = layer;
+  }
+  void ordered() {  // a copy in the stream completed everything before it
+    hist_kind[0] = hist_kind[1] = kNone;
+    hist_layer[0] = hist_layer[1] = -1;
+  }
+  // decode(L) right after append(L): rows below n-1 were written two or more
+  // launches before the append, and the launch before the append neither
+  // released early nor wrote layer L.
+  bool decode_may_prefetch(int L) const {
+    return hist_kind[0] == kAppend && hist_layer[0] == L && hist_kind[1] != kAppend &&
+           hist_layer[1] != L;
+  }
+  // step(L): the preceding launch released this one only after its own
+  // wait, and did not write layer L itself.
+  bool step_may_prefetch(int L) const {
+    return hist_kind[0] != kAppend && hist_layer[0] != L;
+  }
 };
 
 struct molot_paged_plan {
@@ -633,7 +672,6 @@ int molot_kv_set_length(molot_kv_cache* kv, int layer, int n) {
   if (!kv || layer < 0 || layer >= kv->n_layers || n < 0 || n > kv->cap)
     return fail(MOLOT_ERR_INVALID, "bad layer or length");
   kv->len[layer] = n;
-  kv->last_append_layer = -1;
   return MOLOT_OK;
 }
 
@@ -650,7 +688,7 @@ int molot_kv_write(molot_kv_cache* kv, int layer, int slot0, int nrows, const fl
   if (!k || !v || slot0 < 0 || nrows < 0 || slot0 + nrows > kv->cap)
     return fail(MOLOT_ERR_INVALID, "rows outside the cache");
   if (nrows == 0) return MOLOT_OK;
-  kv->last_append_layer = -1;
+  kv->ordered();
   float *kc, *vc;
   molot_kv_layer_data(kv, layer, &kc, &vc);
   // [nrows][nkv*hd] rows in, [nkv][cap][hd] head-major cache out: one
@@ -680,7 +718,7 @@ int molot_attn_append_rope(molot_kv_cache* kv, int layer, const float* q, const 
                           (cudaStream_t)stream);
   if (rc) return rc;
   kv->len[layer]++;
-  kv->last_append_layer = layer;
+  kv->record(molot_kv_cache::kAppend, layer);
   return MOLOT_OK;
 }
 
@@ -692,11 +730,55 @@ int molot_attn_decode(molot_kv_cache* kv, int src_layer, const float* q, float* 
   if (n == 0) return fail(MOLOT_ERR_CACHE_EMPTY, "fwd: shared KV empty");
   float *kc, *vc;
   molot_kv_layer_data(kv, src_layer, &kc, &vc);
-  const bool prefetch = kv->last_append_layer == src_layer;
-  kv->last_append_layer = -1;
-  return decode_uniform(kv->ws, q, o, kc, vc, nq, kv->nkv, n, kv->hd, kv->hd,
-                        (long long)kv->cap * kv->hd, scale, pos_cur, window, (cudaStream_t)stream,
-                        prefetch);
+  const bool prefetch = kv->decode_may_prefetch(src_layer);
+  int rc = decode_uniform(kv->ws, q, o, kc, vc, nq, kv->nkv, n, kv->hd, kv->hd,
+                          (long long)kv->cap * kv->hd, scale, pos_cur, window,
+                          (cudaStream_t)stream, prefetch);
+  if (rc == MOLOT_OK) kv->record(molot_kv_cache::kDecode, -1);
+  return rc;
+}
+
+int molot_attn_step(molot_kv_cache* kv, int layer, const float* q, const float* k,
+                    const float* v, const float* q_norm, const float* k_norm, int v_norm,
+                    float eps, const float* freq, int pos, float* o, int nq, float scale,
+                    int window, void* stream) {
+  if (!kv || layer < 0 || layer >= kv->n_layers) return fail(MOLOT_ERR_INVALID, "bad layer");
+  if (!q || !k || !v || !o) return fail(MOLOT_ERR_INVALID, "null pointer");
+  if (kv->len[layer] >= kv->cap) return fail(MOLOT_ERR_CACHE_FULL, "fwd: KV cache full");
+  float *kc, *vc;
+  molot_kv_layer_data(kv, layer, &kc, &vc);
+  DecodeArgs f = {};
+  f.k_raw = k;
+  f.v_raw = v;
+  f.q_norm = q_norm;
+  f.k_norm = k_norm;
+  f.v_norm = v_norm;
+  f.eps = eps;
+  f.freq = freq;
+  f.pos = pos;
+  f.K_w = kc;
+  f.V_w = vc;
+  const int n = kv->len[layer] + 1;  // the new token occupies slot n-1
+  if (n <= window_start(pos, window)) {
+    // Nothing to attend to (attn.h:163 leaves zeros); still append the row.
+    // The rotated q goes to o, which the memset then clears.
+    int rc = append_strided(q, k, v, o, q_norm, k_norm, v_norm, eps, freq, pos, kc, vc,
+                            n - 1, nq, kv->nkv, kv->hd, kv->hd, (long long)kv->cap * kv->hd,
+                            (cudaStream_t)stream);
+    if (rc) return rc;
+    MOLOT_CUDA(cudaMemsetAsync(o, 0, sizeof(float) * (size_t)nq * kv->hd, (cudaStream_t)stream));
+    kv->len[layer] = n;
+    kv->ordered();
+    return MOLOT_OK;
+  }
+  const bool prefetch = kv->step_may_prefetch(layer);
+  int rc = decode_uniform(kv->ws, q, o, kc, vc, nq, kv->nkv, n, kv->hd, kv->hd,
+                          (long long)kv->cap * kv->hd, scale, pos, window, (cudaStream_t)stream,
+                          prefetch, &f);
+  if (rc) return rc;
+  kv->len[layer] = n;
+  kv->record(molot_kv_cache::kDecode, layer);
+  return MOLOT_OK;
 }
 
 int molot_kv_check(molot_kv_cache* kv, void* stream) {

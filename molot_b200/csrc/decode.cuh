@@ -34,6 +34,7 @@
 
 #include <cstdint>
 
+#include "append.cuh"
 #include "ptx.cuh"
 
 namespace molot {
@@ -90,6 +91,22 @@ struct DecodeArgs {
   // preceding launch is the append that wrote slot n-1).  When clear, it
   // waits before its first copy.
   int prefetch_old_rows;
+  // Fused per-token prologue (forward.h:554-575), single sequence only.  When
+  // fused != 0, Q holds the raw q projection and slot n-1 is the new token:
+  // the kernel normalises and rotates q in registers, normalises/rotates the
+  // new k and v rows, writes them to slot n-1 of K_w / V_w (the writable
+  // views of K / V) and attends to them without streaming that slot.
+  int fused;
+  const float* k_raw;   // [nkv][D]
+  const float* v_raw;   // [nkv][D]
+  const float* q_norm;  // [D] or null
+  const float* k_norm;  // [D] or null
+  int v_norm;
+  float eps;
+  const float* freq;    // [D/2] or null (NoPE)
+  int pos;              // RoPE position of the new token
+  float* K_w;
+  float* V_w;
   // Scratch.
   float* partials;  // [2*grid][partial_record_floats(G, D)]
   int* counters;    // [S] per-segment tickets, zero between launches
@@ -120,8 +137,9 @@ struct DecodeSmem {
       4 * (kConsumerWarps * GS * D > 6 * kConsumerWarps * 32 ? kConsumerWarps * GS * D
                                                              : 6 * kConsumerWarps * 32);
   static constexpr int kMergeML = kConsumerWarps * GS * 2 * 4;
+  static constexpr int kNewRow = 2 * D * 4;  // fused mode: the new k and v rows
   static constexpr int kBars = 2 * TS::STAGES * 8;
-  static constexpr int kTotal = kStageBytes + kMergeO + kMergeML + kBars + 16;
+  static constexpr int kTotal = kStageBytes + kMergeO + kMergeML + kNewRow + kBars + 16;
 };
 
 // Floats of one partial record: o[G][D], then m[G], l[G]; padded to a
@@ -192,14 +210,17 @@ template <int D, int GS, int RC, bool FULL>
 __device__ __forceinline__ void process_rows(const float* kr, const float* vr, int tok, int pt0,
                                              int pt1, float scale, float (&q)[GS][D / 8],
                                              float (&o)[GS][D / 8], float (&m2)[GS],
-                                             float (&l)[GS]) {
+                                             float (&l)[GS], int new_tok, const float* nk,
+                                             const float* nv) {
   constexpr int DV = D / 16;
   float sc[RC][GS];
   bool ok[RC];
 #pragma unroll
   for (int r = 0; r < RC; ++r) {
     ok[r] = FULL || (tok + r >= pt0 && tok + r < pt1);
-    const float* k = kr + r * D;
+    // The fused step's new row (slot new_tok) is not in the stage; its k and
+    // v sit in shared memory (nk, nv).  Full tiles never contain it.
+    const float* k = (!FULL && tok + r == new_tok) ? nk : kr + r * D;
     float a0[GS], a1[GS];
 #pragma unroll
     for (int h = 0; h < GS; ++h) {
@@ -261,7 +282,7 @@ __device__ __forceinline__ void process_rows(const float* kr, const float* vr, i
   }
 #pragma unroll
   for (int r = 0; r < RC; ++r) {
-    const float* v = vr + r * D;
+    const float* v = (!FULL && tok + r == new_tok) ? nv : vr + r * D;
 #pragma unroll
     for (int mm = 0; mm < DV; ++mm) {
       const float v0 = FULL ? v[16 * mm] : (ok[r] ? v[16 * mm] : 0.f);
@@ -271,6 +292,106 @@ __device__ __forceinline__ void process_rows(const float* kr, const float* vr, i
         o[h][2 * mm] = __fmaf_rn(p[r][h], v0, o[h][2 * mm]);
         o[h][2 * mm + 1] = __fmaf_rn(p[r][h], v1, o[h][2 * mm + 1]);
       }
+    }
+  }
+}
+
+// Fused step, q side (forward.h:554-558): the warp's q registers hold the
+// raw projection in the row-group lane layout (dims {16m+l8, 16m+l8+8}).
+// Per-head weighted RMSNorm with the reference's sum-of-squares order (the
+// same tree as the dot), then NEOX RoPE; a lane holds both halves of each
+// of its rotation pairs (dim i and i + D/2), so no data moves between lanes.
+// The arithmetic is operation for operation that of norm_rope_append_kernel.
+template <int D, int GS>
+__device__ __forceinline__ void fused_rotate_q(const DecodeArgs& a, float (&q)[GS][D / 8],
+                                               int l8) {
+  constexpr int DV = D / 16;
+  constexpr int HV = DV / 2;
+  if (a.q_norm) {
+#pragma unroll
+    for (int h = 0; h < GS; ++h) {
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int mm = 0; mm < DV; ++mm) {
+        a0 = __fmaf_rn(q[h][2 * mm], q[h][2 * mm], a0);
+        a1 = __fmaf_rn(q[h][2 * mm + 1], q[h][2 * mm + 1], a1);
+      }
+      float t = __fadd_rn(a0, a1);
+      t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 4));
+      t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
+      t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 1));
+      const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)D), a.eps)));
+#pragma unroll
+      for (int i = 0; i < 2 * DV; ++i) {
+        const int dim = 16 * (i >> 1) + l8 + 8 * (i & 1);
+        q[h][i] = __fmul_rn(__fmul_rn(q[h][i], inv), __ldg(a.q_norm + dim));
+      }
+    }
+  }
+  if (a.freq) {
+#pragma unroll
+    for (int i = 0; i < 2 * HV; ++i) {
+      const int dim = 16 * (i >> 1) + l8 + 8 * (i & 1);  // < D/2; partner dim + D/2
+      float s, c;
+      sincosf(__fmul_rn((float)a.pos, __ldg(a.freq + dim)), &s, &c);
+#pragma unroll
+      for (int h = 0; h < GS; ++h) {
+        const float y0 = q[h][i], y1 = q[h][i + 2 * HV];
+        q[h][i] = __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, s));
+        q[h][i + 2 * HV] = __fadd_rn(__fmul_rn(y0, s), __fmul_rn(y1, c));
+      }
+    }
+  }
+}
+
+// Fused step, k/v side (forward.h:562-575) for kv head sv.g: warp 0 builds
+// the normalised, rotated k row, warp 1 the normalised v row (plain RMSNorm
+// over all nkv*D values); both land in shared memory (for this launch) and
+// in slot n-1 of the cache (for later ones).
+template <int D>
+__device__ __forceinline__ void fused_new_row(const DecodeArgs& a, const SegView& sv, int warp,
+                                              int lane, float* new_k, float* new_v) {
+  constexpr int H = D / 2;
+  const long long row = (long long)sv.b * a.kv_bstride + (long long)(sv.n - 1) * a.stride_t +
+                        (long long)sv.g * a.stride_h;
+  if (warp == 0) {
+    const float* x = a.k_raw + (long long)sv.g * D;
+    float inv = 1.f;
+    if (a.k_norm) {
+      const float ss = warp_sumsq16(x, D, lane);
+      inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), a.eps)));
+    }
+    for (int i = lane; i < H; i += 32) {
+      float y0 = x[i], y1 = x[i + H];
+      if (a.k_norm) {
+        y0 = __fmul_rn(__fmul_rn(y0, inv), a.k_norm[i]);
+        y1 = __fmul_rn(__fmul_rn(y1, inv), a.k_norm[i + H]);
+      }
+      if (a.freq) {
+        float s, c;
+        sincosf(__fmul_rn((float)a.pos, a.freq[i]), &s, &c);
+        const float z0 = __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, s));
+        const float z1 = __fadd_rn(__fmul_rn(y0, s), __fmul_rn(y1, c));
+        y0 = z0;
+        y1 = z1;
+      }
+      new_k[i] = y0;
+      new_k[i + H] = y1;
+      a.K_w[row + i] = y0;
+      a.K_w[row + i + H] = y1;
+    }
+  } else {
+    float vinv = 1.f;
+    if (a.v_norm) {
+      const int nv = a.nkv * D;
+      const float ss = warp_sumsq16(a.v_raw, nv, lane);
+      vinv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)nv), a.eps)));
+    }
+    const float* vh = a.v_raw + (long long)sv.g * D;
+    for (int i = lane; i < D; i += 32) {
+      const float val = a.v_norm ? __fmul_rn(vh[i], vinv) : vh[i];
+      new_v[i] = val;
+      a.V_w[row + i] = val;
     }
   }
 }
@@ -391,8 +512,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   unsigned char* stages = smem;
   float* merge_o = reinterpret_cast<float*>(smem + SM::kStageBytes);
   float* merge_ml = reinterpret_cast<float*>(smem + SM::kStageBytes + SM::kMergeO);
-  uint64_t* full_bar =
-      reinterpret_cast<uint64_t*>(smem + SM::kStageBytes + SM::kMergeO + SM::kMergeML);
+  float* new_k = reinterpret_cast<float*>(smem + SM::kStageBytes + SM::kMergeO + SM::kMergeML);
+  float* new_v = new_k + D;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + SM::kStageBytes + SM::kMergeO +
+                                                   SM::kMergeML + SM::kNewRow);
   uint64_t* empty_bar = full_bar + STAGES;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty_bar + STAGES);
   volatile int* ticket_sm = abort_flag + 1;
@@ -433,6 +556,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         const int le = sv.blo + (int)(pend - sv.gbeg);
         const int pt0 = max(sv.t0, lb * kBlk);
         const int pt1 = min(sv.n, le * kBlk);
+        // Fused mode: slot n-1 is produced in this launch and never streamed.
+        const int pt1c = a.fused ? min(pt1, sv.n - 1) : pt1;
         for (int blk = lb; blk < le; blk += TS::TB, ++it) {
           const int stage = it % STAGES;
           if (it >= STAGES && !*abort_flag) {
@@ -445,7 +570,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
           const int tok0 = blk * kBlk;
           // Slots written by the immediately preceding launch (the new
           // token's row) may only be read after that launch has completed.
-          if (!waited && (!a.prefetch_old_rows || min(tok0 + TS::T, pt1) >= sv.n)) {
+          if (!waited && (!a.prefetch_old_rows || min(tok0 + TS::T, pt1c) >= sv.n)) {
             ptx::pdl_wait();
             waited = true;
           }
@@ -454,7 +579,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int lo = max(tok0 + q * QR, pt0);
-            const int hi = min(tok0 + (q + 1) * QR, pt1);
+            const int hi = min(tok0 + (q + 1) * QR, pt1c);
             qa[q] = lo;
             qn[q] = hi > lo ? hi - lo : 0;
             bytes += (uint32_t)qn[q] * D * 4u * 2u;
@@ -570,6 +695,16 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
           l[h] = 0.f;
         }
       }
+      // Fused step: q arrived raw; the piece holding slot n-1 also builds
+      // the new k/v row.
+      const int new_tok = a.fused ? sv.n - 1 : -1;
+      if (a.fused) {
+        fused_rotate_q<D, GS>(a, q, l8);
+        if (pend == sv.gend) {
+          if (warp < 2) fused_new_row<D>(a, sv, warp, lane, new_k, new_v);
+          ptx::named_bar_sync(1, kConsumerWarps * 32);
+        }
+      }
 
       for (int blk = lb; blk < le; blk += TS::TB, ++it) {
         const int stage = it % STAGES;
@@ -588,17 +723,20 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
           const int tok_base = blk * kBlk + grp * QR + wi * R;
           // Only a piece's first and last tiles can hold rows outside
           // [pt0, pt1); the rest take the predicate-free path.
-          const bool full = blk * kBlk >= pt0 && blk * kBlk + TS::T <= pt1;
+          const bool full = blk * kBlk >= pt0 && blk * kBlk + TS::T <= pt1 &&
+                            !(new_tok >= blk * kBlk && new_tok < blk * kBlk + TS::T);
           if (full) {
 #pragma unroll
             for (int r0 = 0; r0 < R; r0 += RC)
               process_rows<D, GS, RC, true>(kq + (wi * R + r0) * D, vq + (wi * R + r0) * D,
-                                            tok_base + r0, pt0, pt1, a.scale, q, o, m, l);
+                                            tok_base + r0, pt0, pt1, a.scale, q, o, m, l,
+                                            new_tok, new_k + l8, new_v + l8);
           } else {
 #pragma unroll
             for (int r0 = 0; r0 < R; r0 += RC)
               process_rows<D, GS, RC, false>(kq + (wi * R + r0) * D, vq + (wi * R + r0) * D,
-                                             tok_base + r0, pt0, pt1, a.scale, q, o, m, l);
+                                             tok_base + r0, pt0, pt1, a.scale, q, o, m, l,
+                                             new_tok, new_k + l8, new_v + l8);
           }
         }
         __syncwarp();
