@@ -411,7 +411,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["molot", "reference"], default="molot")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--path", choices=["fused", "split"], default="split",
+    ap.add_argument("--path", choices=["fused", "split"], default="fused",
                     help="fused: molot_attn_step (one launch per layer); split: "
                          "molot_attn_append_rope + molot_attn_decode")
     ap.add_argument("--layers", type=int, default=0,

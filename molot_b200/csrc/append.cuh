@@ -54,6 +54,7 @@ constexpr int kAppendWarps = 4;
 __device__ __forceinline__ float warp_sumsq16(const float* x, int n, int lane) {
   const int a = lane & 15;
   float acc = 0.f;
+#pragma unroll 8
   for (int i = a; i + 16 - a <= n; i += 16) acc = __fmaf_rn(x[i], x[i], acc);
   acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 8));
   acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));

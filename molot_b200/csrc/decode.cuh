@@ -50,6 +50,9 @@ constexpr int kProducerRegs = 40;
 static_assert(2 * 128 * kConsumerRegs + 128 * kProducerRegs <= kDecodeThreads * 168,
               "register split exceeds the launch allocation");
 constexpr int kQuarterPadBytes = 32;
+// Fused step: raw v values (nkv*D) a CTA stages for the new-row build; above
+// this the build reads them from global memory.
+constexpr int kMaxStagedV = 8 * kConsumerWarps * 32;
 
 // Status codes written into the device status word.
 constexpr int kDevErrConsumerTimeout = 1;
@@ -137,9 +140,12 @@ struct DecodeSmem {
       4 * (kConsumerWarps * GS * D > 6 * kConsumerWarps * 32 ? kConsumerWarps * GS * D
                                                              : 6 * kConsumerWarps * 32);
   static constexpr int kMergeML = kConsumerWarps * GS * 2 * 4;
-  static constexpr int kNewRow = 2 * D * 4;  // fused mode: the new k and v rows
+  // fused mode: the new k and v rows, then the launch's constants (cos and
+  // sin of the RoPE angles [D/2] each, q_norm [D], k_norm [D])
+  static constexpr int kNewRow = 2 * D * 4 + 3 * D * 4;
   static constexpr int kBars = 2 * TS::STAGES * 8;
   static constexpr int kTotal = kStageBytes + kMergeO + kMergeML + kNewRow + kBars + 16;
+  static_assert(kTotal <= 227 * 1024, "decode CTA exceeds the shared-memory limit");
 };
 
 // Floats of one partial record: o[G][D], then m[G], l[G]; padded to a
@@ -296,6 +302,60 @@ __device__ __forceinline__ void process_rows(const float* kr, const float* vr, i
   }
 }
 
+// Fused step, launch constants: cos/sin of the RoPE angles pos*freq[i]
+// (tab[i], tab[D/2+i]) and the q_norm / k_norm weights (tab[D+i],
+// tab[2D+i]), staged in shared memory once per CTA by the 256 consumer
+// threads (the caller's named barrier publishes them).  When `raw` is
+// non-null the raw k row `kx` ([D]) and all nkv*D raw v values are staged
+// there too (raw[0..D), raw[D..D+nkv*D)), for the new-row build.  Every
+// global load is issued before the first dependent operation, so the whole
+// prologue costs one memory round trip.  forward.h:562-575 computes the same
+// values per row.
+template <int D>
+__device__ __forceinline__ void fused_fill_tables(const DecodeArgs& a, float* tab, int ctid,
+                                                  float* raw, const float* kx) {
+  constexpr int NT = kConsumerWarps * 32;
+  constexpr int IT = (D + NT - 1) / NT;
+  constexpr int kMaxV = kMaxStagedV / NT;
+  float f[IT], wq[IT], wk[IT], kr[IT], vv[kMaxV];
+  const int nv = a.nkv * D;
+#pragma unroll
+  for (int r = 0; r < IT; ++r) {
+    const int i = ctid + r * NT;
+    f[r] = (i < D / 2 && a.freq) ? ptx::ld_nc_issue(a.freq + i) : 0.f;
+    wq[r] = (i < D && a.q_norm) ? ptx::ld_nc_issue(a.q_norm + i) : 0.f;
+    wk[r] = (i < D && a.k_norm) ? ptx::ld_nc_issue(a.k_norm + i) : 0.f;
+    kr[r] = (i < D && raw) ? ptx::ld_nc_issue(kx + i) : 0.f;
+  }
+#pragma unroll
+  for (int r = 0; r < kMaxV; ++r) {
+    const int j = ctid + r * NT;
+    vv[r] = (raw && j < nv) ? ptx::ld_nc_issue(a.v_raw + j) : 0.f;
+  }
+#pragma unroll
+  for (int r = 0; r < IT; ++r) {
+    const int i = ctid + r * NT;
+    if (i < D / 2 && a.freq) {
+      float sn, cs;
+      sincosf(__fmul_rn((float)a.pos, f[r]), &sn, &cs);
+      tab[i] = cs;
+      tab[D / 2 + i] = sn;
+    }
+    if (i < D) {
+      tab[D + i] = wq[r];
+      tab[2 * D + i] = wk[r];
+      if (raw) raw[i] = kr[r];
+    }
+  }
+  if (raw) {
+#pragma unroll
+    for (int r = 0; r < kMaxV; ++r) {
+      const int j = ctid + r * NT;
+      if (j < nv) raw[D + j] = vv[r];
+    }
+  }
+}
+
 // Fused step, q side (forward.h:554-558): the warp's q registers hold the
 // raw projection in the row-group lane layout (dims {16m+l8, 16m+l8+8}).
 // Per-head weighted RMSNorm with the reference's sum-of-squares order (the
@@ -304,7 +364,7 @@ __device__ __forceinline__ void process_rows(const float* kr, const float* vr, i
 // The arithmetic is operation for operation that of norm_rope_append_kernel.
 template <int D, int GS>
 __device__ __forceinline__ void fused_rotate_q(const DecodeArgs& a, float (&q)[GS][D / 8],
-                                               int l8) {
+                                               int l8, const float* tab) {
   constexpr int DV = D / 16;
   constexpr int HV = DV / 2;
   if (a.q_norm) {
@@ -324,7 +384,7 @@ __device__ __forceinline__ void fused_rotate_q(const DecodeArgs& a, float (&q)[G
 #pragma unroll
       for (int i = 0; i < 2 * DV; ++i) {
         const int dim = 16 * (i >> 1) + l8 + 8 * (i & 1);
-        q[h][i] = __fmul_rn(__fmul_rn(q[h][i], inv), __ldg(a.q_norm + dim));
+        q[h][i] = __fmul_rn(__fmul_rn(q[h][i], inv), tab[D + dim]);
       }
     }
   }
@@ -332,8 +392,7 @@ __device__ __forceinline__ void fused_rotate_q(const DecodeArgs& a, float (&q)[G
 #pragma unroll
     for (int i = 0; i < 2 * HV; ++i) {
       const int dim = 16 * (i >> 1) + l8 + 8 * (i & 1);  // < D/2; partner dim + D/2
-      float s, c;
-      sincosf(__fmul_rn((float)a.pos, __ldg(a.freq + dim)), &s, &c);
+      const float c = tab[dim], s = tab[D / 2 + dim];
 #pragma unroll
       for (int h = 0; h < GS; ++h) {
         const float y0 = q[h][i], y1 = q[h][i + 2 * HV];
@@ -347,29 +406,32 @@ __device__ __forceinline__ void fused_rotate_q(const DecodeArgs& a, float (&q)[G
 // Fused step, k/v side (forward.h:562-575) for kv head sv.g: warp 0 builds
 // the normalised, rotated k row, warp 1 the normalised v row (plain RMSNorm
 // over all nkv*D values); both land in shared memory (for this launch) and
-// in slot n-1 of the cache (for later ones).
+// in slot n-1 of the cache (for later ones).  Weights and angles come from
+// the staged table.
 template <int D>
 __device__ __forceinline__ void fused_new_row(const DecodeArgs& a, const SegView& sv, int warp,
-                                              int lane, float* new_k, float* new_v) {
+                                              int lane, float* new_k, float* new_v,
+                                              const float* tab, const float* kx,
+                                              const float* vx) {
   constexpr int H = D / 2;
   const long long row = (long long)sv.b * a.kv_bstride + (long long)(sv.n - 1) * a.stride_t +
                         (long long)sv.g * a.stride_h;
   if (warp == 0) {
-    const float* x = a.k_raw + (long long)sv.g * D;
+    const float* x = kx;
     float inv = 1.f;
     if (a.k_norm) {
       const float ss = warp_sumsq16(x, D, lane);
       inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), a.eps)));
     }
+#pragma unroll
     for (int i = lane; i < H; i += 32) {
       float y0 = x[i], y1 = x[i + H];
       if (a.k_norm) {
-        y0 = __fmul_rn(__fmul_rn(y0, inv), a.k_norm[i]);
-        y1 = __fmul_rn(__fmul_rn(y1, inv), a.k_norm[i + H]);
+        y0 = __fmul_rn(__fmul_rn(y0, inv), tab[2 * D + i]);
+        y1 = __fmul_rn(__fmul_rn(y1, inv), tab[2 * D + i + H]);
       }
       if (a.freq) {
-        float s, c;
-        sincosf(__fmul_rn((float)a.pos, a.freq[i]), &s, &c);
+        const float c = tab[i], s = tab[H + i];
         const float z0 = __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, s));
         const float z1 = __fadd_rn(__fmul_rn(y0, s), __fmul_rn(y1, c));
         y0 = z0;
@@ -384,10 +446,11 @@ __device__ __forceinline__ void fused_new_row(const DecodeArgs& a, const SegView
     float vinv = 1.f;
     if (a.v_norm) {
       const int nv = a.nkv * D;
-      const float ss = warp_sumsq16(a.v_raw, nv, lane);
+      const float ss = warp_sumsq16(vx, nv, lane);
       vinv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)nv), a.eps)));
     }
-    const float* vh = a.v_raw + (long long)sv.g * D;
+    const float* vh = vx + (long long)sv.g * D;
+#pragma unroll
     for (int i = lane; i < D; i += 32) {
       const float val = a.v_norm ? __fmul_rn(vh[i], vinv) : vh[i];
       new_v[i] = val;
@@ -514,6 +577,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   float* merge_ml = reinterpret_cast<float*>(smem + SM::kStageBytes + SM::kMergeO);
   float* new_k = reinterpret_cast<float*>(smem + SM::kStageBytes + SM::kMergeO + SM::kMergeML);
   float* new_v = new_k + D;
+  float* tab = new_v + D;  // fused mode: cos, sin, q_norm, k_norm
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + SM::kStageBytes + SM::kMergeO +
                                                    SM::kMergeML + SM::kNewRow);
   uint64_t* empty_bar = full_bar + STAGES;
@@ -667,6 +731,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   float m[GS], l[GS];
 
   int it = 0;
+  bool tables_ready = false;
   long long pos = cbeg;
   int s = s_first;
   while (pos < cend) {
@@ -686,8 +751,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         for (int h = 0; h < GS; ++h) {
 #pragma unroll
           for (int mm = 0; mm < DV; ++mm) {
-            q[h][2 * mm] = __ldg(qb + h * D + 16 * mm);
-            q[h][2 * mm + 1] = __ldg(qb + h * D + 16 * mm + 8);
+            q[h][2 * mm] = ptx::ld_nc_issue(qb + h * D + 16 * mm);
+            q[h][2 * mm + 1] = ptx::ld_nc_issue(qb + h * D + 16 * mm + 8);
             o[h][2 * mm] = 0.f;
             o[h][2 * mm + 1] = 0.f;
           }
@@ -699,9 +764,25 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       // the new k/v row.
       const int new_tok = a.fused ? sv.n - 1 : -1;
       if (a.fused) {
-        fused_rotate_q<D, GS>(a, q, l8);
-        if (pend == sv.gend) {
-          if (warp < 2) fused_new_row<D>(a, sv, warp, lane, new_k, new_v);
+        const bool newrow = pend == sv.gend;
+        const float* kx = a.k_raw + (long long)sv.g * D;  // raw k row of head g
+        const float* vx = a.v_raw;                          // raw v, all heads
+        if (!tables_ready) {  // once per CTA; the q loads above are in flight
+          // merge_o is free until this piece's finalize: stage the raw rows
+          // there when this piece builds the new row.
+          const bool stage = newrow && a.nkv * D <= kMaxStagedV &&
+                             (D + a.nkv * D) * 4 <= SM::kMergeO;
+          fused_fill_tables<D>(a, tab, ctid, stage ? merge_o : nullptr, kx);
+          ptx::named_bar_sync(1, kConsumerWarps * 32);
+          tables_ready = true;
+          if (stage) {
+            kx = merge_o;
+            vx = merge_o + D;
+          }
+        }
+        fused_rotate_q<D, GS>(a, q, l8, tab);
+        if (newrow) {
+          if (warp < 2) fused_new_row<D>(a, sv, warp, lane, new_k, new_v, tab, kx, vx);
           ptx::named_bar_sync(1, kConsumerWarps * 32);
         }
       }

@@ -115,5 +115,15 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Read-only global load issued exactly where it stands: a volatile asm
+// statement is neither sunk towards its first use nor moved across the
+// barriers around it, so loads meant to overlap one another stay in flight
+// together.
+__device__ __forceinline__ float ld_nc_issue(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+
 }  // namespace ptx
 }  // namespace molot
