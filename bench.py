@@ -1,7 +1,7 @@
 """Benchmark: GQA decode attention, KV GB/s and tokens/s (BASELINE metric).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl molot|reference]
-                    [--config cfg2|cfg1|cfg3|cfg4|cfg5]
+                    [--config cfg2|cfg1|cfg3|cfg4|cfg5] [--path fused|split]
 
 Default workload ("cfg2"): one decode step of a 32-layer
 Llama-shaped model at 16k context -- Hq=32, Hkv=8, head_dim=128, 16384 cached
@@ -9,17 +9,33 @@ slots + the new token (n=16385), RoPE theta=5e5.  Per layer the step runs
 the library's public call molot_attn_step: QK-norm/RoPE of the raw q/k, the
 append of the new row and split-KV decode over the HBM-resident cache, in
 one launch (--path split: molot_attn_append_rope + molot_attn_decode, two
-launches).  K/V and
-q/k/v are seeded N(0,1) synthetic data generated on the device.  The 4.3 GB
-of KV is far larger than L2 (126 MB), so no flush is needed.
+launches).  K/V and q/k/v are seeded N(0,1) synthetic data generated on the
+device.  The 4.3 GB of KV is far larger than L2 (126 MB), so no flush is
+needed.  With N>1 every rank runs its own replica (one sequence per GPU,
+weak scaling, no collective on the data path).
 
-value  : unique KV bytes (2*Hkv*n*d*4 per layer, all layers, all ranks)
-         / max-over-ranks device time of the K timed steps, inputs resident.
+Other BASELINE configs (parity cases, also benchable):
+  cfg1  the same at ctx 4096 (bench.cc shape);
+  cfg3  Gemma-3-4B shape: 34 layers, Hq=8, Hkv=4, d=256, QK-norm + V-norm,
+        every 6th layer global (theta 1e6, full 32769 slots), the rest
+        sliding-window (1024 slots, theta 1e4), scale 1, one launch per layer;
+  cfg4  continuous batching, Llama-3-8B shape, 64 sequences with lengths
+        U[512, 32768] (seeded), 16-slot pages with a shuffled block table;
+        sequences split over the ranks by LPT on their lengths (strong
+        scaling, no collective), batched append + paged decode per layer;
+  cfg5  Llama-3-70B shape (80 layers, Hq=64, Hkv=8), 32 sequences with
+        lengths U[8192, 131072]; kv heads split over the ranks, each
+        layer's outputs all-gathered over NCCL on a second stream.
+  cfg4/cfg5 hold more KV than one GPU: --resident-gb of distinct layer pools
+  stay resident and the step cycles through them (each pool is far larger
+  than L2, so every layer still streams from HBM).
+
+value  : unique KV bytes read per step (2*Hkv*slots*d*4 per layer and
+         sequence, all ranks) / max-over-ranks device time of the K timed
+         steps, inputs resident.
 e2e    : the same metric through the same public API with the step's inputs
          (raw q/k/v of every layer) copied host->device from pinned memory
          and the attention outputs copied back, inside the timed region.
-With N>1 every rank runs its own replica (one sequence per GPU, weak
-scaling, no collective on the data path).
 
 --impl reference times the reference's own CPU implementation
 (attn_decode_gqa_cache from attn.h, compiled unchanged into
@@ -44,11 +60,19 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 CONFIGS = {
-    # name: (layers, nq, nkv, d, n_cached, rope_theta, window, scale)
-    "cfg1": dict(layers=32, nq=32, nkv=8, d=128, ctx=4096, theta=1e4, window=0,
+    "cfg1": dict(kind="single", layers=32, nq=32, nkv=8, d=128, ctx=4096, theta=1e4, window=0,
                  desc="single-sequence GQA decode, ctx 4096 (bench.cc shape)"),
-    "cfg2": dict(layers=32, nq=32, nkv=8, d=128, ctx=16384, theta=5e5, window=0,
+    "cfg2": dict(kind="single", layers=32, nq=32, nkv=8, d=128, ctx=16384, theta=5e5, window=0,
                  desc="single-sequence GQA decode, ctx 16384, 32-layer sweep"),
+    "cfg3": dict(kind="gemma", layers=34, nq=8, nkv=4, d=256, ctx=32768, swa_window=1024,
+                 swa_theta=1e4, global_theta=1e6, global_every=6, scale=1.0,
+                 desc="Gemma-3-4B shape, 5:1 SWA(1024)/global at ctx 32768, QK-norm + V-norm"),
+    "cfg4": dict(kind="paged_seq", layers=32, nq=32, nkv=8, d=128, batch=64, len_lo=512,
+                 len_hi=32768, page=16, theta=5e5, seed=4,
+                 desc="paged continuous batching, Llama-3-8B shape, B=64, n~U[512,32768]"),
+    "cfg5": dict(kind="paged_head", layers=80, nq=64, nkv=8, d=128, batch=32, len_lo=8192,
+                 len_hi=131072, page=16, theta=5e5, seed=5,
+                 desc="Llama-3-70B shape, B=32, n~U[8192,131072], kv-head sharded"),
 }
 METRIC = "GQA decode attn KV GB/s (% of HBM peak) and tok/s at ctx 16k, 1/2/4/8 GPU"
 
@@ -132,55 +156,144 @@ def dist_env():
     return world, rank, local
 
 
+# ------------------------------------------------------------------ workloads
+
+def paged_lengths(cfg):
+    """Cached context length of each sequence (seeded U[len_lo, len_hi])."""
+    rng = np.random.default_rng(cfg["seed"])
+    return [int(x) for x in rng.integers(cfg["len_lo"], cfg["len_hi"] + 1, size=cfg["batch"])]
+
+
+def gemma_layers(cfg):
+    """(window, rope theta) per layer: every global_every-th layer is global."""
+    k = cfg["global_every"]
+    return [(0, cfg["global_theta"]) if l % k == k - 1 else (cfg["swa_window"], cfg["swa_theta"])
+            for l in range(cfg["layers"])]
+
+
+def attended(n, window):
+    """Slots a decode at position n-1 attends (attn.h:137)."""
+    return min(n, window) if window > 0 else n
+
+
+def step_bytes(cfg):
+    """Unique KV bytes one decode step reads (all layers, all sequences)."""
+    kind, nkv, d = cfg["kind"], cfg["nkv"], cfg["d"]
+    if kind == "single":
+        return cfg["layers"] * 2 * nkv * (cfg["ctx"] + 1) * d * 4
+    if kind == "gemma":
+        n = cfg["ctx"] + 1
+        return sum(2 * nkv * attended(n, w) * d * 4 for w, _ in gemma_layers(cfg))
+    return cfg["layers"] * sum(2 * nkv * (x + 1) * d * 4 for x in paged_lengths(cfg))
+
+
+class RefWorkload:
+    """Representative calls of the reference's attn_decode_gqa_cache for a
+    config (the reference is single-sequence and unpaged: a paged config is
+    per-sequence calls on contiguous [n][nkv*d] caches, page gather excluded).
+    call(i) runs the i-th call; step_seconds() extrapolates one step of the
+    GPU arm's workload from the per-call means."""
+
+    def __init__(self, cfg, impl, cores):
+        import oracle
+        self.oracle, self.impl, self.cores, self.cfg = oracle, impl, cores, cfg
+        kind, nq, nkv, d = cfg["kind"], cfg["nq"], cfg["nkv"], cfg["d"]
+        if kind == "single":
+            n = cfg["ctx"] + 1
+            self.items = [(n, n - 1, 0)]
+        elif kind == "gemma":
+            n = cfg["ctx"] + 1
+            self.items = [(n, n - 1, 0), (n, n - 1, cfg["swa_window"])]
+        else:
+            lens = paged_lengths(cfg)
+            order = np.random.default_rng(cfg["seed"] + 100).permutation(len(lens))
+            self.items = [(lens[i] + 1, lens[i], 0) for i in order]
+        nmax = max(x[0] for x in self.items)
+        rng = np.random.default_rng(7)
+        nbuf = 2 if kind in ("single", "gemma") else 1  # distinct buffers >> CPU caches
+        self.Q = rng.standard_normal((nq, d), dtype=np.float32)
+        self.K = [rng.standard_normal((nmax, nkv * d), dtype=np.float32) for _ in range(nbuf)]
+        self.V = [rng.standard_normal((nmax, nkv * d), dtype=np.float32) for _ in range(nbuf)]
+        self.t = [0.0] * len(self.items)
+        self.c = [0] * len(self.items)
+        self.bytes = 0
+        self.seconds = 0.0
+
+    def call(self, i, record=True):
+        cfg = self.cfg
+        nq, nkv, d = cfg["nq"], cfg["nkv"], cfg["d"]
+        j = i % len(self.items)
+        n, pos, w = self.items[j]
+        buf = i % len(self.K)
+        K, V = self.K[buf][:n], self.V[buf][:n]
+        scale = 1.0 / math.sqrt(d)
+        t0 = time.perf_counter()
+        if self.impl == "reference":
+            self.oracle.attn_decode_gqa_cache(self.Q, K, V, nq, nkv, n, d, scale, pos, w,
+                                              impl="ref", nthreads=self.cores)
+        else:
+            self.oracle.attn_decode_gqa_cache(self.Q, K, V, nq, nkv, n, d, scale, pos, w)
+        dt = time.perf_counter() - t0
+        if record:
+            self.t[j] += dt
+            self.c[j] += 1
+            self.bytes += 2 * nkv * attended(n, w) * d * 4
+            self.seconds += dt
+        return dt
+
+    def step_seconds(self):
+        cfg = self.cfg
+        mean = [t / c if c else 0.0 for t, c in zip(self.t, self.c)]
+        if cfg["kind"] == "single":
+            return cfg["layers"] * mean[0]
+        if cfg["kind"] == "gemma":
+            ng = sum(1 for w, _ in gemma_layers(cfg) if w == 0)
+            return ng * mean[0] + (cfg["layers"] - ng) * mean[1]
+        return step_bytes(cfg) / (self.bytes / self.seconds)
+
+    def describe(self, what):
+        return (f"{sum(self.c)} calls of attn_decode_gqa_cache ({what}), "
+                f"{self.seconds:.1f}s; per-step time extrapolated from per-call means")
+
+
+def ref_kind_and_cores():
+    import oracle
+    if oracle.ref() is not None:
+        return "reference", os.cpu_count() or 1
+    return "port", 1
+
+
 # ------------------------------------------------------------------ reference arm
 
 def run_reference(args, cfg):
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
-    import oracle
-    lib = oracle.ref()
-    kind = "reference"
-    if lib is None:
-        kind = "port"
-    cores = os.cpu_count() or 1
-    nq, nkv, d, n = cfg["nq"], cfg["nkv"], cfg["d"], cfg["ctx"] + 1
-    scale = 1.0 / math.sqrt(d)
-    rng = np.random.default_rng(7)
-    nbuf = 2  # distinct layer buffers, each 134 MB >> any CPU cache
-    bufs = [(rng.standard_normal((nq, d), dtype=np.float32),
-             rng.standard_normal((n, nkv * d), dtype=np.float32),
-             rng.standard_normal((n, nkv * d), dtype=np.float32)) for _ in range(nbuf)]
-
-    def one(i):
-        Q, K, V = bufs[i % nbuf]
-        if kind == "reference":
-            oracle.attn_decode_gqa_cache(Q, K, V, nq, nkv, n, d, scale, n - 1, 0, impl="ref",
-                                         nthreads=cores)
-        else:
-            oracle.attn_decode_gqa_cache(Q, K, V, nq, nkv, n, d, scale, n - 1, 0)
-
-    layers_per_step = 2
+    kind, cores = ref_kind_and_cores()
+    wl = RefWorkload(cfg, kind, cores)
+    per_step = len(wl.items) if cfg["kind"] == "gemma" else 2
     for i in range(args.warmup):
-        one(i)
-    t0 = time.perf_counter()
-    for i in range(args.steps * layers_per_step):
-        one(i)
-    dt = (time.perf_counter() - t0) / (args.steps * layers_per_step)  # s per layer
-    kv_bytes = 2 * nkv * n * d * 4
-    value = kv_bytes / dt / 1e9
+        wl.call(i, record=False)
+    for i in range(args.steps * per_step):
+        wl.call(i)
+    sec = wl.step_seconds()
+    value = step_bytes(cfg) / sec / 1e9
+    batch = cfg.get("batch", 1)
+    what = {"single": f"one layer, n={cfg.get('ctx', 0) + 1}",
+            "gemma": "a global and a 1024-slot SWA layer, alternating",
+            }.get(cfg["kind"], "one sequence per call, lengths from the config's seeded draw")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dt * cfg["layers"] * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.config}: {cfg['desc']} (reference CPU, per-layer sample)",
-                   "layers": cfg["layers"], "nq": nq, "nkv": nkv, "head_dim": d, "n": n},
-        "tok_per_s": round(1.0 / (dt * cfg["layers"]), 3),
+        "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak" if cfg["kind"] in ("single", "gemma") else "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": f"{args.config}: {cfg['desc']} (reference CPU sample)",
+                   "layers": cfg["layers"], "nq": cfg["nq"], "nkv": cfg["nkv"],
+                   "head_dim": cfg["d"]},
+        "tok_per_s": round(batch / sec, 3),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": kind,
-                         "sample": f"{args.steps * layers_per_step} layer calls of "
-                                   f"attn_decode_gqa_cache (n={n}) over {nbuf} buffers; "
-                                   "per-step time = 32 x mean layer time"},
+                         "sample": wl.describe(what)},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -189,38 +302,23 @@ def run_reference(args, cfg):
 
 
 def cpu_baseline_sample(cfg):
-    """A bounded reference sample for the GPU arm's cpu_baseline key."""
-    import oracle
-    lib = oracle.ref()
-    kind = "reference" if lib is not None else "port"
-    cores = (os.cpu_count() or 1) if kind == "reference" else 1
-    nq, nkv, d, n = cfg["nq"], cfg["nkv"], cfg["d"], cfg["ctx"] + 1
-    rng = np.random.default_rng(11)
-    Q = rng.standard_normal((nq, d), dtype=np.float32)
-    K = rng.standard_normal((n, nkv * d), dtype=np.float32)
-    V = rng.standard_normal((n, nkv * d), dtype=np.float32)
-    scale = 1.0 / math.sqrt(d)
-    calls, t_total = 0, 0.0
+    """A bounded reference sample (~10 s) for the GPU arm's cpu_baseline key."""
+    kind, cores = ref_kind_and_cores()
+    wl = RefWorkload(cfg, kind, cores)
     budget = 10.0 if kind == "reference" else 6.0
-    while t_total < budget and calls < 400:
-        t0 = time.perf_counter()
-        if kind == "reference":
-            oracle.attn_decode_gqa_cache(Q, K, V, nq, nkv, n, d, scale, n - 1, 0, impl="ref",
-                                         nthreads=cores)
-        else:
-            oracle.attn_decode_gqa_cache(Q, K, V, nq, nkv, n, d, scale, n - 1, 0)
-        t_total += time.perf_counter() - t0
-        calls += 1
-    dt = t_total / calls
-    return {"value": round(2 * nkv * n * d * 4 / dt / 1e9, 3), "unit": "GB/s", "cores": cores,
-            "kind": kind,
-            "sample": f"{calls} calls of attn_decode_gqa_cache (one layer, n={n}, "
-                      f"{nq}/{nkv}/{d}) ~{t_total:.1f}s"}
+    wl.call(0, record=False)
+    i = 0
+    while wl.seconds < budget and i < 400:
+        wl.call(i)
+        i += 1
+    sec = wl.step_seconds()
+    return {"value": round(step_bytes(cfg) / sec / 1e9, 3), "unit": "GB/s", "cores": cores,
+            "kind": kind, "sample": wl.describe(f"{cfg['kind']} workload")}
 
 
 # ------------------------------------------------------------------ molot arm
 
-def run_molot(args, cfg):
+def run_single(args, cfg):
     import torch
     import torch.distributed as dist
 
@@ -403,6 +501,362 @@ def run_molot(args, cfg):
     return 0
 
 
+class Rt:
+    """Process group, device and device-timing helpers of the molot arm."""
+
+    def __init__(self):
+        import datetime
+        import torch
+        import torch.distributed as dist
+        self.torch, self.dist = torch, dist
+        self.world, self.rank, self.local = dist_env()
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        self.dev = torch.device("cuda", self.local)
+
+    def barrier(self):
+        self.torch.cuda.synchronize()
+        if self.world > 1:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def reduce(self, x, op):
+        if self.world == 1:
+            return x
+        t = self.torch.tensor([float(x)], dtype=self.torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=op)
+        return float(t.item())
+
+    def max(self, x):
+        return self.reduce(x, self.dist.ReduceOp.MAX)
+
+    def sum(self, x):
+        return self.reduce(x, self.dist.ReduceOp.SUM)
+
+    def timed(self, fn, iters):
+        """Mean ms per call of fn over `iters` calls, CUDA events on the
+        current stream, bracketed by barrier + synchronize."""
+        torch = self.torch
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        self.barrier()
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters
+
+    def close(self):
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def rope_freq(torch, theta, d, dev):
+    return torch.tensor([1.0 / theta ** (2.0 * i / d) for i in range(d // 2)],
+                        dtype=torch.float32, device=dev)
+
+
+def pinned_like(torch, t, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(t.shape, generator=g).pin_memory()
+
+
+def emit(rt, args, cfg, ms, e2e_ms, clk, h2d, d2h, launches, roof, config, scaling, extra=None):
+    """The bench JSON line (rank 0)."""
+    # weak scaling = replicas (every rank runs the whole step); strong = the
+    # step's sequences or kv heads are split over the ranks
+    total = step_bytes(cfg) * (rt.world if scaling == "weak" else 1)
+    peak, peak_kind = hbm_peak()
+    value = total / (ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": rt.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) K/V and q/k/v generated on device)",
+        "config": config,
+        "tok_per_s": round(cfg.get("batch", 1) * (rt.world if scaling == "weak" else 1)
+                           * 1000.0 / ms, 2),
+        "pct_hbm_peak": round(100.0 * value / rt.world / peak, 2),
+        "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": int(launches),
+        "roofline": dict(roof, peak=peak, unit="GB/s", frac=round(roof["achieved"] / peak, 4),
+                         peak_source=f"{peak_kind} hbm_gbs"),
+        "clocks": clk,
+    }
+    if extra:
+        line.update(extra)
+    if rt.world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample(cfg)
+    print(json.dumps(line), flush=True)
+
+
+def run_gemma(args, cfg):
+    """cfg3: one molot_attn_step launch per layer; SWA layers read 1024 slots."""
+    rt = Rt()
+    torch = rt.torch
+    import molot_b200 as mb
+
+    L, nq, nkv, d = cfg["layers"], cfg["nq"], cfg["nkv"], cfg["d"]
+    ctx, scale = cfg["ctx"], cfg["scale"]
+    n = ctx + 1
+    layers = gemma_layers(cfg)
+    cache = mb.KVCache(L, nkv, d, n)
+    gen = torch.Generator(device=rt.dev)
+    gen.manual_seed(1234 + rt.rank)
+    for l, (w, _) in enumerate(layers):
+        kt, vt = cache.layer_tensors(l)  # head-major [nkv][cap][hd]
+        lo = max(0, ctx - w + 1) if w else 0
+        kt[:, lo:ctx].normal_(generator=gen)
+        vt[:, lo:ctx].normal_(generator=gen)
+    q_raw = torch.randn((L, nq * d), device=rt.dev, generator=gen)
+    k_raw = torch.randn((L, nkv * d), device=rt.dev, generator=gen)
+    v_raw = torch.randn((L, nkv * d), device=rt.dev, generator=gen)
+    q_norm = (1 + 0.1 * torch.randn(d, device=rt.dev, generator=gen)).contiguous()
+    k_norm = (1 + 0.1 * torch.randn(d, device=rt.dev, generator=gen)).contiguous()
+    freq = {th: rope_freq(torch, th, d, rt.dev) for _, th in layers}
+    out = torch.empty((L, nq * d), device=rt.dev)
+    glob = [l for l, (w, _) in enumerate(layers) if w == 0]
+
+    def step(qr, kr, vr, o, only=None):
+        st = torch.cuda.current_stream()
+        for l in (range(L) if only is None else only):
+            w, th = layers[l]
+            cache.set_length(l, ctx)
+            cache.step(l, qr[l], kr[l], vr[l], o[l], scale, ctx, w, q_norm, k_norm, True, 1e-6,
+                       freq[th], nq, st)
+
+    for _ in range(args.warmup):
+        step(q_raw, k_raw, v_raw, out)
+    cache.check()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step(q_raw, k_raw, v_raw, out)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph, ggraph = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step(q_raw, k_raw, v_raw, out)
+    with torch.cuda.graph(ggraph):
+        step(q_raw, k_raw, v_raw, out, only=glob)
+    for _ in range(args.warmup):
+        graph.replay()
+    clocks = ClockSampler(rt.local)
+    clocks.start()
+    time.sleep(0.3)
+    ms = rt.max(rt.timed(graph.replay, args.steps))
+    clk = clocks.stop()
+    for _ in range(args.warmup):
+        ggraph.replay()
+    glob_ms = rt.timed(ggraph.replay, args.steps) / len(glob)
+    cache.check()
+
+    h = [pinned_like(torch, t, 5 + i) for i, t in enumerate((q_raw, k_raw, v_raw))]
+    h_o = torch.empty((L, nq * d)).pin_memory()
+    dq, dk, dv = (torch.empty_like(t) for t in (q_raw, k_raw, v_raw))
+    d_o = torch.empty_like(out)
+
+    def e2e_step():
+        dq.copy_(h[0], non_blocking=True)
+        dk.copy_(h[1], non_blocking=True)
+        dv.copy_(h[2], non_blocking=True)
+        step(dq, dk, dv, d_o)
+        h_o.copy_(d_o, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    e2e_ms = rt.max(rt.timed(e2e_step, args.steps))
+    cache.check()
+    del graph, ggraph
+    gbytes = 2 * nkv * n * d * 4
+    if rt.rank == 0:
+        emit(rt, args, cfg, ms, e2e_ms, clk,
+             h2d=4 * L * (nq + 2 * nkv) * d, d2h=4 * L * nq * d, launches=L * args.steps,
+             roof={"bound": "hbm", "achieved": round(gbytes / (glob_ms * 1e-3) / 1e9, 1),
+                   "traffic": read_traffic("gqa_decode_kernel", args.config),
+                   "kernel": "gqa_decode_kernel<256,2,1> (fused step, global layer)",
+                   "timed": "the 5 global-layer launches alone",
+                   "bytes_per_launch": gbytes, "avg_launch_ms": round(glob_ms, 5)},
+             config={"workload": f"{args.config}: {cfg['desc']}", "layers": L, "nq": nq,
+                     "nkv": nkv, "head_dim": d, "n": n, "global_layers": glob,
+                     "swa_window": cfg["swa_window"], "scale": scale,
+                     "parallelism": f"replicas x{rt.world} (one sequence per GPU)",
+                     "l2": "inputs larger than L2 (1.585 GB KV read per step)"},
+             scaling="weak",
+             extra={"path": "molot_attn_step per layer (QK-norm, V-norm, RoPE, append, "
+                            "decode in one launch)"})
+    cache.close()
+    rt.close()
+    return 0
+
+
+def fill_normal(torch, dst, template):
+    """Fill a device tensor with N(0,1) values by tiling a seeded template
+    (generating tens of GB of normals directly takes too long)."""
+    flat = dst.view(-1)
+    T = template.numel()
+    for off in range(0, flat.numel(), T):
+        k = min(T, flat.numel() - off)
+        flat[off:off + k].copy_(template[:k])
+
+
+def run_paged(args, cfg):
+    """cfg4 (sequences split over ranks) / cfg5 (kv heads split over ranks,
+    outputs all-gathered): batched append + paged decode per layer."""
+    rt = Rt()
+    torch = rt.torch
+    import molot_b200 as mb
+    from molot_b200 import shard
+
+    L, nq, nkv, d, ps = cfg["layers"], cfg["nq"], cfg["nkv"], cfg["d"], cfg["page"]
+    lens = paged_lengths(cfg)
+    B, G = len(lens), nq // nkv
+    if cfg["kind"] == "paged_seq":
+        mine = shard.lpt_partition(lens, rt.world)[rt.rank]
+        g0, g1 = 0, nkv
+        parallelism = f"sequence-sharded (LPT on lengths) over {rt.world} rank(s), no collective"
+    else:
+        mine = list(range(B))
+        g0, g1 = shard.head_shard(nkv, rt.world, rt.rank)
+        parallelism = (f"kv-head sharded over {rt.world} rank(s) ({nkv // rt.world} kv heads "
+                       "each); per-layer NCCL all-gather of O on a second stream")
+    gather = cfg["kind"] == "paged_head" and rt.world > 1
+    nkv_l, Bl = g1 - g0, len(mine)
+    nq_l = nkv_l * G
+    seq = [lens[i] + 1 for i in mine]  # slots including the new token's
+    pages = [math.ceil(x / ps) for x in seq]
+    P = sum(pages)
+    rng = np.random.default_rng(cfg["seed"] + 1000 + rt.rank)
+    perm = rng.permutation(P).astype(np.int32)
+    bt = np.zeros((Bl, max(pages)), np.int32)
+    k = 0
+    for b, m in enumerate(pages):
+        bt[b, :m] = perm[k:k + m]
+        k += m
+    bt_dev = torch.from_numpy(bt).to(rt.dev)
+    pool_bytes = 2 * P * nkv_l * ps * d * 4
+    L_res = max(1, min(L, int(args.resident_gb * 1e9 // pool_bytes)))
+    gen = torch.Generator(device=rt.dev)
+    gen.manual_seed(1234 + rt.rank)
+    template = torch.randn(1 << 26, device=rt.dev, generator=gen)
+    pools = []
+    for _ in range(L_res):
+        K = torch.empty((P, nkv_l, ps, d), device=rt.dev)
+        V = torch.empty((P, nkv_l, ps, d), device=rt.dev)
+        fill_normal(torch, K, template)
+        fill_normal(torch, V, template[7:])
+        pools.append((K, V))
+    del template
+    q_raw = torch.randn((L, Bl, nq_l, d), device=rt.dev, generator=gen)
+    k_raw = torch.randn((L, Bl, nkv_l, d), device=rt.dev, generator=gen)
+    v_raw = torch.randn((L, Bl, nkv_l, d), device=rt.dev, generator=gen)
+    q_rot = torch.empty_like(q_raw)
+    out = torch.empty_like(q_raw)
+    o_full = torch.empty((L, B, nq, d), device=rt.dev) if gather else None
+    freq = rope_freq(torch, cfg["theta"], d, rt.dev)
+    scale = 1.0 / math.sqrt(d)
+    plan = mb.PagedPlan()
+    plan.build(nq_l, nkv_l, d, seq, None, 0)
+    comm = torch.cuda.Stream() if gather else None
+
+    def step(qr, kr, vr, o, decode_only=False):
+        st = torch.cuda.current_stream()
+        for l in range(L):
+            K, V = pools[l % L_res]
+            if not decode_only:
+                plan.append(qr[l], kr[l], vr[l], q_rot[l], K, V, bt_dev, ps, None, None, False,
+                            1e-6, freq, st)
+            plan.decode(q_rot[l], o[l], K, V, bt_dev, ps, scale, st)
+            if gather and not decode_only:
+                ev = torch.cuda.Event()
+                ev.record(st)
+                with torch.cuda.stream(comm):
+                    comm.wait_event(ev)
+                    shard.gather_heads(o[l], out=o_full[l])
+        if gather and not decode_only:
+            st.wait_stream(comm)
+
+    for _ in range(args.warmup):
+        step(q_raw, k_raw, v_raw, out)
+    plan.check()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step(q_raw, k_raw, v_raw, out, decode_only=True)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    dgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(dgraph):
+        step(q_raw, k_raw, v_raw, out, decode_only=True)
+    graph = None
+    if not gather:  # NCCL stays out of graphs; the gathered step runs eagerly
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step(q_raw, k_raw, v_raw, out)
+        run = graph.replay
+    else:
+        def run():
+            step(q_raw, k_raw, v_raw, out)
+    for _ in range(args.warmup):
+        run()
+    clocks = ClockSampler(rt.local)
+    clocks.start()
+    time.sleep(0.3)
+    ms = rt.max(rt.timed(run, args.steps))
+    clk = clocks.stop()
+    for _ in range(args.warmup):
+        dgraph.replay()
+    dec_ms = rt.timed(dgraph.replay, args.steps) / L
+    plan.check()
+
+    h = [pinned_like(torch, t, 5 + i) for i, t in enumerate((q_raw, k_raw, v_raw))]
+    res = o_full if gather else out
+    h_o = torch.empty(res.shape).pin_memory()
+    dq, dk, dv = (torch.empty_like(t) for t in (q_raw, k_raw, v_raw))
+    d_o = torch.empty_like(out)
+
+    def e2e_step():
+        dq.copy_(h[0], non_blocking=True)
+        dk.copy_(h[1], non_blocking=True)
+        dv.copy_(h[2], non_blocking=True)
+        step(dq, dk, dv, d_o)
+        h_o.copy_(o_full if gather else d_o, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    e2e_ms = rt.max(rt.timed(e2e_step, args.steps))
+    plan.check()
+    del graph, dgraph
+    local_layer_bytes = sum(2 * nkv_l * x * d * 4 for x in seq)
+    h2d = rt.sum(4 * L * Bl * (nq_l + 2 * nkv_l) * d)
+    d2h = rt.sum(h_o.numel() * 4)
+    if rt.rank == 0:
+        emit(rt, args, cfg, ms, e2e_ms, clk, h2d=h2d, d2h=d2h,
+             launches=2 * L * args.steps,
+             roof={"bound": "hbm", "achieved": round(local_layer_bytes / (dec_ms * 1e-3) / 1e9, 1),
+                   "traffic": read_traffic("gqa_decode_kernel", args.config),
+                   "kernel": "gqa_decode_kernel<128,4,1> (paged plan)",
+                   "timed": "rank 0's paged decode launches alone",
+                   "bytes_per_launch": local_layer_bytes, "avg_launch_ms": round(dec_ms, 5)},
+             config={"workload": f"{args.config}: {cfg['desc']}", "layers": L, "nq": nq,
+                     "nkv": nkv, "head_dim": d, "batch": B, "batch_rank0": Bl,
+                     "len_min": min(lens), "len_mean": round(sum(lens) / B, 1),
+                     "len_max": max(lens), "page_size": ps,
+                     "resident_layer_pools": L_res, "parallelism": parallelism,
+                     "l2": f"each layer pool ({pool_bytes / 1e9:.2f} GB on rank 0) > L2"},
+             scaling="strong",
+             extra={"path": "molot_paged_append + molot_paged_decode per layer"
+                            + (" + NCCL all-gather" if gather else "")})
+    plan.close()
+    rt.close()
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -414,6 +868,8 @@ def main(argv=None):
     ap.add_argument("--path", choices=["fused", "split"], default="fused",
                     help="fused: molot_attn_step (one launch per layer); split: "
                          "molot_attn_append_rope + molot_attn_decode")
+    ap.add_argument("--resident-gb", type=float, default=40.0,
+                    help="cfg4/cfg5: device memory for distinct layer pools per rank")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (small cases for profiler captures)")
     args = ap.parse_args(argv)
@@ -424,7 +880,11 @@ def main(argv=None):
         cfg["layers"] = args.layers
     if args.impl == "reference":
         return run_reference(args, cfg)
-    return run_molot(args, cfg)
+    if cfg["kind"] == "single":
+        return run_single(args, cfg)
+    if cfg["kind"] == "gemma":
+        return run_gemma(args, cfg)
+    return run_paged(args, cfg)
 
 
 if __name__ == "__main__":

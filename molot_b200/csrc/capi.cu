@@ -288,6 +288,7 @@ int decode_uniform(Workspace& ws, const float* Q, float* O, const float* K, cons
   if ((rc = prepare_kernel(k, dev))) return rc;
   DecodeArgs a = {};
   a.grid = grid;
+  a.aligned = grid >= nkv ? 1 : 0;  // one segment per CTA (see DecodeArgs)
   a.prefetch_old_rows = prefetch_old_rows ? 1 : 0;
   if (fused) {  // per-token prologue fused into this launch (slot n-1 is new)
     a.fused = 1;

@@ -88,6 +88,13 @@ struct DecodeArgs {
   long long NB;
   int nblk_u, blo_u;  // uniform: blocks per segment and first block index
   int grid;  // CTAs of the decode grid (the partition is computed from it)
+  // Segment-aligned partition (uniform mode, grid >= S): every CTA works
+  // inside one segment -- the first grid%S segments get grid/S+1 CTAs, the
+  // rest grid/S -- and splits that segment's blocks evenly with its
+  // neighbours.  No CTA then finalises a piece half-way through its range
+  // (which stalls its stream and made segment-straddling CTAs the slowest).
+  // Otherwise the blocks of all segments are split evenly (stream-K).
+  int aligned;
   // Programmatic dependent launch.  When set, the producer may stream each
   // segment's slots below its newest one (n-1) before the preceding launch
   // has completed: they were written two or more launches earlier (the
@@ -154,9 +161,34 @@ __host__ __device__ constexpr int partial_record_floats(int G, int D) {
   return (G * D + 2 * G + 3) & ~3;
 }
 
-__device__ __forceinline__ long long cta_of_block(long long x, long long NB, int grid) {
-  // Largest c with floor(c*NB/grid) <= x.
-  return ((x + 1) * grid + NB - 1) / NB - 1;
+// Aligned partition: first CTA of segment s and the number of its CTAs.
+__device__ __forceinline__ int aligned_first_cta(const DecodeArgs& a, int s) {
+  const int q = a.grid / a.S, r = a.grid % a.S;
+  return s * q + min(s, r);
+}
+__device__ __forceinline__ int aligned_seg_of_cta(const DecodeArgs& a, int c) {
+  const int q = a.grid / a.S, r = a.grid % a.S;
+  return c < r * (q + 1) ? c / (q + 1) : r + (c - r * (q + 1)) / q;
+}
+
+// First block (global index) of CTA c's range; c == grid gives NB.
+__device__ __forceinline__ long long range_begin(const DecodeArgs& a, int c) {
+  if (!a.aligned) return (long long)c * a.NB / a.grid;
+  if (c >= a.grid) return a.NB;
+  const int s = aligned_seg_of_cta(a, c);
+  const int c0 = aligned_first_cta(a, s);
+  const int cs = aligned_first_cta(a, s + 1) - c0;
+  return (long long)s * a.nblk_u + (long long)a.nblk_u * (c - c0) / cs;
+}
+
+// CTA whose range holds block x: the largest c with range_begin(c) <= x.
+__device__ __forceinline__ long long cta_of_block(const DecodeArgs& a, long long x) {
+  if (!a.aligned) return ((x + 1) * a.grid + a.NB - 1) / a.NB - 1;
+  const int s = (int)(x / a.nblk_u);
+  const long long local = x - (long long)s * a.nblk_u;
+  const int c0 = aligned_first_cta(a, s);
+  const int cs = aligned_first_cta(a, s + 1) - c0;
+  return c0 + ((local + 1) * cs + a.nblk_u - 1) / a.nblk_u - 1;
 }
 
 struct SegView {
@@ -185,7 +217,7 @@ __device__ __forceinline__ SegView seg_view(const DecodeArgs& a, int s) {
 }
 
 __device__ __forceinline__ int first_seg_of_cta(const DecodeArgs& a, int c) {
-  if (a.uniform) return (int)(((long long)c * a.NB / a.grid) / a.nblk_u);
+  if (a.uniform) return (int)(range_begin(a, c) / a.nblk_u);
   return __ldg(a.cta_seg + c);
 }
 
@@ -475,7 +507,7 @@ __device__ __forceinline__ void combine_segment(const DecodeArgs& a, int s, cons
   const int G = a.G;
   const int psz = partial_record_floats(G, D);
   const int nc = (int)(cl - cf + 1);
-  const int slot_first = 2 * (int)cf + (((long long)cf * a.NB / a.grid) >= sv.gbeg ? 0 : 1);
+  const int slot_first = 2 * (int)cf + (range_begin(a, (int)cf) >= sv.gbeg ? 0 : 1);
   const int nchunk = G * D / 4;
   const int csplit = max(1, (kConsumerWarps * 32) / nchunk);
   for (int task = ctid; task < nchunk * csplit; task += kConsumerWarps * 32) {
@@ -502,18 +534,27 @@ __device__ __forceinline__ void combine_segment(const DecodeArgs& a, int s, cons
           oc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
+      // Batch maximum first, so the batch's weights are independent
+      // exponentials rather than a chain of rescales.
+      float Mn = M;
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) Mn = fmaxf(Mn, mc[u]);
+      const float fa = (M == -CUDART_INF_F) ? 0.f : ex2(M - Mn);
+      L *= fa;
+      acc.x *= fa;
+      acc.y *= fa;
+      acc.z *= fa;
+      acc.w *= fa;
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
-        const float Mn = fmaxf(M, mc[u]);
-        const float fa = (M == -CUDART_INF_F) ? 0.f : ex2(M - Mn);
         const float fb = (mc[u] == -CUDART_INF_F) ? 0.f : ex2(mc[u] - Mn);
-        L = L * fa + lc[u] * fb;
-        acc.x = acc.x * fa + oc[u].x * fb;
-        acc.y = acc.y * fa + oc[u].y * fb;
-        acc.z = acc.z * fa + oc[u].z * fb;
-        acc.w = acc.w * fa + oc[u].w * fb;
-        M = Mn;
+        L = __fmaf_rn(lc[u], fb, L);
+        acc.x = __fmaf_rn(oc[u].x, fb, acc.x);
+        acc.y = __fmaf_rn(oc[u].y, fb, acc.y);
+        acc.z = __fmaf_rn(oc[u].z, fb, acc.z);
+        acc.w = __fmaf_rn(oc[u].w, fb, acc.w);
       }
+      M = Mn;
     }
     if (csplit == 1) {
       float* dst = out_seg + chunk * 4;
@@ -564,7 +605,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   constexpr int STAGES = TS::STAGES;
   constexpr int WPS = kConsumerWarps / HS;  // warps per head set
   constexpr int R = QR / WPS;               // rows per warp per quarter per tile
-  constexpr int RC = R < 4 ? R : 4;         // rows per online-softmax update
+  // rows per online-softmax update (2 at D = 256, where registers are tightest)
+  constexpr int RC = D > 128 ? (R < 2 ? R : 2) : (R < 4 ? R : 4);
   constexpr int DV = D / 16;
   static_assert(kConsumerWarps % HS == 0, "head sets must divide the consumer warps");
   static_assert(QR % WPS == 0 && R >= 1, "rows per quarter must divide among warps");
@@ -583,6 +625,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   uint64_t* empty_bar = full_bar + STAGES;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty_bar + STAGES);
   volatile int* ticket_sm = abort_flag + 1;
+  volatile int* seg_cta_sm = abort_flag + 2;  // [2]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -597,9 +640,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   }
   __syncthreads();
 
-  const int grid = a.grid;
-  const long long cbeg = (long long)blockIdx.x * a.NB / grid;
-  const long long cend = (long long)(blockIdx.x + 1) * a.NB / grid;
+  const long long cbeg = range_begin(a, blockIdx.x);
+  const long long cend = range_begin(a, blockIdx.x + 1);
   const int s_first = first_seg_of_cta(a, blockIdx.x);
 
   if (warp >= kConsumerWarps) {
@@ -743,6 +785,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       const int pt0 = max(sv.t0, lb * kBlk);
       const int pt1 = min(sv.n, le * kBlk);
       const bool whole = (pos == sv.gbeg) && (pend == sv.gend);
+      // CTAs sharing this segment, for the merge after the piece: computed
+      // here, off the critical path at the piece's end, and parked in shared
+      // memory (read after the finalize barriers) rather than in registers.
+      if (!whole && ctid == 0) {
+        seg_cta_sm[0] = (int)cta_of_block(a, sv.gbeg);
+        seg_cta_sm[1] = (int)cta_of_block(a, sv.gend - 1);
+      }
       const int head0 = sv.g * a.G + set * GS;  // first query head of this warp's set
 
       {
@@ -825,32 +874,50 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       }
 
       // ---- finalize the piece: merge 4 row groups, then warps, then CTAs.
-#pragma unroll
-      for (int off = 8; off <= 16; off <<= 1) {
+      // Row groups merge by reduce-scatter: the xor-16 round leaves each
+      // lane half of its 2*DV values (the half its group bit 1 selects), the
+      // xor-8 round a quarter, so group grp ends owning o-values
+      // [grp*DV/2, (grp+1)*DV/2) of its lane's set; m and l are all-reduced.
+      {
+        const int bit1 = (lane >> 4) & 1, bit0 = (lane >> 3) & 1;
 #pragma unroll
         for (int h = 0; h < GS; ++h) {
-          const float mo = __shfl_xor_sync(0xffffffffu, m[h], off);
-          const float lo = __shfl_xor_sync(0xffffffffu, l[h], off);
-          const float M = fmaxf(m[h], mo);
-          const float fs = (m[h] == -CUDART_INF_F) ? 0.f : ex2(m[h] - M);
-          const float fo = (mo == -CUDART_INF_F) ? 0.f : ex2(mo - M);
+          // round 1 (xor 16): keep slot j of [0, DV) <- value j + bit1*DV
+          float mo = __shfl_xor_sync(0xffffffffu, m[h], 16);
+          float lo = __shfl_xor_sync(0xffffffffu, l[h], 16);
+          float M = fmaxf(m[h], mo);
+          float fs = (m[h] == -CUDART_INF_F) ? 0.f : ex2(m[h] - M);
+          float fo = (mo == -CUDART_INF_F) ? 0.f : ex2(mo - M);
           l[h] = l[h] * fs + lo * fo;
 #pragma unroll
-          for (int i = 0; i < 2 * DV; ++i) {
-            const float ov = __shfl_xor_sync(0xffffffffu, o[h][i], off);
-            o[h][i] = o[h][i] * fs + ov * fo;
+          for (int j = 0; j < DV; ++j) {
+            const float keep = bit1 ? o[h][DV + j] : o[h][j];
+            const float send = bit1 ? o[h][j] : o[h][DV + j];
+            const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+            o[h][j] = keep * fs + recv * fo;
           }
           m[h] = M;
-        }
-      }
-      if (lane < 8) {
+          // round 2 (xor 8): keep slot j of [0, DV/2) <- slot j + bit0*DV/2
+          mo = __shfl_xor_sync(0xffffffffu, m[h], 8);
+          lo = __shfl_xor_sync(0xffffffffu, l[h], 8);
+          M = fmaxf(m[h], mo);
+          fs = (m[h] == -CUDART_INF_F) ? 0.f : ex2(m[h] - M);
+          fo = (mo == -CUDART_INF_F) ? 0.f : ex2(mo - M);
+          l[h] = l[h] * fs + lo * fo;
 #pragma unroll
-        for (int h = 0; h < GS; ++h) {
+          for (int j = 0; j < DV / 2; ++j) {
+            const float keep = bit0 ? o[h][DV / 2 + j] : o[h][j];
+            const float send = bit0 ? o[h][j] : o[h][DV / 2 + j];
+            const float recv = __shfl_xor_sync(0xffffffffu, send, 8);
+            o[h][j] = keep * fs + recv * fo;
+          }
+          m[h] = M;
+          // slot j now holds o-value i = grp*DV/2 + j: dim 16*(i/2) + l8 + 8*(i&1)
           float* dst = merge_o + ((size_t)warp * GS + h) * D + l8;
 #pragma unroll
-          for (int mm = 0; mm < DV; ++mm) {
-            dst[16 * mm] = o[h][2 * mm];
-            dst[16 * mm + 8] = o[h][2 * mm + 1];
+          for (int j = 0; j < DV / 2; ++j) {
+            const int i = (bit1 * 2 + bit0) * (DV / 2) + j;
+            dst[16 * (i >> 1) + 8 * (i & 1)] = o[h][j];
           }
           if (lane == 0) {
             merge_ml[(warp * GS + h) * 2] = m[h];
@@ -898,8 +965,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       if (!whole) {
         // One thread publishes the CTA's partial and takes a ticket; the CTA
         // that draws the last ticket of the segment merges all partials.
-        const long long cf = cta_of_block(sv.gbeg, a.NB, grid);
-        const long long cl = cta_of_block(sv.gend - 1, a.NB, grid);
+        const long long cf = seg_cta_sm[0];
+        const long long cl = seg_cta_sm[1];
         if (ctid == 0) *ticket_sm = ptx::atom_add_acq_rel_gpu(a.counters + s, 1);
         ptx::named_bar_sync(1, kConsumerWarps * 32);
         if (*ticket_sm == (int)(cl - cf)) {
