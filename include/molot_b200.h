@@ -117,7 +117,9 @@ int molot_attn_decode_strided_noalloc(const float* Q, const float* K, const floa
  * and k (nkv heads) get per-head weighted RMSNorm when q_norm / k_norm are
  * non-null, then NEOX RoPE at `pos` when freq ([d/2]) is non-null; v gets a
  * plain RMSNorm over all nkv*d values when v_norm != 0.  The rotated q goes
- * to q_out; k and v are written to slot `slot` of kc / vc. */
+ * to q_out; k and v are written to slot `slot` of kc / vc.  With k, v, kc and
+ * vc all NULL only q is processed (a shared-KV layer's query, forward.h:554-558,
+ * before molot_attn_decode on its source layer). */
 int molot_norm_rope_append_dev(const float* q, const float* k, const float* v, float* q_out,
                                const float* q_norm, const float* k_norm, int v_norm, float eps,
                                const float* freq, int pos, float* kc, float* vc, int slot,

@@ -64,6 +64,15 @@ inline void attn_decode_gqa_win(const float* Q, const float* K, const float* V, 
   check(molot_attn_decode_gqa_win(Q, K, V, O, nq, nkv, n, d, scale, pos_cur, window));
 }
 
+// forward.h:554-558 for a shared-KV layer's query only: per-head RMSNorm
+// (q_norm may be null) and NEOX RoPE (freq may be null: NoPE), device
+// buffers, stream-ordered.
+inline void norm_rope_q_dev(const float* q, float* q_out, const float* q_norm, float eps,
+                            const float* freq, int pos, int nq, int d, void* stream = nullptr) {
+  check(molot_norm_rope_append_dev(q, nullptr, nullptr, q_out, q_norm, nullptr, 0, eps, freq, pos,
+                                   nullptr, nullptr, 0, nq, 1, d, stream));
+}
+
 // HBM-resident replacement for Runner::KVC: one handle for all layers.
 // Device pointers in, device pointers out; stream-ordered (stream = a
 // cudaStream_t, nullptr = legacy default stream).
@@ -96,6 +105,14 @@ class KVCache {
                                  freq, pos, nq, stream));
   }
   // forward.h:578-590: attention over the cache of src_layer.
+  // forward.h:554-590 for a KV-owning layer in one launch: QK-norm / V-norm /
+  // RoPE of the raw q, k, v, append at slot n, attention into o.
+  void step(int layer, const float* q, const float* k, const float* v, const float* q_norm,
+            const float* k_norm, bool v_norm, float eps, const float* freq, int pos, float* o,
+            int nq, float scale, int window, void* stream = nullptr) {
+    check(molot_attn_step(h_, layer, q, k, v, q_norm, k_norm, v_norm ? 1 : 0, eps, freq, pos, o,
+                          nq, scale, window, stream));
+  }
   void decode(int src_layer, const float* q, float* o, int nq, float scale, int pos_cur,
               int window, void* stream = nullptr) {
     check(molot_attn_decode(h_, src_layer, q, o, nq, scale, pos_cur, window, stream));

@@ -592,7 +592,10 @@ int append_strided(const float* q, const float* k, const float* v, float* q_out,
                    const float* q_norm, const float* k_norm, int v_norm, float eps,
                    const float* freq, int pos, float* kc, float* vc, int slot, int nq, int nkv,
                    int d, long long stride_t, long long stride_h, cudaStream_t st) {
-  if (!q || !k || !v || !q_out || !kc || !vc) return fail(MOLOT_ERR_INVALID, "null pointer");
+  // k, v, kc and vc all null: q only (a shared-KV layer's query, forward.h:554-558)
+  const bool q_only = !k && !v && !kc && !vc;
+  if (!q || !q_out || (!q_only && (!k || !v || !kc || !vc)))
+    return fail(MOLOT_ERR_INVALID, "null pointer");
   if (nq <= 0 || nkv <= 0 || slot < 0) return fail(MOLOT_ERR_INVALID, "bad sizes");
   AppendArgs a = {};
   a.q_in = q;
@@ -605,7 +608,7 @@ int append_strided(const float* q, const float* k, const float* v, float* q_out,
   a.eps = eps;
   a.freq = freq;
   a.nq = nq;
-  a.nkv = nkv;
+  a.nkv = q_only ? 0 : nkv;  // the kernel runs one warp per q and k head
   a.pos = pos;
   a.slot = slot;
   a.K = kc;

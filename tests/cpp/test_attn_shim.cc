@@ -120,8 +120,12 @@ int main() {
       cudaMemcpy(dq, q.data(), q.size() * 4, cudaMemcpyHostToDevice);
       cudaMemcpy(dk, k.data(), k.size() * 4, cudaMemcpyHostToDevice);
       cudaMemcpy(dv, v.data(), v.size() * 4, cudaMemcpyHostToDevice);
-      cache.append_rope(0, dq, dk, dv, dqr, dqn, dkn, true, 1e-6f, dfreq, pos, nq);
-      cache.decode(0, dqr, dout, nq, 1.0f, pos, window);
+      if (step % 2 == 0) {  // two launches
+        cache.append_rope(0, dq, dk, dv, dqr, dqn, dkn, true, 1e-6f, dfreq, pos, nq);
+        cache.decode(0, dqr, dout, nq, 1.0f, pos, window);
+      } else {  // one launch
+        cache.step(0, dq, dk, dv, dqn, dkn, true, 1e-6f, dfreq, pos, dout, nq, 1.0f, window);
+      }
       cache.sync();
       cudaMemcpy(out.data(), dout, out.size() * 4, cudaMemcpyDeviceToHost);
       int st = oracle_attn_layer_step(q.data(), k.data(), v.data(), qn.data(), kn.data(), 1, 1e-6f,
@@ -132,7 +136,28 @@ int main() {
     }
     CHECK(cache.n(0) == n0 + 5, "cache length %d", cache.n(0));
     CHECK(worst <= 1e-5, "KVCache layer step rel err %g", worst);
-    std::printf("[ok] KVCache append_rope+decode x5 rel_err=%.2e\n", worst);
+    std::printf("[ok] KVCache append_rope+decode / step x5 rel_err=%.2e\n", worst);
+    // a shared-KV layer (model.h:565-583): its own q, normalised and rotated
+    // alone, attends to layer 0's cache
+    {
+      const int pos = n0 + 5;
+      std::vector<float> q(nq * hd), out(nq * hd), ref(nq * hd), qr(nq * hd);
+      for (auto& x : q) x = frand();
+      cudaMemcpy(dq, q.data(), q.size() * 4, cudaMemcpyHostToDevice);
+      molot_b200::norm_rope_q_dev(dq, dqr, dqn, 1e-6f, dfreq, pos, nq, hd);
+      cache.decode(0, dqr, dout, nq, 1.0f, pos, window);
+      cache.sync();
+      cudaMemcpy(out.data(), dout, out.size() * 4, cudaMemcpyDeviceToHost);
+      for (int h = 0; h < nq; ++h) {
+        oracle_rmsnorm(q.data() + h * hd, qn.data(), qr.data() + h * hd, hd, 1e-6f);
+        oracle_rope_apply(qr.data() + h * hd, hd, pos, freq.data());
+      }
+      oracle_attn_decode_gqa_cache(qr.data(), kc.data(), vc.data(), ref.data(), nq, nkv, n_host,
+                                   hd, 1.0f, pos, window);
+      const double e = rel_err(out, ref);
+      CHECK(e <= 1e-5, "shared-KV reader rel err %g", e);
+      std::printf("[ok] norm_rope_q_dev + shared-KV decode rel_err=%.2e\n", e);
+    }
     // forward.h:580: a shared-KV layer reading an empty cache throws
     bool threw = false;
     try {

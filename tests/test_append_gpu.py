@@ -152,3 +152,24 @@ def test_cache_full_and_empty_errors(mb, torch_cuda):
         kv.check()
     finally:
         kv.close()
+
+
+def test_q_only_rotation(mb, torch_cuda, orc):
+    """molot_norm_rope_append_dev with k, v and the cache NULL: a shared-KV
+    layer's query (forward.h:554-558) alone."""
+    torch = torch_cuda
+    nq, d, pos = 8, 256, 4321
+    rng = np.random.default_rng(5)
+    q = rng.standard_normal(nq * d).astype(np.float32)
+    qn = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    freq = orc.rope_inv_freq(1e6, d)
+    q_out = torch.empty(nq * d, device="cuda")
+    mb.norm_rope_append(cu(torch, q), None, None, q_out, cu(torch, qn), None, False, 1e-6,
+                        cu(torch, freq), pos, None, None, 0, nq, 1, d)
+    torch.cuda.synchronize()
+    want = np.concatenate([orc.rope_apply(orc.rmsnorm(q[h * d:(h + 1) * d], qn, 1e-6), d, pos, freq)
+                           for h in range(nq)])
+    assert orc.rel_err(q_out.cpu().numpy(), want) < 1e-6
+    with pytest.raises(mb.MolotError):  # k given without its cache
+        mb.norm_rope_append(cu(torch, q), cu(torch, q[:d]), None, q_out, None, None, False, 1e-6,
+                            None, pos, None, None, 0, nq, 1, d)
