@@ -113,6 +113,20 @@ int molot_attn_decode_strided_noalloc(const float* Q, const float* K, const floa
                                       long long stride_h, float scale, int pos_cur, int window,
                                       void* stream);
 
+/* Replaces molot::attn_prefill_gqa (gemm.h:409-446) on host buffers: Qm, Om
+ * [M][nq][d], K/V [N][nkv*d] (attn.h:122-124 layout); query m sits at
+ * position pos0+m and attends slots [max(0, pos-window+1), min(pos+1, N)).
+ * nq/nkv must divide 64; d 64, 128 or 256. */
+int molot_attn_prefill_gqa(const float* Qm, const float* K, const float* V, float* Om, int nq,
+                           int nkv, int M, int N, int d, float scale, int pos0, int window);
+
+/* molot_attn_prefill_gqa on device buffers with any cache strides (slot t of
+ * kv head g at K + t*stride_t + g*stride_h), stream-ordered. */
+int molot_attn_prefill_strided_dev(const float* Q, const float* K, const float* V, float* O,
+                                   int nq, int nkv, int M, int N, int d, long long stride_t,
+                                   long long stride_h, float scale, int pos0, int window,
+                                   void* stream);
+
 /* forward.h:554-575 on device buffers for a [cap][nkv*d] cache: q (nq heads)
  * and k (nkv heads) get per-head weighted RMSNorm when q_norm / k_norm are
  * non-null, then NEOX RoPE at `pos` when freq ([d/2]) is non-null; v gets a
@@ -173,6 +187,23 @@ int molot_attn_step(molot_kv_cache* kv, int layer, const float* q, const float* 
                     const float* v, const float* q_norm, const float* k_norm, int v_norm,
                     float eps, const float* freq, int pos, float* o, int nq, float scale,
                     int window, void* stream);
+
+/* forward.h:368-392 (prefill prologue) for M tokens of a KV-owning layer:
+ * q [M][nq][hd], k, v [M][nkv][hd] raw projections of tokens at positions
+ * pos0..pos0+M-1 get the QK-norm / V-norm / RoPE of molot_attn_append_rope;
+ * rotated q goes to q_out [M][nq][hd], k/v rows to slots n..n+M-1, n += M.
+ * MOLOT_ERR_CACHE_FULL when n + M > cap (forward.h:385).  M <= 65535. */
+int molot_attn_append_rope_tokens(molot_kv_cache* kv, int layer, const float* q, const float* k,
+                                  const float* v, float* q_out, const float* q_norm,
+                                  const float* k_norm, int v_norm, float eps, const float* freq,
+                                  int pos0, int M, int nq, void* stream);
+
+/* Replaces molot::attn_prefill_gqa at forward.h:396 (gemm.h:409-446):
+ * causal / sliding-window attention of M rotated queries q [M][nq][hd]
+ * (query m at position pos0+m) over the cache of `src_layer` with its
+ * current length N; o [M][nq][hd].  nq/nkv must divide 64. */
+int molot_attn_prefill(molot_kv_cache* kv, int src_layer, const float* q, float* o, int nq, int M,
+                       float scale, int pos0, int window, void* stream);
 
 /* Synchronises the handle's stream work and reports device-side timeouts. */
 int molot_kv_check(molot_kv_cache* kv, void* stream);

@@ -64,6 +64,12 @@ inline void attn_decode_gqa_win(const float* Q, const float* K, const float* V, 
   check(molot_attn_decode_gqa_win(Q, K, V, O, nq, nkv, n, d, scale, pos_cur, window));
 }
 
+// gemm.h:409-446 (causal prefill attention), host buffers, ready on return
+inline void attn_prefill_gqa(const float* Qm, const float* K, const float* V, float* Om, int nq,
+                             int nkv, int M, int N, int d, float scale, int pos0, int window) {
+  check(molot_attn_prefill_gqa(Qm, K, V, Om, nq, nkv, M, N, d, scale, pos0, window));
+}
+
 // forward.h:554-558 for a shared-KV layer's query only: per-head RMSNorm
 // (q_norm may be null) and NEOX RoPE (freq may be null: NoPE), device
 // buffers, stream-ordered.
@@ -112,6 +118,19 @@ class KVCache {
             int nq, float scale, int window, void* stream = nullptr) {
     check(molot_attn_step(h_, layer, q, k, v, q_norm, k_norm, v_norm ? 1 : 0, eps, freq, pos, o,
                           nq, scale, window, stream));
+  }
+  // forward.h:368-392: prologue of M tokens, rows appended at n..n+M-1
+  void append_rope_tokens(int layer, const float* q, const float* k, const float* v,
+                          float* q_out, const float* q_norm, const float* k_norm, bool v_norm,
+                          float eps, const float* freq, int pos0, int M, int nq,
+                          void* stream = nullptr) {
+    check(molot_attn_append_rope_tokens(h_, layer, q, k, v, q_out, q_norm, k_norm, v_norm ? 1 : 0,
+                                        eps, freq, pos0, M, nq, stream));
+  }
+  // forward.h:394-398: prefill attention over src_layer's cache
+  void prefill(int src_layer, const float* q, float* o, int nq, int M, float scale, int pos0,
+               int window, void* stream = nullptr) {
+    check(molot_attn_prefill(h_, src_layer, q, o, nq, M, scale, pos0, window, stream));
   }
   void decode(int src_layer, const float* q, float* o, int nq, float scale, int pos_cur,
               int window, void* stream = nullptr) {

@@ -94,6 +94,12 @@ _decl("molot_attn_append_rope", [_p, _i, _p, _p, _p, _p, _p, _p, _i, _f, _p, _i,
 _decl("molot_attn_decode", [_p, _i, _p, _p, _i, _f, _i, _i, _p])
 _decl("molot_kv_check", [_p, _p])
 _decl("molot_attn_step", [_p, _i, _p, _p, _p, _p, _p, _i, _f, _p, _i, _p, _i, _f, _i, _p])
+_decl("molot_attn_prefill_gqa", [_p, _p, _p, _p, _i, _i, _i, _i, _i, _f, _i, _i])
+_decl("molot_attn_prefill_strided_dev",
+      [_p, _p, _p, _p, _i, _i, _i, _i, _i, _ll, _ll, _f, _i, _i, _p])
+_decl("molot_attn_append_rope_tokens",
+      [_p, _i, _p, _p, _p, _p, _p, _p, _i, _f, _p, _i, _i, _i, _p])
+_decl("molot_attn_prefill", [_p, _i, _p, _p, _i, _i, _f, _i, _i, _p])
 _decl("molot_paged_plan_create", [_pp])
 _decl("molot_paged_plan_destroy", [_p], None)
 _decl("molot_paged_plan_build", [_p, _i, _i, _i, _i, _p, _p, _i, _p])
@@ -185,6 +191,24 @@ def attn_decode_gqa_cache(Q, K, V, nq, nkv, n, qhd, scale, pos_cur, window) -> n
     check(_lib.molot_attn_decode_gqa_cache(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), nq, nkv, n, qhd,
                                            scale, pos_cur, window))
     return O
+
+
+def attn_prefill_gqa(Qm, K, V, nq, nkv, M, N, d, scale, pos0, window) -> np.ndarray:
+    """gemm.h:409-446 on host arrays: Qm [M][nq][d], K/V [N][nkv*d] -> Om [M][nq][d]."""
+    Qm, K, V = _host_f32(Qm), _host_f32(K), _host_f32(V)
+    Om = np.zeros((M, nq, d), np.float32)
+    check(_lib.molot_attn_prefill_gqa(_ptr(Qm), _ptr(K), _ptr(V), _ptr(Om), nq, nkv, M, N, d,
+                                      scale, pos0, window))
+    return Om
+
+
+def prefill_strided(Q, K, V, O, nq, nkv, M, N, d, stride_t, stride_h, scale, pos0, window,
+                    stream=None) -> None:
+    """gemm.h:409-446 on device tensors: Q, O [M][nq][d]; slot t of kv head g
+    at K + t*stride_t + g*stride_h."""
+    check(_lib.molot_attn_prefill_strided_dev(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), nq, nkv, M, N,
+                                              d, stride_t, stride_h, scale, pos0, window,
+                                              _stream_ptr(stream)))
 
 
 def attn_decode_gqa(Q, K, V, nq, nkv, n, d, scale) -> np.ndarray:
@@ -328,6 +352,27 @@ class KVCache:
         check(_lib.molot_attn_step(self._h, layer, _ptr(q), _ptr(k), _ptr(v), _ptr(q_norm),
                                    _ptr(k_norm), int(v_norm), eps, _ptr(freq), pos, _ptr(o), nq,
                                    scale, window, _stream_ptr(stream)))
+
+    def append_rope_tokens(self, layer, q, k, v, q_out, q_norm=None, k_norm=None, v_norm=False,
+                           eps=1e-6, freq=None, pos0=0, M=None, nq=None, stream=None) -> None:
+        """forward.h:368-392: M tokens' prologue, rows appended at n..n+M-1."""
+        M = M if M is not None else k.numel() // (self.nkv * self.hd)
+        nq = nq if nq is not None else q.numel() // (M * self.hd)
+        check(_lib.molot_attn_append_rope_tokens(self._h, layer, _ptr(q), _ptr(k), _ptr(v),
+                                                 _ptr(q_out), _ptr(q_norm), _ptr(k_norm),
+                                                 int(v_norm), eps, _ptr(freq), pos0, M, nq,
+                                                 _stream_ptr(stream)))
+
+    def prefill(self, src_layer, q, o, scale, pos0, window=0, M=None, nq=None,
+                stream=None) -> None:
+        """gemm.h:409-446 over src_layer's cache: q, o [M][nq][hd]."""
+        if M is None or nq is None:
+            if q.dim() == 3:
+                M, nq = q.shape[0], q.shape[1]
+            else:
+                raise ValueError("pass M and nq for flat q")
+        check(_lib.molot_attn_prefill(self._h, src_layer, _ptr(q), _ptr(o), nq, M, scale, pos0,
+                                      window, _stream_ptr(stream)))
 
     def decode(self, src_layer, q, o, scale, pos_cur, window=0, nq=None, stream=None) -> None:
         nq = nq if nq is not None else q.numel() // self.hd

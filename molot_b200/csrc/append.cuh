@@ -36,6 +36,10 @@ struct AppendArgs {
   int nq, nkv;
   // Position and cache slot of the new token.
   int pos, slot;                            // when seq_pos is null
+  // Several tokens of one sequence (prefill, forward.h:368-392): entry b
+  // is the token at position pos + b*tok_step, written to slot
+  // slot + b*tok_step (tok_step 0: one token per sequence).
+  int tok_step;
   const int* seq_pos;                       // [B] or null
   const int* seq_slot;                      // [B] or null
   // Cache addressing (same conventions as DecodeArgs).
@@ -90,14 +94,14 @@ __global__ void __launch_bounds__(kAppendWarps * 32)
   const int head = blockIdx.x * kAppendWarps + warp;
   const int b = blockIdx.y;
   if (head >= a.nq + a.nkv) return;
-  const int pos = a.seq_pos ? a.seq_pos[b] : a.pos;
+  const int pos = a.seq_pos ? a.seq_pos[b] : a.pos + b * a.tok_step;
 
   const bool is_q = head < a.nq;
   const int g = is_q ? head : head - a.nq;
   const float* x = is_q ? a.q_in + (long long)b * a.q_bstride + (long long)g * D
                         : a.k_in + (long long)b * a.kv_in_bstride + (long long)g * D;
   const float* w = is_q ? a.q_norm : a.k_norm;
-  const int slot = is_q ? 0 : (a.seq_slot ? a.seq_slot[b] : a.slot);
+  const int slot = is_q ? 0 : (a.seq_slot ? a.seq_slot[b] : a.slot + b * a.tok_step);
   float* dst = is_q ? a.q_out + (long long)b * a.qo_bstride + (long long)g * D
                     : cache_row(a, a.K, b, g, slot, D);
 

@@ -14,6 +14,7 @@
 #include "append.cuh"
 #include "decode.cuh"
 #include "molot_b200.h"
+#include "prefill.cuh"
 
 namespace molot {
 namespace {
@@ -411,6 +412,97 @@ int host_decode(const float* Q, const float* K, const float* V, float* O, int nq
   return c.ws.check(c.stream, true);
 }
 
+// ------------------------------------------------------------- prefill
+
+bool pick_prefill(int D, KernelRef* k) {
+  switch (D) {
+    case 64: *k = {reinterpret_cast<const void*>(&gqa_prefill_kernel<64>), PrefillTile<64>::kTotal};
+      return true;
+    case 128: *k = {reinterpret_cast<const void*>(&gqa_prefill_kernel<128>), PrefillTile<128>::kTotal};
+      return true;
+    case 256: *k = {reinterpret_cast<const void*>(&gqa_prefill_kernel<256>), PrefillTile<256>::kTotal};
+      return true;
+  }
+  return false;
+}
+
+// gemm.h:409-446 on device buffers: Q/O [M][nq][d] (token stride q_tstride /
+// o_tstride floats), slot t of kv head g at K + t*stride_t + g*stride_h.
+int prefill_strided(Workspace& ws, const float* Q, long long q_tstride, float* O,
+                    long long o_tstride, const float* K, const float* V, int nq, int nkv, int M,
+                    int N, int d, long long stride_t, long long stride_h, float scale, int pos0,
+                    int window, cudaStream_t st) {
+  if (!Q || !O || !K || !V) return fail(MOLOT_ERR_INVALID, "null pointer");
+  if (nq <= 0 || nkv <= 0 || nq % nkv || M < 0 || N < 0 || pos0 < 0)
+    return fail(MOLOT_ERR_INVALID, "bad sizes (nq must be a multiple of nkv)");
+  const int G = nq / nkv;
+  if (G > kPrefillRows || kPrefillRows % G)
+    return fail(MOLOT_ERR_UNSUPPORTED, "prefill group size must divide 64");
+  KernelRef k;
+  if (!pick_prefill(d, &k)) return fail(MOLOT_ERR_UNSUPPORTED, "prefill head_dim not built");
+  if (!aligned16(Q) || !aligned16(O) || !aligned16(K) || !aligned16(V) || (q_tstride & 3) ||
+      (o_tstride & 3) || (stride_t & 3) || (stride_h & 3))
+    return fail(MOLOT_ERR_INVALID, "buffers must be 16-byte aligned with strides multiple of 4");
+  if (M == 0) return MOLOT_OK;
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  if ((rc = ws.ensure(dev, 0, 0, 0))) return rc;
+  if ((rc = prepare_kernel(k, dev))) return rc;
+  PrefillArgs a = {};
+  a.Q = Q;
+  a.q_tstride = q_tstride;
+  a.O = O;
+  a.o_tstride = o_tstride;
+  a.K = K;
+  a.V = V;
+  a.stride_t = stride_t;
+  a.stride_h = stride_h;
+  a.nq = nq;
+  a.nkv = nkv;
+  a.G = G;
+  a.M = M;
+  a.N = N;
+  a.pos0 = pos0;
+  a.window = window;
+  a.scale = scale;
+  a.BP = kPrefillRows / G;
+  a.nblk_m = (M + a.BP - 1) / a.BP;
+  a.status = ws.status;
+  a.timeout_ns = kWaitLimitNs;
+  return launch(k.fn, dim3(a.nblk_m, nkv), dim3(kPrefillThreads), k.smem, st, &a);
+}
+
+// Host drop-in: stage Qm / K / V, run, copy Om back.
+int host_prefill(const float* Qm, const float* K, const float* V, float* Om, int nq, int nkv,
+                 int M, int N, int d, float scale, int pos0, int window) {
+  if (!Qm || !K || !V || !Om) return fail(MOLOT_ERR_INVALID, "null pointer");
+  if (M < 0 || N < 0 || nq <= 0 || nkv <= 0 || d <= 0)
+    return fail(MOLOT_ERR_INVALID, "sizes must be non-negative");
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  HostCtx& c = host_ctx(dev);
+  std::lock_guard<std::mutex> lk(c.mu);
+  if ((rc = c.init(dev))) return rc;
+  const size_t qn = (size_t)M * nq * d, kvn = (size_t)N * nkv * d;
+  const size_t oq = 0, ok = round4(qn), ov = ok + round4(kvn), oo = ov + round4(kvn);
+  if ((rc = c.reserve(oo + round4(qn) + 4))) return rc;
+  float* dq = c.buf + oq;
+  float* dk = c.buf + ok;
+  float* dv = c.buf + ov;
+  float* dout = c.buf + oo;
+  if (qn) MOLOT_CUDA(cudaMemcpyAsync(dq, Qm, qn * 4, cudaMemcpyHostToDevice, c.stream));
+  if (kvn) {
+    MOLOT_CUDA(cudaMemcpyAsync(dk, K, kvn * 4, cudaMemcpyHostToDevice, c.stream));
+    MOLOT_CUDA(cudaMemcpyAsync(dv, V, kvn * 4, cudaMemcpyHostToDevice, c.stream));
+  }
+  rc = prefill_strided(c.ws, dq, (long long)nq * d, dout, (long long)nq * d, dk, dv, nq, nkv, M,
+                       N, d, (long long)nkv * d, d, scale, pos0, window, c.stream);
+  if (rc) return rc;
+  if (qn) MOLOT_CUDA(cudaMemcpyAsync(Om, dout, qn * 4, cudaMemcpyDeviceToHost, c.stream));
+  MOLOT_CUDA(cudaStreamSynchronize(c.stream));
+  return c.ws.check(c.stream, true);
+}
+
 }  // namespace
 
 // Lets other translation units of the library report through
@@ -783,6 +875,87 @@ int molot_attn_step(molot_kv_cache* kv, int layer, const float* q, const float* 
   kv->len[layer] = n;
   kv->record(molot_kv_cache::kDecode, layer);
   return MOLOT_OK;
+}
+
+// forward.h:368-392 for M tokens of a KV-owning layer: per-token QK-norm /
+// V-norm / RoPE at positions pos0..pos0+M-1, rows appended at slots
+// n..n+M-1, n += M.
+int molot_attn_append_rope_tokens(molot_kv_cache* kv, int layer, const float* q, const float* k,
+                                  const float* v, float* q_out, const float* q_norm,
+                                  const float* k_norm, int v_norm, float eps, const float* freq,
+                                  int pos0, int M, int nq, void* stream) {
+  if (!kv || layer < 0 || layer >= kv->n_layers) return fail(MOLOT_ERR_INVALID, "bad layer");
+  if (!q || !k || !v || !q_out) return fail(MOLOT_ERR_INVALID, "null pointer");
+  if (M < 0 || M > 65535 || nq <= 0 || nq % kv->nkv || pos0 < 0)
+    return fail(MOLOT_ERR_INVALID, "bad token count / nq");
+  if (M == 0) return MOLOT_OK;
+  const int n = kv->len[layer];
+  if (n + M > kv->cap) return fail(MOLOT_ERR_CACHE_FULL, "fwd: KV cache full");
+  float *kc, *vc;
+  molot_kv_layer_data(kv, layer, &kc, &vc);
+  AppendArgs a = {};
+  a.q_in = q;
+  a.q_bstride = (long long)nq * kv->hd;
+  a.k_in = k;
+  a.v_in = v;
+  a.kv_in_bstride = (long long)kv->nkv * kv->hd;
+  a.q_out = q_out;
+  a.qo_bstride = (long long)nq * kv->hd;
+  a.q_norm = q_norm;
+  a.k_norm = k_norm;
+  a.v_norm = v_norm;
+  a.eps = eps;
+  a.freq = freq;
+  a.nq = nq;
+  a.nkv = kv->nkv;
+  a.pos = pos0;
+  a.slot = n;
+  a.tok_step = 1;
+  a.K = kc;
+  a.V = vc;
+  a.kv_bstride = 0;
+  a.stride_t = kv->hd;
+  a.stride_h = (long long)kv->cap * kv->hd;
+  int rc = append_launch(a, kv->hd, M, (cudaStream_t)stream);
+  if (rc) return rc;
+  kv->len[layer] = n + M;
+  kv->record(molot_kv_cache::kAppend, layer);
+  return MOLOT_OK;
+}
+
+// gemm.h:409-446 over the cache of src_layer (its current length N; the
+// layer itself or its shared-KV source): q, o [M][nq][hd] device.
+int molot_attn_prefill(molot_kv_cache* kv, int src_layer, const float* q, float* o, int nq, int M,
+                       float scale, int pos0, int window, void* stream) {
+  if (!kv || src_layer < 0 || src_layer >= kv->n_layers)
+    return fail(MOLOT_ERR_INVALID, "bad layer");
+  if (nq <= 0 || nq % kv->nkv) return fail(MOLOT_ERR_INVALID, "nq must be a multiple of nkv");
+  float *kc, *vc;
+  molot_kv_layer_data(kv, src_layer, &kc, &vc);
+  const int hd = kv->hd;
+  int rc = prefill_strided(kv->ws, q, (long long)nq * hd, o, (long long)nq * hd, kc, vc, nq,
+                           kv->nkv, M, kv->len[src_layer], hd, hd, (long long)kv->cap * hd,
+                           scale, pos0, window, (cudaStream_t)stream);
+  if (rc) return rc;
+  kv->record(molot_kv_cache::kDecode, -1);  // releases its successor after its own wait
+  return MOLOT_OK;
+}
+
+int molot_attn_prefill_strided_dev(const float* Q, const float* K, const float* V, float* O,
+                                   int nq, int nkv, int M, int N, int d, long long stride_t,
+                                   long long stride_h, float scale, int pos0, int window,
+                                   void* stream) {
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  HostCtx& c = host_ctx(dev);
+  std::lock_guard<std::mutex> lk(c.mu);
+  return prefill_strided(c.ws, Q, (long long)nq * d, O, (long long)nq * d, K, V, nq, nkv, M, N,
+                         d, stride_t, stride_h, scale, pos0, window, (cudaStream_t)stream);
+}
+
+int molot_attn_prefill_gqa(const float* Qm, const float* K, const float* V, float* Om, int nq,
+                           int nkv, int M, int N, int d, float scale, int pos0, int window) {
+  return host_prefill(Qm, K, V, Om, nq, nkv, M, N, d, scale, pos0, window);
 }
 
 int molot_kv_check(molot_kv_cache* kv, void* stream) {

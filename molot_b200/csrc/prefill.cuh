@@ -1,0 +1,303 @@
+// Causal / sliding-window GQA prefill attention (gemm.h:409-446,
+// attn_prefill_gqa, called at forward.h:396): M new queries at positions
+// pos0..pos0+M-1 against the filled cache [0, N).  Query m of head h attends
+// slots [t0, nn): nn = min(pos+1, N), t0 = max(0, pos-window+1) (window > 0)
+// capped at N; an empty range yields zeros, as the reference's.
+//
+// One CTA = one kv head x 64 query rows (kPrefillRows / G positions, all G
+// query heads of the kv head: each K/V row staged in shared memory serves
+// every grouped head).  FP32 on the CUDA cores -- the reference's contract is
+// FP32 to 1e-5 -- flash-attention style: key tiles of BN slots stream through
+// a two-stage shared-memory ring (one TMA bulk copy per K or V row, rows
+// padded by 4 floats so the column reads of K are bank-conflict free); per
+// tile S = Q K^T in registers (4 rows x BN/16 keys per thread), an online
+// softmax in base 2, P to shared memory, O += P V in registers (4 rows x D/16
+// dims per thread).  Grid: (query blocks, nkv), the longest (latest) query
+// blocks first.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <math_constants.h>
+
+#include <cstdint>
+
+#include "ptx.cuh"
+
+namespace molot {
+
+constexpr int kPrefillThreads = 256;  // 16 x 16: ty owns 4 rows, tx a column set
+constexpr int kPrefillRows = 64;      // query rows (position, head) per CTA
+
+template <int D>
+struct PrefillTile {
+  static constexpr int BN = D > 128 ? 32 : 64;  // keys per tile
+  static constexpr int NJ = BN / 16;            // score columns per thread
+  static constexpr int LD = D + 4;              // padded K/V/Q row pitch (floats)
+  static constexpr int PLD = BN + 4;            // P row pitch (floats)
+  static constexpr int kQ = kPrefillRows * LD * 4;
+  static constexpr int kKV = BN * LD * 4;  // one K or V tile
+  static constexpr int kP = kPrefillRows * PLD * 4;
+  static constexpr int kBars = 3 * 8;
+  static constexpr int kTotal = kQ + 4 * kKV + kP + kBars + 16;
+  static_assert(kTotal <= 227 * 1024, "prefill CTA exceeds the shared-memory limit");
+  static_assert(D % 64 == 0, "head dim must be a multiple of 64");
+};
+
+struct PrefillArgs {
+  const float* Q;  // query m, head h: Q + m*q_tstride + h*D
+  long long q_tstride;
+  float* O;  // same layout, o_tstride
+  long long o_tstride;
+  const float* K;  // slot t of kv head g: K + t*stride_t + g*stride_h
+  const float* V;
+  long long stride_t, stride_h;
+  int nq, nkv, G, M, N, pos0, window;
+  float scale;
+  int BP;      // query positions per CTA (kPrefillRows / G)
+  int nblk_m;  // ceil(M / BP)
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ float prefill_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kPrefillThreads, 1)
+    gqa_prefill_kernel(const __grid_constant__ PrefillArgs a) {
+  using TP = PrefillTile<D>;
+  constexpr int BN = TP::BN, NJ = TP::NJ, LD = TP::LD, PLD = TP::PLD;
+  constexpr int DJ = D / 64;  // float4 groups of output columns per thread
+  constexpr float kLog2e = 1.4426950408889634f;
+
+  extern __shared__ __align__(128) unsigned char smem[];
+  float* Qs = reinterpret_cast<float*>(smem);
+  float* KVs = reinterpret_cast<float*>(smem + TP::kQ);  // [stage][K,V][BN][LD]
+  float* Ps = reinterpret_cast<float*>(smem + TP::kQ + 4 * TP::kKV);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TP::kQ + 4 * TP::kKV + TP::kP);
+  uint64_t* q_bar = bars + 2;
+  volatile int* abort_sm = reinterpret_cast<volatile int*>(bars + 3);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int ty = tid >> 4, tx = tid & 15;  // a warp = two ty rows of 16 lanes
+  const int g = blockIdx.y;
+  const int mb = a.nblk_m - 1 - blockIdx.x;  // latest (longest) query blocks first
+  const int G = a.G;
+
+  if (tid == 0) {
+    ptx::mbar_init(bars + 0, 1);
+    ptx::mbar_init(bars + 1, 1);
+    ptx::mbar_init(q_bar, 1);
+    *abort_sm = 0;
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  // Inputs (q, the cache rows) may come from the preceding launch.
+  ptx::pdl_wait();
+  if (tid == 0) ptx::pdl_launch_dependents();
+
+  // Block geometry: rows r = m_local*G + h_local.
+  const int m_first = mb * a.BP;
+  const int m_end = min(a.M, m_first + a.BP);
+  auto row_t0 = [&](int m) {
+    const int pos = a.pos0 + m;
+    int t0 = (a.window > 0 && pos - a.window + 1 > 0) ? pos - a.window + 1 : 0;
+    return t0 < a.N ? t0 : a.N;
+  };
+  auto row_nn = [&](int m) { return min(a.pos0 + m + 1, a.N); };
+  const int t_lo = row_t0(m_first);
+  const int t_hi = row_nn(m_end - 1);
+  const int ntiles = t_hi > t_lo ? (t_hi - t_lo + BN - 1) / BN : 0;
+  const int valid_rows = (m_end - m_first) * G;
+
+  // ---- stage Q (one bulk copy per valid row) and the first key tile
+  const uint64_t pol = ptx::policy_evict_first();
+  auto issue_tile = [&](int i) {  // warp 0 only
+    const int stage = i & 1;
+    const int ts = t_lo + i * BN;
+    const int rows = min(BN, t_hi - ts);
+    float* Kd = KVs + (size_t)(stage * 2) * BN * LD;
+    float* Vd = Kd + (size_t)BN * LD;
+    if (lane == 0) ptx::mbar_arrive_expect_tx(bars + stage, (uint32_t)rows * D * 4u * 2u);
+    __syncwarp();
+    for (int c = lane; c < rows; c += 32) {
+      const long long off = (long long)(ts + c) * a.stride_t + (long long)g * a.stride_h;
+      ptx::bulk_g2s(Kd + (size_t)c * LD, a.K + off, D * 4u, bars + stage, pol);
+      ptx::bulk_g2s(Vd + (size_t)c * LD, a.V + off, D * 4u, bars + stage, pol);
+    }
+  };
+  if (warp == 0) {
+    if (lane == 0) ptx::mbar_arrive_expect_tx(q_bar, (uint32_t)valid_rows * D * 4u);
+    __syncwarp();
+    for (int r = lane; r < valid_rows; r += 32) {
+      const int m = m_first + r / G, h = g * G + r % G;
+      ptx::bulk_g2s(Qs + (size_t)r * LD, a.Q + (long long)m * a.q_tstride + (long long)h * D,
+                    D * 4u, q_bar, pol);
+    }
+    if (ntiles > 0) issue_tile(0);
+  }
+
+  // Per-row state (4 rows per thread, replicated over the 16 tx lanes).
+  int rt0[4], rnn[4];
+  float mrow[4], lrow[4];
+  float o[4][DJ * 4];
+#pragma unroll
+  for (int ii = 0; ii < 4; ++ii) {
+    const int r = ty * 4 + ii;
+    const int m = m_first + r / G;
+    const bool ok = r < valid_rows;
+    rt0[ii] = ok ? row_t0(m) : 0;
+    rnn[ii] = ok ? row_nn(m) : 0;  // invalid rows attend nothing
+    mrow[ii] = -CUDART_INF_F;
+    lrow[ii] = 0.f;
+#pragma unroll
+    for (int j = 0; j < DJ * 4; ++j) o[ii][j] = 0.f;
+  }
+  if (!ptx::mbar_wait_bounded(q_bar, 0, a.timeout_ns)) *abort_sm = 1;
+
+  const float sl2 = a.scale * kLog2e;
+  for (int i = 0; i < ntiles; ++i) {
+    const int stage = i & 1;
+    // The other stage was last read by tile i-1, finished before the barrier
+    // that closed that iteration.
+    if (warp == 0 && i + 1 < ntiles && !*abort_sm) issue_tile(i + 1);
+    if (!ptx::mbar_wait_bounded(bars + stage, (i >> 1) & 1, a.timeout_ns)) *abort_sm = 1;
+    __syncthreads();
+    if (*abort_sm) break;
+    const float* Kt = KVs + (size_t)(stage * 2) * BN * LD;
+    const float* Vt = Kt + (size_t)BN * LD;
+    const int ts = t_lo + i * BN;
+    const int kc = min(BN, t_hi - ts);
+
+    // ---- S = Q K^T for rows ty*4+ii, keys tx+16j
+    float s[4][NJ];
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) s[ii][j] = 0.f;
+    const float* qb = Qs + (size_t)(ty * 4) * LD;
+    const float* kb = Kt + (size_t)tx * LD;
+#pragma unroll 4
+    for (int k = 0; k < D; k += 4) {
+      float4 qv[4], kv[NJ];
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii) qv[ii] = *reinterpret_cast<const float4*>(qb + ii * LD + k);
+#pragma unroll
+      for (int j = 0; j < NJ; ++j)
+        kv[j] = *reinterpret_cast<const float4*>(kb + (size_t)(16 * j) * LD + k);
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          s[ii][j] = fmaf(qv[ii].x, kv[j].x, s[ii][j]);
+          s[ii][j] = fmaf(qv[ii].y, kv[j].y, s[ii][j]);
+          s[ii][j] = fmaf(qv[ii].z, kv[j].z, s[ii][j]);
+          s[ii][j] = fmaf(qv[ii].w, kv[j].w, s[ii][j]);
+        }
+    }
+
+    // ---- online softmax (base 2), P to shared memory
+#pragma unroll
+    for (int ii = 0; ii < 4; ++ii) {
+      float tmax = -CUDART_INF_F;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int t = ts + tx + 16 * j;
+        const bool ok = t >= rt0[ii] && t < rnn[ii];
+        s[ii][j] = ok ? s[ii][j] * sl2 : -CUDART_INF_F;
+        tmax = fmaxf(tmax, s[ii][j]);
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1)
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+      const float mnew = fmaxf(mrow[ii], tmax);
+      const float alpha = (mrow[ii] == -CUDART_INF_F) ? 0.f : prefill_ex2(mrow[ii] - mnew);
+      float psum = 0.f;
+      float* prow = Ps + (size_t)(ty * 4 + ii) * PLD;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const float p = (s[ii][j] == -CUDART_INF_F) ? 0.f : prefill_ex2(s[ii][j] - mnew);
+        psum += p;
+        prow[tx + 16 * j] = p;
+      }
+      lrow[ii] = lrow[ii] * alpha + psum;  // this lane's share of the row sum
+      mrow[ii] = mnew;
+#pragma unroll
+      for (int j = 0; j < DJ * 4; ++j) o[ii][j] *= alpha;
+    }
+    __syncthreads();
+
+    // ---- O += P V over the kc valid keys of the tile
+    const float* pb = Ps + (size_t)(ty * 4) * PLD;
+    int c = 0;
+    for (; c + 4 <= kc; c += 4) {
+      float4 pv[4];
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii) pv[ii] = *reinterpret_cast<const float4*>(pb + ii * PLD + c);
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const float* vr = Vt + (size_t)(c + cc) * LD + tx * 4;
+#pragma unroll
+        for (int jj = 0; jj < DJ; ++jj) {
+          const float4 v4 = *reinterpret_cast<const float4*>(vr + 64 * jj);
+#pragma unroll
+          for (int ii = 0; ii < 4; ++ii) {
+            const float p = cc == 0 ? pv[ii].x : cc == 1 ? pv[ii].y : cc == 2 ? pv[ii].z : pv[ii].w;
+            o[ii][jj * 4 + 0] = fmaf(p, v4.x, o[ii][jj * 4 + 0]);
+            o[ii][jj * 4 + 1] = fmaf(p, v4.y, o[ii][jj * 4 + 1]);
+            o[ii][jj * 4 + 2] = fmaf(p, v4.z, o[ii][jj * 4 + 2]);
+            o[ii][jj * 4 + 3] = fmaf(p, v4.w, o[ii][jj * 4 + 3]);
+          }
+        }
+      }
+    }
+    for (; c < kc; ++c) {  // ragged end of the last tile
+      const float* vr = Vt + (size_t)c * LD + tx * 4;
+#pragma unroll
+      for (int jj = 0; jj < DJ; ++jj) {
+        const float4 v4 = *reinterpret_cast<const float4*>(vr + 64 * jj);
+#pragma unroll
+        for (int ii = 0; ii < 4; ++ii) {
+          const float p = pb[ii * PLD + c];
+          o[ii][jj * 4 + 0] = fmaf(p, v4.x, o[ii][jj * 4 + 0]);
+          o[ii][jj * 4 + 1] = fmaf(p, v4.y, o[ii][jj * 4 + 1]);
+          o[ii][jj * 4 + 2] = fmaf(p, v4.z, o[ii][jj * 4 + 2]);
+          o[ii][jj * 4 + 3] = fmaf(p, v4.w, o[ii][jj * 4 + 3]);
+        }
+      }
+    }
+    __syncthreads();  // P and this stage are free again
+  }
+  if (*abort_sm) {
+    if (tid == 0) atomicCAS(a.status, 0, 3);
+    return;
+  }
+
+  // ---- epilogue: full row sums, normalise, store
+#pragma unroll
+  for (int ii = 0; ii < 4; ++ii) {
+    float l = lrow[ii];
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+    const int r = ty * 4 + ii;
+    if (r >= valid_rows) continue;
+    const int m = m_first + r / G, h = g * G + r % G;
+    const float inv = l > 0.f ? 1.f / l : 0.f;  // empty range: zeros (gemm.h:431-436)
+    float* dst = a.O + (long long)m * a.o_tstride + (long long)h * D + tx * 4;
+#pragma unroll
+    for (int jj = 0; jj < DJ; ++jj) {
+      float4 v;
+      v.x = o[ii][jj * 4 + 0] * inv;
+      v.y = o[ii][jj * 4 + 1] * inv;
+      v.z = o[ii][jj * 4 + 2] * inv;
+      v.w = o[ii][jj * 4 + 3] * inv;
+      *reinterpret_cast<float4*>(dst + 64 * jj) = v;
+    }
+  }
+}
+
+}  // namespace molot

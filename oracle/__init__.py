@@ -90,6 +90,8 @@ def port():
                  [_p, _p, _p, _p, _p, _i, _f, _p, _i, _p, _p, _p, _i, _p, _i, _i, _i, _f, _i], _i)
         _declare(lib, "oracle_attn_decode_paged",
                  [_p, _p, _p, _p, _p, _i, _p, _p, _i, _i, _i, _i, _i, _f, _i])
+        _declare(lib, "oracle_attn_prefill_gqa",
+                 [_p, _p, _p, _p, _i, _i, _i, _i, _i, _f, _i, _i])
         _port = lib
     return _port
 
@@ -121,6 +123,9 @@ def ref():
             _declare(lib, "ref_dot", [_p, _p, _i], _f)
             _declare(lib, "ref_attn_layer_step",
                      [_p, _p, _p, _p, _p, _i, _f, _p, _i, _p, _p, _p, _i, _p, _i, _i, _i, _f, _i, _i], _i)
+            if hasattr(lib, "ref_attn_prefill_gqa"):
+                _declare(lib, "ref_attn_prefill_gqa",
+                         [_p, _p, _p, _p, _i, _i, _i, _i, _i, _f, _i, _i, _i])
             _ref = lib
     return _ref
 
@@ -214,6 +219,24 @@ def attn_layer_step(q, k, v, q_norm, k_norm, v_norm, eps, freq, pos, kc, vc, n, 
             raise RuntimeError("reference shim unavailable on this host")
         st = lib.ref_attn_layer_step(*args, nthreads or (os.cpu_count() or 1))
     return st, nn.value, out
+
+
+def attn_prefill_gqa(Qm, K, V, nq, nkv, M, N, d, scale, pos0, window, impl="port",
+                     nthreads=0):
+    """gemm.h:409-446 on host arrays: Qm [M][nq][d], K/V [N][nkv*d] (at least
+    N rows); returns Om [M][nq][d]."""
+    Qm, K, V = _f32(Qm), _f32(K), _f32(V)
+    Om = np.zeros((M, nq, d), np.float32)
+    if impl == "port":
+        port().oracle_attn_prefill_gqa(_ptr(Qm), _ptr(K), _ptr(V), _ptr(Om), nq, nkv, M, N, d,
+                                       scale, pos0, window)
+    else:
+        lib = ref()
+        if lib is None:
+            raise RuntimeError("reference shim unavailable on this host")
+        lib.ref_attn_prefill_gqa(_ptr(Qm), _ptr(K), _ptr(V), _ptr(Om), nq, nkv, M, N, d, scale,
+                                 pos0, window, nthreads or (os.cpu_count() or 1))
+    return Om
 
 
 def rope_apply(x, d, pos, inv_freq, impl="port"):

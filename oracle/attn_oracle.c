@@ -235,3 +235,46 @@ void oracle_attn_decode_paged(const float* Q, const float* Kpool, const float* V
     free(vc);
   }
 }
+
+/* gemm.h:409-446 attn_prefill_gqa: causal prefill of M queries (positions
+ * pos0+m) against a filled [N][nkv*d] cache.  Per (head, query): slots
+ * [t0, nn) with nn = min(pos+1, N) and t0 = max(0, pos-window+1) capped at N;
+ * scores = dot*scale; two-pass softmax with expf and a double denominator;
+ * inv = (float)(1/den); o[j] accumulated over t in order with w = s*inv. */
+void oracle_attn_prefill_gqa(const float* Qm, const float* K, const float* V, float* Om, int nq,
+                             int nkv, int M, int N, int d, float scale, int pos0, int window) {
+  int groups = nq / nkv;
+  long S = (long)nkv * d;
+  float* scores = (float*)malloc(sizeof(float) * (size_t)(N > 0 ? N : 1));
+  for (int h = 0; h < nq; ++h) {
+    int kv = h / groups;
+    for (int m = 0; m < M; ++m) {
+      int pos = pos0 + m;
+      int t0 = 0;
+      if (window > 0 && pos - window + 1 > t0) t0 = pos - window + 1;
+      if (t0 > N) t0 = N;
+      int nn = pos + 1 < N ? pos + 1 : N;
+      const float* qh = Qm + ((long)m * nq + h) * d;
+      float* oh = Om + ((long)m * nq + h) * d;
+      float mx = -1e30f;
+      for (int t = t0; t < nn; ++t) {
+        float s = oracle_dot(qh, K + (long)t * S + (long)kv * d, d) * scale;
+        scores[t] = s;
+        if (s > mx) mx = s;
+      }
+      double den = 0;
+      for (int t = t0; t < nn; ++t) {
+        scores[t] = expf(scores[t] - mx);
+        den += scores[t];
+      }
+      float inv = (float)(1.0 / den);
+      for (int j = 0; j < d; ++j) oh[j] = 0;
+      for (int t = t0; t < nn; ++t) {
+        float w = scores[t] * inv;
+        const float* vv = V + (long)t * S + (long)kv * d;
+        for (int j = 0; j < d; ++j) oh[j] = fmaf(vv[j], w, oh[j]);
+      }
+    }
+  }
+  free(scores);
+}

@@ -76,6 +76,11 @@ void oracle_attn_decode_paged(const float* Q, const float* Kpool, const float* V
                               const int* positions, int B, int nq, int nkv, int d, int page_size,
                               float scale, int window);
 
+/* Causal prefill attention, gemm.h:409-446: Qm, Om [M][nq][d], K/V
+ * [N][nkv*d]; query m sits at position pos0+m. */
+void oracle_attn_prefill_gqa(const float* Qm, const float* K, const float* V, float* Om, int nq,
+                             int nkv, int M, int N, int d, float scale, int pos0, int window);
+
 #ifdef __cplusplus
 }
 #endif

@@ -139,4 +139,13 @@ int ref_attn_layer_step(float* q, float* k, float* v, const float* q_norm, const
   return 0;
 }
 
+// gemm.h:409-446 (causal prefill attention over a filled cache)
+void ref_attn_prefill_gqa(const float* Qm, const float* K, const float* V, float* Om, int nq,
+                          int nkv, int M, int N, int d, float scale, int pos0, int window,
+                          int nthreads) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  molot::attn_prefill_gqa(Qm, K, V, Om, nq, nkv, M, N, d, scale, pos0, window,
+                          pool_for(nthreads));
+}
+
 }  // extern "C"

@@ -19,6 +19,8 @@ from __future__ import annotations
 import os
 import sys
 
+import zlib
+
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -113,26 +115,57 @@ def layer_step_case():
                 out=out, q_rot=q, k_row=kc[n0].copy(), v_row=vc[n0].copy())
 
 
-def main():
+def prefill_cases():
+    """gemm.h:409-446 causal prefill over a filled cache (forward.h:396): the
+    cache holds pos0 earlier slots plus the M new ones (N = pos0 + M)."""
+    out = {}
+    specs = {
+        "g4_d64_full": (8, 2, 64, 40, 20, 0, 0.125),
+        "g4_d64_swa16": (8, 2, 64, 40, 20, 16, 0.125),
+        "g4_d128": (8, 2, 128, 20, 45, 0, 128 ** -0.5),
+        "g2_d256_swa": (4, 2, 256, 16, 30, 24, 1.0),
+        "g8_d128_pos0": (8, 1, 128, 17, 0, 0, 128 ** -0.5),
+    }
+    for name, (nq, nkv, d, M, pos0, window, scale) in specs.items():
+        rng = np.random.default_rng(zlib.crc32(name.encode()))
+        N = pos0 + M
+        Q = rng.standard_normal((M, nq, d)).astype(np.float32)
+        K = rng.standard_normal((N, nkv * d)).astype(np.float32)
+        V = rng.standard_normal((N, nkv * d)).astype(np.float32)
+        O = oracle.attn_prefill_gqa(Q, K, V, nq, nkv, M, N, d, scale, pos0, window, impl="ref",
+                                    nthreads=4)
+        out[name] = dict(Q=Q, K=K, V=V, O=O, params=np.array([nq, nkv, d, M, N, pos0, window],
+                                                              np.int64),
+                         scale=np.float32(scale))
+    return out
+
+
+def flatten(cases):
+    flat = {}
+    for name, case in cases.items():
+        for k, v in case.items():
+            flat[f"{name}/{k}"] = v
+    return flat
+
+
+FIXTURES = {
+    "attn_gqa_cache.npz": lambda: flatten(attn_cases()),
+    "attn_head_bench.npz": head_case,
+    "exp16.npz": exp_case,
+    "norm_rope.npz": lambda: flatten(norm_rope_case()),
+    "layer_step.npz": layer_step_case,
+    "prefill.npz": lambda: flatten(prefill_cases()),
+}
+
+
+def main(names=None):
+    """Write the named fixtures (all when none are given)."""
     if oracle.ref() is None:
         raise SystemExit("reference shim not available (needs the reference tree and AVX-512)")
-    flat = {}
-    for name, case in attn_cases().items():
-        for k, v in case.items():
-            flat[f"{name}/{k}"] = v
-    np.savez_compressed(os.path.join(HERE, "attn_gqa_cache.npz"), **flat)
-    np.savez_compressed(os.path.join(HERE, "attn_head_bench.npz"), **head_case())
-    np.savez_compressed(os.path.join(HERE, "exp16.npz"), **exp_case())
-    flat = {}
-    for name, case in norm_rope_case().items():
-        for k, v in case.items():
-            flat[f"{name}/{k}"] = v
-    np.savez_compressed(os.path.join(HERE, "norm_rope.npz"), **flat)
-    np.savez_compressed(os.path.join(HERE, "layer_step.npz"), **layer_step_case())
-    for f in sorted(os.listdir(HERE)):
-        if f.endswith(".npz"):
-            print(f, os.path.getsize(os.path.join(HERE, f)))
+    for fname in names or sorted(FIXTURES):
+        np.savez_compressed(os.path.join(HERE, fname), **FIXTURES[fname]())
+        print(fname, os.path.getsize(os.path.join(HERE, fname)))
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:])

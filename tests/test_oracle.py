@@ -157,3 +157,17 @@ def test_rel_err_metric(orc):
     want = np.array([1.0, -2.0, 0.0])
     assert orc.rel_err(want, want) == 0.0
     assert abs(orc.rel_err(want + np.array([0, 0, 2e-5]), want) - 1e-5) < 1e-12
+
+
+def test_prefill_oracle_matches_reference_golden():
+    """The C restatement of gemm.h:409-446 against the reference's own
+    attn_prefill_gqa run on the same inputs (tests/golden/prefill.npz)."""
+    import oracle
+    z = np.load(os.path.join(GOLDEN, "prefill.npz"))
+    names = sorted({k.split("/")[0] for k in z.files})
+    assert len(names) == 5
+    for name in names:
+        nq, nkv, d, M, N, pos0, window = (int(x) for x in z[f"{name}/params"])
+        got = oracle.attn_prefill_gqa(z[f"{name}/Q"], z[f"{name}/K"], z[f"{name}/V"], nq, nkv, M,
+                                      N, d, float(z[f"{name}/scale"]), pos0, window)
+        assert oracle.rel_err(got, z[f"{name}/O"]) < 1e-6, name
