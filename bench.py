@@ -70,6 +70,9 @@ CONFIGS = {
     "cfg4": dict(kind="paged_seq", layers=32, nq=32, nkv=8, d=128, batch=64, len_lo=512,
                  len_hi=32768, page=16, theta=5e5, seed=4,
                  desc="paged continuous batching, Llama-3-8B shape, B=64, n~U[512,32768]"),
+    "prefill": dict(kind="prefill", layers=32, nq=32, nkv=8, d=128, prompt=4096, theta=5e5,
+                    window=0, desc="prefill of a 4096-token prompt, Llama-3-8B attention shape "
+                                   "(not a BASELINE config: the next row after decode)"),
     "cfg5": dict(kind="paged_head", layers=80, nq=64, nkv=8, d=128, batch=32, len_lo=8192,
                  len_hi=131072, page=16, theta=5e5, seed=5,
                  desc="Llama-3-70B shape, B=32, n~U[8192,131072], kv-head sharded"),
@@ -176,6 +179,24 @@ def attended(n, window):
     return min(n, window) if window > 0 else n
 
 
+def prefill_flops(cfg):
+    """Attention FLOPs of one prefill layer: 2 (QK) + 2 (PV) multiply-adds
+    per attended (query, slot, head, dim)."""
+    M, w = cfg["prompt"], cfg["window"]
+    pairs = sum(min(m + 1, w) if w > 0 else m + 1 for m in range(M))
+    return 4 * cfg["nq"] * cfg["d"] * pairs
+
+
+PREFILL_METRIC = "prefill attention TFLOP/s (FP32), 4096-token prompt"
+
+
+def step_work(cfg):
+    """(metric, unit, amount per step, divisor to the unit's base) of a config."""
+    if cfg["kind"] == "prefill":
+        return PREFILL_METRIC, "TFLOP/s", cfg["layers"] * prefill_flops(cfg), 1e12
+    return METRIC, "GB/s", step_bytes(cfg), 1e9
+
+
 def step_bytes(cfg):
     """Unique KV bytes one decode step reads (all layers, all sequences)."""
     kind, nkv, d = cfg["kind"], cfg["nkv"], cfg["d"]
@@ -198,7 +219,9 @@ class RefWorkload:
         import oracle
         self.oracle, self.impl, self.cores, self.cfg = oracle, impl, cores, cfg
         kind, nq, nkv, d = cfg["kind"], cfg["nq"], cfg["nkv"], cfg["d"]
-        if kind == "single":
+        if kind == "prefill":
+            self.items = [(cfg["prompt"], 0, cfg["window"])]
+        elif kind == "single":
             n = cfg["ctx"] + 1
             self.items = [(n, n - 1, 0)]
         elif kind == "gemma":
@@ -212,6 +235,8 @@ class RefWorkload:
         rng = np.random.default_rng(7)
         nbuf = 2 if kind in ("single", "gemma") else 1  # distinct buffers >> CPU caches
         self.Q = rng.standard_normal((nq, d), dtype=np.float32)
+        if kind == "prefill":
+            self.Qm = rng.standard_normal((cfg["prompt"], nq, d), dtype=np.float32)
         self.K = [rng.standard_normal((nmax, nkv * d), dtype=np.float32) for _ in range(nbuf)]
         self.V = [rng.standard_normal((nmax, nkv * d), dtype=np.float32) for _ in range(nbuf)]
         self.t = [0.0] * len(self.items)
@@ -227,6 +252,19 @@ class RefWorkload:
         buf = i % len(self.K)
         K, V = self.K[buf][:n], self.V[buf][:n]
         scale = 1.0 / math.sqrt(d)
+        if cfg["kind"] == "prefill":  # n = prompt length, pos0 = 0
+            Qm = self.Qm
+            t0 = time.perf_counter()
+            self.oracle.attn_prefill_gqa(Qm, K, V, nq, nkv, n, n, d, scale, 0, w,
+                                         impl="ref" if self.impl == "reference" else "port",
+                                         nthreads=self.cores)
+            dt = time.perf_counter() - t0
+            if record:
+                self.t[j] += dt
+                self.c[j] += 1
+                self.bytes += prefill_flops(cfg)  # FLOPs for this kind
+                self.seconds += dt
+            return dt
         t0 = time.perf_counter()
         if self.impl == "reference":
             self.oracle.attn_decode_gqa_cache(self.Q, K, V, nq, nkv, n, d, scale, pos, w,
@@ -244,7 +282,7 @@ class RefWorkload:
     def step_seconds(self):
         cfg = self.cfg
         mean = [t / c if c else 0.0 for t, c in zip(self.t, self.c)]
-        if cfg["kind"] == "single":
+        if cfg["kind"] in ("single", "prefill"):
             return cfg["layers"] * mean[0]
         if cfg["kind"] == "gemma":
             ng = sum(1 for w, _ in gemma_layers(cfg) if w == 0)
@@ -252,7 +290,8 @@ class RefWorkload:
         return step_bytes(cfg) / (self.bytes / self.seconds)
 
     def describe(self, what):
-        return (f"{sum(self.c)} calls of attn_decode_gqa_cache ({what}), "
+        fn = "attn_prefill_gqa" if self.cfg["kind"] == "prefill" else "attn_decode_gqa_cache"
+        return (f"{sum(self.c)} calls of {fn} ({what}), "
                 f"{self.seconds:.1f}s; per-step time extrapolated from per-call means")
 
 
@@ -277,24 +316,26 @@ def run_reference(args, cfg):
     for i in range(args.steps * per_step):
         wl.call(i)
     sec = wl.step_seconds()
-    value = step_bytes(cfg) / sec / 1e9
-    batch = cfg.get("batch", 1)
+    metric, unit, amount, div = step_work(cfg)
+    value = amount / sec / div
+    batch = cfg.get("batch", cfg.get("prompt", 1) if cfg["kind"] == "prefill" else 1)
     what = {"single": f"one layer, n={cfg.get('ctx', 0) + 1}",
             "gemma": "a global and a 1024-slot SWA layer, alternating",
+            "prefill": f"one layer's attn_prefill_gqa over a {cfg.get('prompt')}-token prompt",
             }.get(cfg["kind"], "one sequence per call, lengths from the config's seeded draw")
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "impl": "reference", "metric": metric, "value": round(value, 3), "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak" if cfg["kind"] in ("single", "gemma") else "strong",
+        "scaling": "weak" if cfg["kind"] in ("single", "gemma", "prefill") else "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
         "config": {"workload": f"{args.config}: {cfg['desc']} (reference CPU sample)",
                    "layers": cfg["layers"], "nq": cfg["nq"], "nkv": cfg["nkv"],
                    "head_dim": cfg["d"]},
         "tok_per_s": round(batch / sec, 3),
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+        "cpu_baseline": {"value": round(value, 3), "unit": unit, "cores": cores, "kind": kind,
                          "sample": wl.describe(what)},
-        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+        "e2e": {"value": round(value, 3), "unit": unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -312,7 +353,8 @@ def cpu_baseline_sample(cfg):
         wl.call(i)
         i += 1
     sec = wl.step_seconds()
-    return {"value": round(step_bytes(cfg) / sec / 1e9, 3), "unit": "GB/s", "cores": cores,
+    _, unit, amount, div = step_work(cfg)
+    return {"value": round(amount / sec / div, 3), "unit": unit, "cores": cores,
             "kind": kind, "sample": wl.describe(f"{cfg['kind']} workload")}
 
 
@@ -695,6 +737,113 @@ def run_gemma(args, cfg):
     return 0
 
 
+def run_prefill(args, cfg):
+    """Prefill config: per layer molot_attn_append_rope_tokens (QK-norm/RoPE of
+    the prompt's M tokens, rows appended) then molot_attn_prefill."""
+    rt = Rt()
+    torch = rt.torch
+    import molot_b200 as mb
+
+    L, nq, nkv, d, M = cfg["layers"], cfg["nq"], cfg["nkv"], cfg["d"], cfg["prompt"]
+    window, scale = cfg["window"], 1.0 / math.sqrt(d)
+    cache = mb.KVCache(L, nkv, d, M)
+    gen = torch.Generator(device=rt.dev)
+    gen.manual_seed(1234 + rt.rank)
+    q_raw = torch.randn((L, M, nq, d), device=rt.dev, generator=gen)
+    k_raw = torch.randn((L, M, nkv, d), device=rt.dev, generator=gen)
+    v_raw = torch.randn((L, M, nkv, d), device=rt.dev, generator=gen)
+    q_rot = torch.empty_like(q_raw)
+    out = torch.empty_like(q_raw)
+    freq = rope_freq(torch, cfg["theta"], d, rt.dev)
+
+    def step(qr, kr, vr, o, attn_only=False):
+        st = torch.cuda.current_stream()
+        for l in range(L):
+            if not attn_only:
+                cache.set_length(l, 0)
+                cache.append_rope_tokens(l, qr[l], kr[l], vr[l], q_rot[l], None, None, False,
+                                         1e-6, freq, 0, M, nq, st)
+            cache.prefill(l, q_rot[l], o[l], scale, 0, window, M, nq, st)
+
+    for _ in range(args.warmup):
+        step(q_raw, k_raw, v_raw, out)
+    cache.check()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step(q_raw, k_raw, v_raw, out)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph, agraph = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step(q_raw, k_raw, v_raw, out)
+    with torch.cuda.graph(agraph):
+        step(q_raw, k_raw, v_raw, out, attn_only=True)
+    graph.replay()
+    clocks = ClockSampler(rt.local)
+    clocks.start()
+    time.sleep(0.3)
+    ms = rt.max(rt.timed(graph.replay, args.steps))
+    clk = clocks.stop()
+    agraph.replay()
+    attn_ms = rt.timed(agraph.replay, args.steps) / L
+    cache.check()
+
+    h = [pinned_like(torch, t, 5 + i) for i, t in enumerate((q_raw, k_raw, v_raw))]
+    h_o = torch.empty(out.shape).pin_memory()
+    dq, dk, dv = (torch.empty_like(t) for t in (q_raw, k_raw, v_raw))
+    d_o = torch.empty_like(out)
+
+    def e2e_step():
+        dq.copy_(h[0], non_blocking=True)
+        dk.copy_(h[1], non_blocking=True)
+        dv.copy_(h[2], non_blocking=True)
+        step(dq, dk, dv, d_o)
+        h_o.copy_(d_o, non_blocking=True)
+
+    e2e_step()
+    e2e_ms = rt.max(rt.timed(e2e_step, max(1, args.steps // 4)))
+    cache.check()
+    del graph, agraph
+    metric, unit, amount, div = step_work(cfg)
+    flops_layer = prefill_flops(cfg)
+    # nominal FP32 CUDA-core peak (no measured FP32 figure exists for this pool)
+    sm_count = torch.cuda.get_device_properties(rt.dev).multi_processor_count
+    peak = sm_count * 128 * 2 * 1.965e9 / 1e12
+    if rt.rank == 0:
+        value = amount * rt.world / (ms * 1e-3) / div
+        line = {
+            "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": rt.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) q/k/v generated on device)",
+            "config": {"workload": f"prefill: {cfg['desc']}", "layers": L, "nq": nq, "nkv": nkv,
+                       "head_dim": d, "prompt": M, "window": window,
+                       "parallelism": f"replicas x{rt.world}",
+                       "l2": "K/V of a layer (33.5 MB) stays in L2 across query blocks"},
+            "tok_per_s": round(M * rt.world * 1000.0 / ms, 1),
+            "e2e": {"value": round(amount * rt.world / (e2e_ms * 1e-3) / div, 2), "unit": unit,
+                    "h2d_bytes_per_step": int(4 * (q_raw.numel() + k_raw.numel() + v_raw.numel())),
+                    "d2h_bytes_per_step": int(4 * out.numel()), "ms_per_step": round(e2e_ms, 3)},
+            "gpu_launches": 2 * L * args.steps,
+            "roofline": {"bound": "fp32", "achieved": round(flops_layer / (attn_ms * 1e-3) / 1e12, 2),
+                         "peak": round(peak, 1), "unit": "TFLOP/s",
+                         "frac": round(flops_layer / (attn_ms * 1e-3) / 1e12 / peak, 4),
+                         "traffic": None, "kernel": "gqa_prefill_kernel<128>",
+                         "peak_source": "nominal FP32 CUDA-core peak (SMs x 128 lanes x 2 x "
+                                        "1965 MHz); no measured FP32 figure",
+                         "flops_per_launch": flops_layer, "avg_launch_ms": round(attn_ms, 4)},
+            "clocks": clk,
+            "path": "molot_attn_append_rope_tokens + molot_attn_prefill per layer",
+        }
+        if rt.world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_sample(cfg)
+        print(json.dumps(line), flush=True)
+    cache.close()
+    rt.close()
+    return 0
+
+
 def fill_normal(torch, dst, template):
     """Fill a device tensor with N(0,1) values by tiling a seeded template
     (generating tens of GB of normals directly takes too long)."""
@@ -884,6 +1033,8 @@ def main(argv=None):
         return run_single(args, cfg)
     if cfg["kind"] == "gemma":
         return run_gemma(args, cfg)
+    if cfg["kind"] == "prefill":
+        return run_prefill(args, cfg)
     return run_paged(args, cfg)
 
 
