@@ -7,12 +7,16 @@
 // One CTA = one kv head x 64 query rows (kPrefillRows / G positions, all G
 // query heads of the kv head: each K/V row staged in shared memory serves
 // every grouped head).  FP32 on the CUDA cores -- the reference's contract is
-// FP32 to 1e-5 -- flash-attention style: key tiles of BN slots stream through
-// a two-stage shared-memory ring (one TMA bulk copy per K or V row, rows
-// padded by 4 floats so the column reads of K are bank-conflict free); per
-// tile S = Q K^T in registers (4 rows x BN/16 keys per thread), an online
-// softmax in base 2, P to shared memory, O += P V in registers (4 rows x D/16
-// dims per thread).  Grid: (query blocks, nkv), the longest (latest) query
+// FP32 to 1e-5 -- flash-attention style: a producer warp streams key tiles of
+// BN slots through a two-stage shared-memory ring (one TMA bulk copy per K or
+// V row, rows padded by 4 floats so the column reads of K are bank-conflict
+// free; full/empty mbarriers per stage); the 8 consumer warps each own 8
+// query rows (two groups of 16 lanes, 4 rows each): per tile S = Q K^T in
+// registers (4 rows x BN/16 keys per thread), an online softmax in base 2, P
+// to the warp's own rows of shared memory, O += P V in registers (4 rows x
+// D/16 dims per thread).  No CTA-wide barrier runs inside the key loop: a
+// warp only reads P it wrote itself, and stages are recycled through the
+// empty barriers.  Grid: (query blocks, nkv), the longest (latest) query
 // blocks first.
 #pragma once
 
@@ -25,7 +29,8 @@
 
 namespace molot {
 
-constexpr int kPrefillThreads = 256;  // 16 x 16: ty owns 4 rows, tx a column set
+constexpr int kPrefillConsumers = 256;  // 16 x 16: ty owns 4 rows, tx a column set
+constexpr int kPrefillThreads = kPrefillConsumers + 32;  // + one producer warp
 constexpr int kPrefillRows = 64;      // query rows (position, head) per CTA
 
 template <int D>
@@ -37,7 +42,7 @@ struct PrefillTile {
   static constexpr int kQ = kPrefillRows * LD * 4;
   static constexpr int kKV = BN * LD * 4;  // one K or V tile
   static constexpr int kP = kPrefillRows * PLD * 4;
-  static constexpr int kBars = 3 * 8;
+  static constexpr int kBars = 5 * 8;  // full[2], empty[2], q
   static constexpr int kTotal = kQ + 4 * kKV + kP + kBars + 16;
   static_assert(kTotal <= 227 * 1024, "prefill CTA exceeds the shared-memory limit");
   static_assert(D % 64 == 0, "head dim must be a multiple of 64");
@@ -77,9 +82,10 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   float* Qs = reinterpret_cast<float*>(smem);
   float* KVs = reinterpret_cast<float*>(smem + TP::kQ);  // [stage][K,V][BN][LD]
   float* Ps = reinterpret_cast<float*>(smem + TP::kQ + 4 * TP::kKV);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TP::kQ + 4 * TP::kKV + TP::kP);
-  uint64_t* q_bar = bars + 2;
-  volatile int* abort_sm = reinterpret_cast<volatile int*>(bars + 3);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TP::kQ + 4 * TP::kKV + TP::kP);
+  uint64_t* empty = full + 2;
+  uint64_t* q_bar = full + 4;
+  volatile int* abort_sm = reinterpret_cast<volatile int*>(full + 5);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -89,8 +95,10 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   const int G = a.G;
 
   if (tid == 0) {
-    ptx::mbar_init(bars + 0, 1);
-    ptx::mbar_init(bars + 1, 1);
+    ptx::mbar_init(full + 0, 1);
+    ptx::mbar_init(full + 1, 1);
+    ptx::mbar_init(empty + 0, kPrefillConsumers / 32);
+    ptx::mbar_init(empty + 1, kPrefillConsumers / 32);
     ptx::mbar_init(q_bar, 1);
     *abort_sm = 0;
     ptx::fence_mbar_init();
@@ -114,23 +122,9 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   const int ntiles = t_hi > t_lo ? (t_hi - t_lo + BN - 1) / BN : 0;
   const int valid_rows = (m_end - m_first) * G;
 
-  // ---- stage Q (one bulk copy per valid row) and the first key tile
-  const uint64_t pol = ptx::policy_evict_first();
-  auto issue_tile = [&](int i) {  // warp 0 only
-    const int stage = i & 1;
-    const int ts = t_lo + i * BN;
-    const int rows = min(BN, t_hi - ts);
-    float* Kd = KVs + (size_t)(stage * 2) * BN * LD;
-    float* Vd = Kd + (size_t)BN * LD;
-    if (lane == 0) ptx::mbar_arrive_expect_tx(bars + stage, (uint32_t)rows * D * 4u * 2u);
-    __syncwarp();
-    for (int c = lane; c < rows; c += 32) {
-      const long long off = (long long)(ts + c) * a.stride_t + (long long)g * a.stride_h;
-      ptx::bulk_g2s(Kd + (size_t)c * LD, a.K + off, D * 4u, bars + stage, pol);
-      ptx::bulk_g2s(Vd + (size_t)c * LD, a.V + off, D * 4u, bars + stage, pol);
-    }
-  };
-  if (warp == 0) {
+  if (warp == kPrefillConsumers / 32) {
+    // ---- producer warp: Q once, then the key tiles through the ring
+    const uint64_t pol = ptx::policy_evict_first();
     if (lane == 0) ptx::mbar_arrive_expect_tx(q_bar, (uint32_t)valid_rows * D * 4u);
     __syncwarp();
     for (int r = lane; r < valid_rows; r += 32) {
@@ -138,7 +132,28 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       ptx::bulk_g2s(Qs + (size_t)r * LD, a.Q + (long long)m * a.q_tstride + (long long)h * D,
                     D * 4u, q_bar, pol);
     }
-    if (ntiles > 0) issue_tile(0);
+    for (int i = 0; i < ntiles; ++i) {
+      const int stage = i & 1;
+      if (i >= 2 && !ptx::mbar_wait_bounded(empty + stage, ((i >> 1) - 1) & 1, a.timeout_ns)) {
+        if (lane == 0) {  // the results of this launch are void: say so now
+          *abort_sm = 1;
+          atomicCAS(a.status, 0, 3);
+        }
+      }
+      __syncwarp();
+      const int ts = t_lo + i * BN;
+      const int rows = min(BN, t_hi - ts);
+      float* Kd = KVs + (size_t)(stage * 2) * BN * LD;
+      float* Vd = Kd + (size_t)BN * LD;
+      if (lane == 0) ptx::mbar_arrive_expect_tx(full + stage, (uint32_t)rows * D * 4u * 2u);
+      __syncwarp();
+      for (int c = lane; c < rows; c += 32) {
+        const long long off = (long long)(ts + c) * a.stride_t + (long long)g * a.stride_h;
+        ptx::bulk_g2s(Kd + (size_t)c * LD, a.K + off, D * 4u, full + stage, pol);
+        ptx::bulk_g2s(Vd + (size_t)c * LD, a.V + off, D * 4u, full + stage, pol);
+      }
+    }
+    return;
   }
 
   // Per-row state (4 rows per thread, replicated over the 16 tx lanes).
@@ -157,17 +172,14 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
 #pragma unroll
     for (int j = 0; j < DJ * 4; ++j) o[ii][j] = 0.f;
   }
-  if (!ptx::mbar_wait_bounded(q_bar, 0, a.timeout_ns)) *abort_sm = 1;
+  bool ok_waits = ptx::mbar_wait_bounded(q_bar, 0, a.timeout_ns);
 
   const float sl2 = a.scale * kLog2e;
   for (int i = 0; i < ntiles; ++i) {
     const int stage = i & 1;
-    // The other stage was last read by tile i-1, finished before the barrier
-    // that closed that iteration.
-    if (warp == 0 && i + 1 < ntiles && !*abort_sm) issue_tile(i + 1);
-    if (!ptx::mbar_wait_bounded(bars + stage, (i >> 1) & 1, a.timeout_ns)) *abort_sm = 1;
-    __syncthreads();
-    if (*abort_sm) break;
+    // A timed-out wait leaves this thread computing on stale data; the
+    // results are then discarded (status word) and every loop still ends.
+    ok_waits &= ptx::mbar_wait_bounded(full + stage, (i >> 1) & 1, a.timeout_ns);
     const float* Kt = KVs + (size_t)(stage * 2) * BN * LD;
     const float* Vt = Kt + (size_t)BN * LD;
     const int ts = t_lo + i * BN;
@@ -229,7 +241,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
 #pragma unroll
       for (int j = 0; j < DJ * 4; ++j) o[ii][j] *= alpha;
     }
-    __syncthreads();
+    __syncwarp();  // P rows ty*4.. are written and read by this warp only
 
     // ---- O += P V over the kc valid keys of the tile
     const float* pb = Ps + (size_t)(ty * 4) * PLD;
@@ -270,10 +282,11 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
         }
       }
     }
-    __syncthreads();  // P and this stage are free again
+    __syncwarp();  // this warp's P rows may be rewritten by the next tile
+    if (lane == 0) ptx::mbar_arrive(empty + stage);
   }
-  if (*abort_sm) {
-    if (tid == 0) atomicCAS(a.status, 0, 3);
+  if (!ok_waits || *abort_sm) {
+    atomicCAS(a.status, 0, 3);
     return;
   }
 
