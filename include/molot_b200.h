@@ -149,15 +149,34 @@ int molot_norm_rope_append_dev(const float* q, const float* k, const float* v, f
  * ---------------------------------------------------------------------- */
 typedef struct molot_kv_cache molot_kv_cache;
 
+/* KV element types of the handle. */
+enum molot_kv_dtype {
+  MOLOT_KV_F32 = 0, /* the reference's format (bit-exact QK scores) */
+  MOLOT_KV_BF16 = 1 /* half the bytes; the reference specifies but does not
+                       implement it: results match the reference run on the
+                       bf16-rounded cache */
+};
+
 int molot_kv_create(int n_layers, int nkv, int hd, int cap, molot_kv_cache** out);
+/* molot_kv_create with a storage type.  With MOLOT_KV_BF16 every row that
+ * enters the cache (write, append, step, prefill prologue) is rounded to
+ * bf16 (nearest even); attention math stays FP32. */
+int molot_kv_create_ex(int n_layers, int nkv, int hd, int cap, int kv_dtype,
+                       molot_kv_cache** out);
+/* MOLOT_KV_F32 or MOLOT_KV_BF16 (or a negative status). */
+int molot_kv_dtype(const molot_kv_cache* kv);
 void molot_kv_destroy(molot_kv_cache* kv);
 int molot_kv_length(const molot_kv_cache* kv, int layer);
 int molot_kv_set_length(molot_kv_cache* kv, int layer, int n);
+/* Device base of a layer's K and V ([nkv][cap][hd]); the elements are
+ * uint16 bf16 bit patterns for MOLOT_KV_BF16 handles despite the type. */
 int molot_kv_layer_data(molot_kv_cache* kv, int layer, float** k, float** v);
 
-/* Copies nrows rows of K and V (each [nrows][nkv*hd], host or device
+/* Copies nrows rows of K and V (each [nrows][nkv*hd] FP32, host or device
  * memory) into slots [slot0, slot0+nrows) of `layer`, stream-ordered; the
- * bulk write a prefill performs (forward.h:370-392).  Does not change n. */
+ * bulk write a prefill performs (forward.h:370-392).  Does not change n.
+ * BF16 handles convert on the device (host rows are staged in a buffer the
+ * handle owns: order such writes on one stream). */
 int molot_kv_write(molot_kv_cache* kv, int layer, int slot0, int nrows, const float* k,
                    const float* v, void* stream);
 

@@ -84,8 +84,9 @@ inline void norm_rope_q_dev(const float* q, float* q_out, const float* q_norm, f
 // cudaStream_t, nullptr = legacy default stream).
 class KVCache {
  public:
-  KVCache(int n_layers, int nkv, int hd, int cap) : nkv_(nkv), hd_(hd), cap_(cap) {
-    check(molot_kv_create(n_layers, nkv, hd, cap, &h_));
+  KVCache(int n_layers, int nkv, int hd, int cap, int kv_dtype = MOLOT_KV_F32)
+      : nkv_(nkv), hd_(hd), cap_(cap) {
+    check(molot_kv_create_ex(n_layers, nkv, hd, cap, kv_dtype, &h_));
   }
   ~KVCache() { molot_kv_destroy(h_); }
   KVCache(const KVCache&) = delete;

@@ -40,6 +40,9 @@ ERR_UNSUPPORTED = -6
 ERR_TIMEOUT = -7
 ERR_NO_DEVICE = -8
 
+KV_F32 = 0   # molot_kv_dtype: the reference's FP32 cache
+KV_BF16 = 1  # BF16 storage (rounded on entry), FP32 math
+
 
 class MolotError(RuntimeError):
     """A non-zero status from the C ABI (the reference throws
@@ -85,6 +88,8 @@ _decl("molot_attn_decode_strided_dev", [_p, _p, _p, _p, _i, _i, _i, _i, _ll, _ll
 _decl("molot_norm_rope_append_dev",
       [_p, _p, _p, _p, _p, _p, _i, _f, _p, _i, _p, _p, _i, _i, _i, _i, _p])
 _decl("molot_kv_create", [_i, _i, _i, _i, _pp])
+_decl("molot_kv_create_ex", [_i, _i, _i, _i, _i, _pp])
+_decl("molot_kv_dtype", [_p])
 _decl("molot_kv_destroy", [_p], None)
 _decl("molot_kv_length", [_p, _i])
 _decl("molot_kv_set_length", [_p, _i, _i])
@@ -287,11 +292,15 @@ def norm_rope_append(q, k, v, q_out, q_norm, k_norm, v_norm, eps, freq, pos, kc,
 class KVCache:
     """HBM-resident per-layer KV cache (replaces forward.h's Runner::KVC)."""
 
-    def __init__(self, n_layers: int, nkv: int, hd: int, cap: int):
+    def __init__(self, n_layers: int, nkv: int, hd: int, cap: int, dtype: str = "f32"):
+        if dtype not in ("f32", "bf16"):
+            raise ValueError("dtype must be 'f32' or 'bf16'")
         h = ctypes.c_void_p()
-        check(_lib.molot_kv_create(n_layers, nkv, hd, cap, ctypes.byref(h)))
+        check(_lib.molot_kv_create_ex(n_layers, nkv, hd, cap,
+                                      KV_BF16 if dtype == "bf16" else KV_F32, ctypes.byref(h)))
         self._h = h
         self.n_layers, self.nkv, self.hd, self.cap = n_layers, nkv, hd, cap
+        self.dtype = dtype
 
     def close(self) -> None:
         if getattr(self, "_h", None):
@@ -325,10 +334,13 @@ class KVCache:
 
     def layer_tensors(self, layer: int):
         """(K, V) torch views [nkv][cap][hd] (head-major) of the layer's
-        device memory."""
+        device memory: float32, or bfloat16 for a bf16 cache."""
         import torch
         kp, vp = self.layer_ptrs(layer)
         shape = (self.nkv, self.cap, self.hd)
+        if self.dtype == "bf16":
+            return (torch.as_tensor(_CudaArray(kp, shape, "<i2"), device="cuda").view(torch.bfloat16),
+                    torch.as_tensor(_CudaArray(vp, shape, "<i2"), device="cuda").view(torch.bfloat16))
         return (torch.as_tensor(_CudaArray(kp, shape), device="cuda"),
                 torch.as_tensor(_CudaArray(vp, shape), device="cuda"))
 

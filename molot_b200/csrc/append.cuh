@@ -10,6 +10,7 @@
 // rounded 1/sqrt (the reference's -ffast-math build may use an rsqrt
 // estimate there, an ulp-level difference).
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -42,9 +43,10 @@ struct AppendArgs {
   int tok_step;
   const int* seq_pos;                       // [B] or null
   const int* seq_slot;                      // [B] or null
-  // Cache addressing (same conventions as DecodeArgs).
-  float* K;
-  float* V;
+  // Cache addressing (same conventions as DecodeArgs; elements of the
+  // kernel's cache type).
+  void* K;
+  void* V;
   long long kv_bstride, stride_t, stride_h;
   const int* block_table;
   int bt_stride, page_size;
@@ -67,8 +69,16 @@ __device__ __forceinline__ float warp_sumsq16(const float* x, int n, int lane) {
   return acc;
 }
 
-__device__ __forceinline__ float* cache_row(const AppendArgs& a, float* base, int b, int g,
-                                            int slot, int D) {
+// The cache's storage of a computed value: FP32 as is, BF16 rounded to
+// nearest even.
+__device__ __forceinline__ void cache_store(float* p, float x) { *p = x; }
+__device__ __forceinline__ void cache_store(__nv_bfloat16* p, float x) {
+  *p = __float2bfloat16_rn(x);
+}
+
+template <class CT>
+__device__ __forceinline__ CT* cache_row(const AppendArgs& a, CT* base, int b, int g, int slot,
+                                         int D) {
   if (a.block_table) {
     const int p = a.block_table[(long long)b * a.bt_stride + slot / a.page_size];
     return base + (long long)p * a.page_stride + (long long)g * a.page_hstride +
@@ -78,7 +88,7 @@ __device__ __forceinline__ float* cache_row(const AppendArgs& a, float* base, in
          (long long)g * a.stride_h;
 }
 
-template <int D>
+template <int D, class CT = float>
 __global__ void __launch_bounds__(kAppendWarps * 32)
     norm_rope_append_kernel(const __grid_constant__ AppendArgs a) {
   static_assert(D % 16 == 0, "head dim must be a multiple of 16");
@@ -102,8 +112,8 @@ __global__ void __launch_bounds__(kAppendWarps * 32)
                         : a.k_in + (long long)b * a.kv_in_bstride + (long long)g * D;
   const float* w = is_q ? a.q_norm : a.k_norm;
   const int slot = is_q ? 0 : (a.seq_slot ? a.seq_slot[b] : a.slot + b * a.tok_step);
-  float* dst = is_q ? a.q_out + (long long)b * a.qo_bstride + (long long)g * D
-                    : cache_row(a, a.K, b, g, slot, D);
+  float* qdst = is_q ? a.q_out + (long long)b * a.qo_bstride + (long long)g * D : nullptr;
+  CT* kdst = is_q ? nullptr : cache_row(a, static_cast<CT*>(a.K), b, g, slot, D);
 
   float inv = 1.f;
   if (w) {
@@ -125,8 +135,13 @@ __global__ void __launch_bounds__(kAppendWarps * 32)
       y0 = z0;
       y1 = z1;
     }
-    dst[i] = y0;
-    dst[i + H] = y1;
+    if (is_q) {
+      qdst[i] = y0;
+      qdst[i + H] = y1;
+    } else {
+      cache_store(kdst + i, y0);
+      cache_store(kdst + i + H, y1);
+    }
   }
 
   if (!is_q) {
@@ -137,9 +152,31 @@ __global__ void __launch_bounds__(kAppendWarps * 32)
       const float ss = warp_sumsq16(vin, nv, lane);
       vinv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)nv), a.eps)));
     }
-    float* vdst = cache_row(a, a.V, b, g, slot, D);
+    CT* vdst = cache_row(a, static_cast<CT*>(a.V), b, g, slot, D);
     const float* vh = vin + (long long)g * D;
-    for (int i = lane; i < D; i += 32) vdst[i] = a.v_norm ? __fmul_rn(vh[i], vinv) : vh[i];
+    for (int i = lane; i < D; i += 32)
+      cache_store(vdst + i, a.v_norm ? __fmul_rn(vh[i], vinv) : vh[i]);
+  }
+}
+
+}  // namespace molot
+
+namespace molot {
+
+// Bulk write of nrows [nkv*D] FP32 rows (k and v, row pitch nkv*D) into
+// slots slot0.. of a head-major cache (slot t of head g at base +
+// g*stride_h + t*D) in the cache's element type; one CTA per (row, head).
+template <class CT>
+__global__ void kv_rows_to_cache_kernel(const float* __restrict__ k, const float* __restrict__ v,
+                                        CT* kc, CT* vc, int slot0, int nkv, int D,
+                                        long long stride_h) {
+  const int r = blockIdx.x, g = blockIdx.y;
+  const float* ks = k + ((long long)r * nkv + g) * D;
+  const float* vs = v + ((long long)r * nkv + g) * D;
+  const long long off = (long long)g * stride_h + (long long)(slot0 + r) * D;
+  for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    cache_store(kc + off + j, ks[j]);
+    cache_store(vc + off + j, vs[j]);
   }
 }
 

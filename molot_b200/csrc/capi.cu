@@ -158,9 +158,47 @@ struct KernelRef {
   int smem = 0;
 };
 
-template <int D, int GS, int HS>
+template <int D, int GS, int HS, class KT = float>
 KernelRef decode_ref() {
-  return {reinterpret_cast<const void*>(&gqa_decode_kernel<D, GS, HS>), DecodeSmem<D, GS>::kTotal};
+  return {reinterpret_cast<const void*>(&gqa_decode_kernel<D, GS, HS, KT>),
+          DecodeSmem<D, GS, KT>::kTotal};
+}
+
+// BF16 caches (the KV handle's storage option): the same group splits.
+bool pick_decode_bf16(int D, int G, KernelRef* k) {
+  using B = __nv_bfloat16;
+  switch (D) {
+    case 64:
+      switch (G) {
+        case 1: *k = decode_ref<64, 1, 1, B>(); return true;
+        case 2: *k = decode_ref<64, 2, 1, B>(); return true;
+        case 4: *k = decode_ref<64, 4, 1, B>(); return true;
+        case 8: *k = decode_ref<64, 8, 1, B>(); return true;
+        case 16: *k = decode_ref<64, 8, 2, B>(); return true;
+        case 32: *k = decode_ref<64, 8, 4, B>(); return true;
+      }
+      return false;
+    case 128:
+      switch (G) {
+        case 1: *k = decode_ref<128, 1, 1, B>(); return true;
+        case 2: *k = decode_ref<128, 2, 1, B>(); return true;
+        case 4: *k = decode_ref<128, 4, 1, B>(); return true;
+        case 8: *k = decode_ref<128, 4, 2, B>(); return true;
+        case 16: *k = decode_ref<128, 4, 4, B>(); return true;
+        case 32: *k = decode_ref<128, 4, 8, B>(); return true;
+      }
+      return false;
+    case 256:
+      switch (G) {
+        case 1: *k = decode_ref<256, 1, 1, B>(); return true;
+        case 2: *k = decode_ref<256, 2, 1, B>(); return true;
+        case 4: *k = decode_ref<256, 2, 2, B>(); return true;
+        case 8: *k = decode_ref<256, 2, 4, B>(); return true;
+        case 16: *k = decode_ref<256, 2, 8, B>(); return true;
+      }
+      return false;
+  }
+  return false;
 }
 
 bool pick_decode(int D, int G, KernelRef* k) {
@@ -198,11 +236,18 @@ bool pick_decode(int D, int G, KernelRef* k) {
   return false;
 }
 
-const void* pick_append(int D) {
+const void* pick_append(int D, bool bf16 = false) {
+  using B = __nv_bfloat16;
   switch (D) {
-    case 64: return reinterpret_cast<const void*>(&norm_rope_append_kernel<64>);
-    case 128: return reinterpret_cast<const void*>(&norm_rope_append_kernel<128>);
-    case 256: return reinterpret_cast<const void*>(&norm_rope_append_kernel<256>);
+    case 64:
+      return bf16 ? reinterpret_cast<const void*>(&norm_rope_append_kernel<64, B>)
+                  : reinterpret_cast<const void*>(&norm_rope_append_kernel<64>);
+    case 128:
+      return bf16 ? reinterpret_cast<const void*>(&norm_rope_append_kernel<128, B>)
+                  : reinterpret_cast<const void*>(&norm_rope_append_kernel<128>);
+    case 256:
+      return bf16 ? reinterpret_cast<const void*>(&norm_rope_append_kernel<256, B>)
+                  : reinterpret_cast<const void*>(&norm_rope_append_kernel<256>);
   }
   return nullptr;
 }
@@ -244,10 +289,10 @@ int window_start(int pos_cur, int window) {
   return (window > 0 && pos_cur - window + 1 > 0) ? pos_cur - window + 1 : 0;
 }
 
-int check_shape(int nq, int nkv, int d, KernelRef* k) {
+int check_shape(int nq, int nkv, int d, KernelRef* k, bool bf16 = false) {
   if (nq <= 0 || nkv <= 0 || d <= 0) return fail(MOLOT_ERR_INVALID, "nq, nkv and d must be > 0");
   if (nq % nkv) return fail(MOLOT_ERR_INVALID, "nq must be a multiple of nkv");
-  if (!pick_decode(d, nq / nkv, k))
+  if (!(bf16 ? pick_decode_bf16(d, nq / nkv, k) : pick_decode(d, nq / nkv, k)))
     return fail(MOLOT_ERR_UNSUPPORTED, "head_dim / group size combination not built: d=" +
                                            std::to_string(d) +
                                            " group=" + std::to_string(nq / nkv));
@@ -262,12 +307,13 @@ int launch_decode(const KernelRef& k, DecodeArgs& a, cudaStream_t st) {
 // Single-sequence decode over a strided contiguous cache.  prefetch_old_rows:
 // see DecodeArgs (set only when the preceding launch is the library's append
 // of slot n-1).
-int decode_uniform(Workspace& ws, const float* Q, float* O, const float* K, const float* V,
+int decode_uniform(Workspace& ws, const float* Q, float* O, const void* K, const void* V,
                    int nq, int nkv, int n, int d, long long stride_t, long long stride_h,
                    float scale, int pos_cur, int window, cudaStream_t st,
-                   bool prefetch_old_rows = false, const DecodeArgs* fused = nullptr) {
+                   bool prefetch_old_rows = false, const DecodeArgs* fused = nullptr,
+                   bool bf16 = false) {
   KernelRef k;
-  int rc = check_shape(nq, nkv, d, &k);
+  int rc = check_shape(nq, nkv, d, &k, bf16);
   if (rc) return rc;
   if (!Q || !O || !K || !V) return fail(MOLOT_ERR_INVALID, "null pointer");
   if (n < 0) return fail(MOLOT_ERR_INVALID, "n must be >= 0");
@@ -331,8 +377,8 @@ int decode_uniform(Workspace& ws, const float* Q, float* O, const float* K, cons
   return launch_decode(k, a, st);
 }
 
-int append_launch(const AppendArgs& a, int d, int B, cudaStream_t st) {
-  const void* fn = pick_append(d);
+int append_launch(const AppendArgs& a, int d, int B, cudaStream_t st, bool bf16 = false) {
+  const void* fn = pick_append(d, bf16);
   if (!fn) return fail(MOLOT_ERR_UNSUPPORTED, "head_dim not built: " + std::to_string(d));
   const int heads = a.nq + a.nkv;
   AppendArgs copy = a;
@@ -414,14 +460,17 @@ int host_decode(const float* Q, const float* K, const float* V, float* O, int nq
 
 // ------------------------------------------------------------- prefill
 
-bool pick_prefill(int D, KernelRef* k) {
+template <int D, class KT>
+KernelRef prefill_ref() {
+  return {reinterpret_cast<const void*>(&gqa_prefill_kernel<D, KT>), PrefillTile<D, KT>::kTotal};
+}
+
+bool pick_prefill(int D, KernelRef* k, bool bf16 = false) {
+  using B = __nv_bfloat16;
   switch (D) {
-    case 64: *k = {reinterpret_cast<const void*>(&gqa_prefill_kernel<64>), PrefillTile<64>::kTotal};
-      return true;
-    case 128: *k = {reinterpret_cast<const void*>(&gqa_prefill_kernel<128>), PrefillTile<128>::kTotal};
-      return true;
-    case 256: *k = {reinterpret_cast<const void*>(&gqa_prefill_kernel<256>), PrefillTile<256>::kTotal};
-      return true;
+    case 64: *k = bf16 ? prefill_ref<64, B>() : prefill_ref<64, float>(); return true;
+    case 128: *k = bf16 ? prefill_ref<128, B>() : prefill_ref<128, float>(); return true;
+    case 256: *k = bf16 ? prefill_ref<256, B>() : prefill_ref<256, float>(); return true;
   }
   return false;
 }
@@ -429,9 +478,9 @@ bool pick_prefill(int D, KernelRef* k) {
 // gemm.h:409-446 on device buffers: Q/O [M][nq][d] (token stride q_tstride /
 // o_tstride floats), slot t of kv head g at K + t*stride_t + g*stride_h.
 int prefill_strided(Workspace& ws, const float* Q, long long q_tstride, float* O,
-                    long long o_tstride, const float* K, const float* V, int nq, int nkv, int M,
+                    long long o_tstride, const void* K, const void* V, int nq, int nkv, int M,
                     int N, int d, long long stride_t, long long stride_h, float scale, int pos0,
-                    int window, cudaStream_t st) {
+                    int window, cudaStream_t st, bool bf16 = false) {
   if (!Q || !O || !K || !V) return fail(MOLOT_ERR_INVALID, "null pointer");
   if (nq <= 0 || nkv <= 0 || nq % nkv || M < 0 || N < 0 || pos0 < 0)
     return fail(MOLOT_ERR_INVALID, "bad sizes (nq must be a multiple of nkv)");
@@ -439,7 +488,7 @@ int prefill_strided(Workspace& ws, const float* Q, long long q_tstride, float* O
   if (G > kPrefillRows || kPrefillRows % G)
     return fail(MOLOT_ERR_UNSUPPORTED, "prefill group size must divide 64");
   KernelRef k;
-  if (!pick_prefill(d, &k)) return fail(MOLOT_ERR_UNSUPPORTED, "prefill head_dim not built");
+  if (!pick_prefill(d, &k, bf16)) return fail(MOLOT_ERR_UNSUPPORTED, "prefill head_dim not built");
   if (!aligned16(Q) || !aligned16(O) || !aligned16(K) || !aligned16(V) || (q_tstride & 3) ||
       (o_tstride & 3) || (stride_t & 3) || (stride_h & 3))
     return fail(MOLOT_ERR_INVALID, "buffers must be 16-byte aligned with strides multiple of 4");
@@ -518,8 +567,13 @@ using namespace molot;
 struct molot_kv_cache {
   int device = -1;
   int n_layers = 0, nkv = 0, hd = 0, cap = 0;
-  size_t layer_floats = 0;  // per K (or V) of one layer, padded
-  float* base = nullptr;
+  int dtype = MOLOT_KV_F32;
+  size_t elem = 4;          // bytes per cache element
+  size_t layer_floats = 0;  // elements per K (or V) of one layer, padded
+  unsigned char* base = nullptr;
+  float* staging = nullptr;  // device copy of host rows for BF16 writes
+  size_t staging_cap = 0;    // floats
+  bool bf16() const { return dtype == MOLOT_KV_BF16; }
   std::vector<int> len;
   Workspace ws;
   // The handle's two most recent kernel launches on its stream (index 0 =
@@ -683,7 +737,8 @@ namespace {
 int append_strided(const float* q, const float* k, const float* v, float* q_out,
                    const float* q_norm, const float* k_norm, int v_norm, float eps,
                    const float* freq, int pos, float* kc, float* vc, int slot, int nq, int nkv,
-                   int d, long long stride_t, long long stride_h, cudaStream_t st) {
+                   int d, long long stride_t, long long stride_h, cudaStream_t st,
+                   bool bf16 = false) {
   // k, v, kc and vc all null: q only (a shared-KV layer's query, forward.h:554-558)
   const bool q_only = !k && !v && !kc && !vc;
   if (!q || !q_out || (!q_only && (!k || !v || !kc || !vc)))
@@ -707,7 +762,7 @@ int append_strided(const float* q, const float* k, const float* v, float* q_out,
   a.V = vc;
   a.stride_t = stride_t;
   a.stride_h = stride_h;
-  return append_launch(a, d, 1, st);
+  return append_launch(a, d, 1, st, bf16);
 }
 }  // namespace
 }  // namespace molot
@@ -723,10 +778,22 @@ int molot_norm_rope_append_dev(const float* q, const float* k, const float* v, f
 // ---------------------------------------------------------------- KV cache handle
 
 int molot_kv_create(int n_layers, int nkv, int hd, int cap, molot_kv_cache** out) {
+  return molot_kv_create_ex(n_layers, nkv, hd, cap, MOLOT_KV_F32, out);
+}
+
+int molot_kv_dtype(const molot_kv_cache* kv) {
+  if (!kv) return fail(MOLOT_ERR_INVALID, "null handle");
+  return kv->dtype;
+}
+
+int molot_kv_create_ex(int n_layers, int nkv, int hd, int cap, int kv_dtype,
+                       molot_kv_cache** out) {
   if (!out) return fail(MOLOT_ERR_INVALID, "null out");
   *out = nullptr;
   if (n_layers <= 0 || nkv <= 0 || hd <= 0 || cap <= 0)
     return fail(MOLOT_ERR_INVALID, "sizes must be positive");
+  if (kv_dtype != MOLOT_KV_F32 && kv_dtype != MOLOT_KV_BF16)
+    return fail(MOLOT_ERR_INVALID, "kv_dtype must be MOLOT_KV_F32 or MOLOT_KV_BF16");
   if (!pick_append(hd)) return fail(MOLOT_ERR_UNSUPPORTED, "head_dim not built");
   int dev, rc;
   if ((rc = current_device(&dev))) return rc;
@@ -736,9 +803,11 @@ int molot_kv_create(int n_layers, int nkv, int hd, int cap, molot_kv_cache** out
   kv->nkv = nkv;
   kv->hd = hd;
   kv->cap = cap;
-  kv->layer_floats = ((size_t)cap * nkv * hd + 63) & ~size_t(63);  // 256-byte aligned layers
+  kv->dtype = kv_dtype;
+  kv->elem = kv_dtype == MOLOT_KV_BF16 ? 2 : 4;
+  kv->layer_floats = ((size_t)cap * nkv * hd + 127) & ~size_t(127);  // 256-byte aligned layers
   kv->len.assign(n_layers, 0);
-  cudaError_t e = cudaMalloc(&kv->base, kv->layer_floats * 2 * n_layers * sizeof(float));
+  cudaError_t e = cudaMalloc(&kv->base, kv->layer_floats * 2 * n_layers * kv->elem);
   if (e != cudaSuccess) {
     delete kv;
     return cuda_fail(e, "cudaMalloc(kv cache)");
@@ -754,6 +823,7 @@ void molot_kv_destroy(molot_kv_cache* kv) {
   cudaSetDevice(kv->device);
   cudaDeviceSynchronize();
   cudaFree(kv->base);
+  cudaFree(kv->staging);
   kv->ws.release();
   if (prev >= 0) cudaSetDevice(prev);
   delete kv;
@@ -773,8 +843,8 @@ int molot_kv_set_length(molot_kv_cache* kv, int layer, int n) {
 
 int molot_kv_layer_data(molot_kv_cache* kv, int layer, float** k, float** v) {
   if (!kv || layer < 0 || layer >= kv->n_layers) return fail(MOLOT_ERR_INVALID, "bad layer");
-  if (k) *k = kv->base + (size_t)(2 * layer) * kv->layer_floats;
-  if (v) *v = kv->base + (size_t)(2 * layer + 1) * kv->layer_floats;
+  if (k) *k = reinterpret_cast<float*>(kv->base + (size_t)(2 * layer) * kv->layer_floats * kv->elem);
+  if (v) *v = reinterpret_cast<float*>(kv->base + (size_t)(2 * layer + 1) * kv->layer_floats * kv->elem);
   return MOLOT_OK;
 }
 
@@ -787,6 +857,35 @@ int molot_kv_write(molot_kv_cache* kv, int layer, int slot0, int nrows, const fl
   kv->ordered();
   float *kc, *vc;
   molot_kv_layer_data(kv, layer, &kc, &vc);
+  if (kv->bf16()) {
+    // Rows are converted on the device; host rows are staged there first.
+    const size_t n = (size_t)nrows * kv->nkv * kv->hd;
+    cudaPointerAttributes pa{};
+    const bool dev_src = cudaPointerGetAttributes(&pa, k) == cudaSuccess &&
+                         (pa.type == cudaMemoryTypeDevice || pa.type == cudaMemoryTypeManaged);
+    cudaGetLastError();  // a host pointer may leave an error behind on older drivers
+    const float *ks = k, *vs = v;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (!dev_src) {
+      if (kv->staging_cap < 2 * n) {
+        MOLOT_CUDA(cudaStreamSynchronize(st));
+        cudaFree(kv->staging);
+        kv->staging = nullptr;
+        kv->staging_cap = 0;
+        MOLOT_CUDA(cudaMalloc(&kv->staging, 2 * n * sizeof(float)));
+        kv->staging_cap = 2 * n;
+      }
+      MOLOT_CUDA(cudaMemcpyAsync(kv->staging, k, n * 4, cudaMemcpyHostToDevice, st));
+      MOLOT_CUDA(cudaMemcpyAsync(kv->staging + n, v, n * 4, cudaMemcpyHostToDevice, st));
+      ks = kv->staging;
+      vs = kv->staging + n;
+    }
+    kv_rows_to_cache_kernel<__nv_bfloat16><<<dim3(nrows, kv->nkv), 128, 0, st>>>(
+        ks, vs, reinterpret_cast<__nv_bfloat16*>(kc), reinterpret_cast<__nv_bfloat16*>(vc), slot0,
+        kv->nkv, kv->hd, (long long)kv->cap * kv->hd);
+    MOLOT_CUDA(cudaGetLastError());
+    return MOLOT_OK;
+  }
   // [nrows][nkv*hd] rows in, [nkv][cap][hd] head-major cache out: one
   // strided copy per kv head.
   const size_t hd = kv->hd, src_pitch = (size_t)kv->nkv * hd * sizeof(float);
@@ -811,7 +910,7 @@ int molot_attn_append_rope(molot_kv_cache* kv, int layer, const float* q, const 
   molot_kv_layer_data(kv, layer, &kc, &vc);
   int rc = append_strided(q, k, v, q_out, q_norm, k_norm, v_norm, eps, freq, pos, kc, vc,
                           kv->len[layer], nq, kv->nkv, kv->hd, kv->hd, (long long)kv->cap * kv->hd,
-                          (cudaStream_t)stream);
+                          (cudaStream_t)stream, kv->bf16());
   if (rc) return rc;
   kv->len[layer]++;
   kv->record(molot_kv_cache::kAppend, layer);
@@ -829,7 +928,7 @@ int molot_attn_decode(molot_kv_cache* kv, int src_layer, const float* q, float* 
   const bool prefetch = kv->decode_may_prefetch(src_layer);
   int rc = decode_uniform(kv->ws, q, o, kc, vc, nq, kv->nkv, n, kv->hd, kv->hd,
                           (long long)kv->cap * kv->hd, scale, pos_cur, window,
-                          (cudaStream_t)stream, prefetch);
+                          (cudaStream_t)stream, prefetch, nullptr, kv->bf16());
   if (rc == MOLOT_OK) kv->record(molot_kv_cache::kDecode, -1);
   return rc;
 }
@@ -860,7 +959,7 @@ int molot_attn_step(molot_kv_cache* kv, int layer, const float* q, const float* 
     // The rotated q goes to o, which the memset then clears.
     int rc = append_strided(q, k, v, o, q_norm, k_norm, v_norm, eps, freq, pos, kc, vc,
                             n - 1, nq, kv->nkv, kv->hd, kv->hd, (long long)kv->cap * kv->hd,
-                            (cudaStream_t)stream);
+                            (cudaStream_t)stream, kv->bf16());
     if (rc) return rc;
     MOLOT_CUDA(cudaMemsetAsync(o, 0, sizeof(float) * (size_t)nq * kv->hd, (cudaStream_t)stream));
     kv->len[layer] = n;
@@ -870,7 +969,7 @@ int molot_attn_step(molot_kv_cache* kv, int layer, const float* q, const float* 
   const bool prefetch = kv->step_may_prefetch(layer);
   int rc = decode_uniform(kv->ws, q, o, kc, vc, nq, kv->nkv, n, kv->hd, kv->hd,
                           (long long)kv->cap * kv->hd, scale, pos, window, (cudaStream_t)stream,
-                          prefetch, &f);
+                          prefetch, &f, kv->bf16());
   if (rc) return rc;
   kv->len[layer] = n;
   kv->record(molot_kv_cache::kDecode, layer);
@@ -916,7 +1015,7 @@ int molot_attn_append_rope_tokens(molot_kv_cache* kv, int layer, const float* q,
   a.kv_bstride = 0;
   a.stride_t = kv->hd;
   a.stride_h = (long long)kv->cap * kv->hd;
-  int rc = append_launch(a, kv->hd, M, (cudaStream_t)stream);
+  int rc = append_launch(a, kv->hd, M, (cudaStream_t)stream, kv->bf16());
   if (rc) return rc;
   kv->len[layer] = n + M;
   kv->record(molot_kv_cache::kAppend, layer);
@@ -935,7 +1034,7 @@ int molot_attn_prefill(molot_kv_cache* kv, int src_layer, const float* q, float*
   const int hd = kv->hd;
   int rc = prefill_strided(kv->ws, q, (long long)nq * hd, o, (long long)nq * hd, kc, vc, nq,
                            kv->nkv, M, kv->len[src_layer], hd, hd, (long long)kv->cap * hd,
-                           scale, pos0, window, (cudaStream_t)stream);
+                           scale, pos0, window, (cudaStream_t)stream, kv->bf16());
   if (rc) return rc;
   kv->record(molot_kv_cache::kDecode, -1);  // releases its successor after its own wait
   return MOLOT_OK;

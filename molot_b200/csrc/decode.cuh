@@ -29,6 +29,7 @@
 //   and CTAs are merged with the usual (max, sum) rescaling.
 //   The same lanes then accumulate p * V for their dimensions.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <math_constants.h>
 
@@ -54,6 +55,62 @@ constexpr int kQuarterPadBytes = 32;
 // this the build reads them from global memory.
 constexpr int kMaxStagedV = 8 * kConsumerWarps * 32;
 
+// KV element types of the cache.  FP32 keeps the reference's bit-exact
+// score order: lane l8 of a row group owns dims {16m+l8, 16m+l8+8}, the
+// reference's accumulator lanes.  BF16 (a storage format the reference
+// specifies but does not implement) packs a lane's pair of dims into one
+// 32-bit word, {16m+2*l8, 16m+2*l8+1}; its parity is against the reference
+// run on the bf16-rounded cache, where only rounding-level order effects
+// remain.
+template <class KT>
+struct KvElem;
+template <>
+struct KvElem<float> {
+  static constexpr int kBytes = 4;
+  __device__ __forceinline__ static int dim(int i, int l8) {
+    return 16 * (i >> 1) + l8 + 8 * (i & 1);
+  }
+  __device__ __forceinline__ static void load2(const float* row, int m, int l8, float& x0,
+                                               float& x1) {
+    x0 = row[16 * m + l8];
+    x1 = row[16 * m + l8 + 8];
+  }
+  __device__ __forceinline__ static float store(float x) { return x; }
+  // The reference's 16-accumulator tree over a row group: this lane holds
+  // accumulators l8 (a0) and l8+8 (a1).
+  __device__ __forceinline__ static float tree16(float a0, float a1) {
+    float t = __fadd_rn(a0, a1);
+    t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 4));
+    t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
+    return __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 1));
+  }
+};
+template <>
+struct KvElem<__nv_bfloat16> {
+  static constexpr int kBytes = 2;
+  __device__ __forceinline__ static int dim(int i, int l8) {
+    return 16 * (i >> 1) + 2 * l8 + (i & 1);
+  }
+  __device__ __forceinline__ static void load2(const __nv_bfloat16* row, int m, int l8,
+                                               float& x0, float& x1) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(row + 16 * m + 2 * l8);
+    x0 = __uint_as_float(w << 16);
+    x1 = __uint_as_float(w & 0xffff0000u);
+  }
+  __device__ __forceinline__ static __nv_bfloat16 store(float x) { return __float2bfloat16_rn(x); }
+  // The same tree with this lane holding accumulators 2*l8 (a0) and 2*l8+1
+  // (a1): acc[j] + acc[j+8] pairs lanes l8 and l8+4, then xor 2, xor 1, and
+  // the last add joins the two components.
+  __device__ __forceinline__ static float tree16(float a0, float a1) {
+#pragma unroll
+    for (int off = 4; off >= 1; off >>= 1) {
+      a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, off));
+      a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, off));
+    }
+    return __fadd_rn(a0, a1);
+  }
+};
+
 // Status codes written into the device status word.
 constexpr int kDevErrConsumerTimeout = 1;
 constexpr int kDevErrProducerTimeout = 2;
@@ -66,9 +123,9 @@ struct DecodeArgs {
   long long o_bstride;
   // Keys / values, contiguous form: slot t of kv head g of sequence b at
   // base + b*kv_bstride + t*stride_t + g*stride_h.
-  const float* K;
-  const float* V;
-  long long kv_bstride, stride_t, stride_h;
+  const void* K;  // elements of the kernel's KV type (float or bf16)
+  const void* V;
+  long long kv_bstride, stride_t, stride_h;  // in elements
   // Paged form (block_table != nullptr): slot t of sequence b lives in page
   // p = block_table[b*bt_stride + t/page_size], row t%page_size, at
   // base + p*page_stride + g*page_hstride + (t%page_size)*D.
@@ -115,8 +172,8 @@ struct DecodeArgs {
   float eps;
   const float* freq;    // [D/2] or null (NoPE)
   int pos;              // RoPE position of the new token
-  float* K_w;
-  float* V_w;
+  void* K_w;
+  void* V_w;
   // Scratch.
   float* partials;  // [2*grid][partial_record_floats(G, D)]
   int* counters;    // [S] per-segment tickets, zero between launches
@@ -124,12 +181,13 @@ struct DecodeArgs {
   unsigned long long timeout_ns;
 };
 
-template <int D>
+template <int D, class KT = float>
 struct TileShape {
-  static constexpr int QR = (D > 128) ? 8 : 16;          // rows per quarter
-  static constexpr int T = 4 * QR;                       // rows per tile
-  static constexpr int TB = T / kBlk;                    // blocks per tile
-  static constexpr int QB = QR * D * 4;                  // quarter bytes
+  static constexpr int EB = KvElem<KT>::kBytes;
+  static constexpr int QR = ((D > 128) ? 8 : 16) * (4 / EB);  // rows per quarter
+  static constexpr int T = 4 * QR;                            // rows per tile
+  static constexpr int TB = T / kBlk;                         // blocks per tile
+  static constexpr int QB = QR * D * EB;                      // quarter bytes
   static constexpr int QSTRIDE = QB + kQuarterPadBytes;  // quarter pitch (bytes)
   static constexpr int KQ = 4 * QSTRIDE;                 // K (or V) part of a stage
   static constexpr int STAGE = 2 * KQ;
@@ -137,9 +195,9 @@ struct TileShape {
   static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
 };
 
-template <int D, int GS>
+template <int D, int GS, class KT = float>
 struct DecodeSmem {
-  using TS = TileShape<D>;
+  using TS = TileShape<D, KT>;
   static constexpr int kStageBytes = TS::STAGES * TS::STAGE;
   // per-warp outputs for the CTA merge; reused as [256][6] scratch by the
   // cross-CTA combine
@@ -242,15 +300,17 @@ __device__ __forceinline__ float ex2(float x) {
 
 // One chunk of RC rows of a row group: QK scores in the reference's
 // accumulation order, lazy online-softmax update, p * V accumulation.
-// kr / vr point at this lane's first element of the chunk's first K / V row
-// in shared memory; rows are D floats apart.  FULL: every row is valid.
-template <int D, int GS, int RC, bool FULL>
-__device__ __forceinline__ void process_rows(const float* kr, const float* vr, int tok, int pt0,
+// kr / vr point at the chunk's first K / V row in shared memory; rows are D
+// elements apart; each lane reads its dims (KvElem<KT>).  FULL: every row is
+// valid.
+template <int D, int GS, int RC, bool FULL, class KT>
+__device__ __forceinline__ void process_rows(const KT* kr, const KT* vr, int tok, int pt0,
                                              int pt1, float scale, float (&q)[GS][D / 8],
                                              float (&o)[GS][D / 8], float (&m2)[GS],
-                                             float (&l)[GS], int new_tok, const float* nk,
-                                             const float* nv) {
+                                             float (&l)[GS], int new_tok, const KT* nk,
+                                             const KT* nv, int l8) {
   constexpr int DV = D / 16;
+  using E = KvElem<KT>;
   float sc[RC][GS];
   bool ok[RC];
 #pragma unroll
@@ -258,7 +318,7 @@ __device__ __forceinline__ void process_rows(const float* kr, const float* vr, i
     ok[r] = FULL || (tok + r >= pt0 && tok + r < pt1);
     // The fused step's new row (slot new_tok) is not in the stage; its k and
     // v sit in shared memory (nk, nv).  Full tiles never contain it.
-    const float* k = (!FULL && tok + r == new_tok) ? nk : kr + r * D;
+    const KT* k = (!FULL && tok + r == new_tok) ? nk : kr + r * D;
     float a0[GS], a1[GS];
 #pragma unroll
     for (int h = 0; h < GS; ++h) {
@@ -267,8 +327,8 @@ __device__ __forceinline__ void process_rows(const float* kr, const float* vr, i
     }
 #pragma unroll
     for (int mm = 0; mm < DV; ++mm) {
-      const float k0 = k[16 * mm];
-      const float k1 = k[16 * mm + 8];
+      float k0, k1;
+      E::load2(k, mm, l8, k0, k1);
 #pragma unroll
       for (int h = 0; h < GS; ++h) {
         a0[h] = __fmaf_rn(q[h][2 * mm], k0, a0[h]);
@@ -320,11 +380,15 @@ __device__ __forceinline__ void process_rows(const float* kr, const float* vr, i
   }
 #pragma unroll
   for (int r = 0; r < RC; ++r) {
-    const float* v = (!FULL && tok + r == new_tok) ? nv : vr + r * D;
+    const KT* v = (!FULL && tok + r == new_tok) ? nv : vr + r * D;
 #pragma unroll
     for (int mm = 0; mm < DV; ++mm) {
-      const float v0 = FULL ? v[16 * mm] : (ok[r] ? v[16 * mm] : 0.f);
-      const float v1 = FULL ? v[16 * mm + 8] : (ok[r] ? v[16 * mm + 8] : 0.f);
+      float v0, v1;
+      E::load2(v, mm, l8, v0, v1);
+      if (!FULL && !ok[r]) {
+        v0 = 0.f;
+        v1 = 0.f;
+      }
 #pragma unroll
       for (int h = 0; h < GS; ++h) {
         o[h][2 * mm] = __fmaf_rn(p[r][h], v0, o[h][2 * mm]);
@@ -394,11 +458,12 @@ __device__ __forceinline__ void fused_fill_tables(const DecodeArgs& a, float* ta
 // same tree as the dot), then NEOX RoPE; a lane holds both halves of each
 // of its rotation pairs (dim i and i + D/2), so no data moves between lanes.
 // The arithmetic is operation for operation that of norm_rope_append_kernel.
-template <int D, int GS>
+template <int D, int GS, class KT>
 __device__ __forceinline__ void fused_rotate_q(const DecodeArgs& a, float (&q)[GS][D / 8],
                                                int l8, const float* tab) {
   constexpr int DV = D / 16;
   constexpr int HV = DV / 2;
+  using E = KvElem<KT>;
   if (a.q_norm) {
 #pragma unroll
     for (int h = 0; h < GS; ++h) {
@@ -408,14 +473,11 @@ __device__ __forceinline__ void fused_rotate_q(const DecodeArgs& a, float (&q)[G
         a0 = __fmaf_rn(q[h][2 * mm], q[h][2 * mm], a0);
         a1 = __fmaf_rn(q[h][2 * mm + 1], q[h][2 * mm + 1], a1);
       }
-      float t = __fadd_rn(a0, a1);
-      t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 4));
-      t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
-      t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 1));
+      const float t = E::tree16(a0, a1);
       const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)D), a.eps)));
 #pragma unroll
       for (int i = 0; i < 2 * DV; ++i) {
-        const int dim = 16 * (i >> 1) + l8 + 8 * (i & 1);
+        const int dim = E::dim(i, l8);
         q[h][i] = __fmul_rn(__fmul_rn(q[h][i], inv), tab[D + dim]);
       }
     }
@@ -423,7 +485,7 @@ __device__ __forceinline__ void fused_rotate_q(const DecodeArgs& a, float (&q)[G
   if (a.freq) {
 #pragma unroll
     for (int i = 0; i < 2 * HV; ++i) {
-      const int dim = 16 * (i >> 1) + l8 + 8 * (i & 1);  // < D/2; partner dim + D/2
+      const int dim = E::dim(i, l8);  // < D/2; partner (index i + 2*HV) at dim + D/2
       const float c = tab[dim], s = tab[D / 2 + dim];
 #pragma unroll
       for (int h = 0; h < GS; ++h) {
@@ -440,12 +502,15 @@ __device__ __forceinline__ void fused_rotate_q(const DecodeArgs& a, float (&q)[G
 // over all nkv*D values); both land in shared memory (for this launch) and
 // in slot n-1 of the cache (for later ones).  Weights and angles come from
 // the staged table.
-template <int D>
+template <int D, class KT>
 __device__ __forceinline__ void fused_new_row(const DecodeArgs& a, const SegView& sv, int warp,
-                                              int lane, float* new_k, float* new_v,
+                                              int lane, KT* new_k, KT* new_v,
                                               const float* tab, const float* kx,
                                               const float* vx) {
   constexpr int H = D / 2;
+  using E = KvElem<KT>;
+  KT* K_w = static_cast<KT*>(a.K_w);
+  KT* V_w = static_cast<KT*>(a.V_w);
   const long long row = (long long)sv.b * a.kv_bstride + (long long)(sv.n - 1) * a.stride_t +
                         (long long)sv.g * a.stride_h;
   if (warp == 0) {
@@ -469,10 +534,12 @@ __device__ __forceinline__ void fused_new_row(const DecodeArgs& a, const SegView
         y0 = z0;
         y1 = z1;
       }
-      new_k[i] = y0;
-      new_k[i + H] = y1;
-      a.K_w[row + i] = y0;
-      a.K_w[row + i + H] = y1;
+      // the cache's format (bf16 rounds here), the same value in both copies
+      const KT z0 = E::store(y0), z1 = E::store(y1);
+      new_k[i] = z0;
+      new_k[i + H] = z1;
+      K_w[row + i] = z0;
+      K_w[row + i + H] = z1;
     }
   } else {
     float vinv = 1.f;
@@ -484,9 +551,9 @@ __device__ __forceinline__ void fused_new_row(const DecodeArgs& a, const SegView
     const float* vh = vx + (long long)sv.g * D;
 #pragma unroll
     for (int i = lane; i < D; i += 32) {
-      const float val = a.v_norm ? __fmul_rn(vh[i], vinv) : vh[i];
+      const KT val = E::store(a.v_norm ? __fmul_rn(vh[i], vinv) : vh[i]);
       new_v[i] = val;
-      a.V_w[row + i] = val;
+      V_w[row + i] = val;
     }
   }
 }
@@ -596,11 +663,13 @@ __device__ __forceinline__ void combine_segment(const DecodeArgs& a, int s, cons
   }
 }
 
-template <int D, int GS, int HS>
+template <int D, int GS, int HS, class KT = float>
 __global__ void __launch_bounds__(kDecodeThreads, 1)
     gqa_decode_kernel(const __grid_constant__ DecodeArgs a) {
-  using TS = TileShape<D>;
-  using SM = DecodeSmem<D, GS>;
+  using TS = TileShape<D, KT>;
+  using SM = DecodeSmem<D, GS, KT>;
+  using E = KvElem<KT>;
+  constexpr int EB = E::kBytes;
   constexpr int QR = TS::QR;
   constexpr int STAGES = TS::STAGES;
   constexpr int WPS = kConsumerWarps / HS;  // warps per head set
@@ -617,9 +686,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   unsigned char* stages = smem;
   float* merge_o = reinterpret_cast<float*>(smem + SM::kStageBytes);
   float* merge_ml = reinterpret_cast<float*>(smem + SM::kStageBytes + SM::kMergeO);
-  float* new_k = reinterpret_cast<float*>(smem + SM::kStageBytes + SM::kMergeO + SM::kMergeML);
-  float* new_v = new_k + D;
-  float* tab = new_v + D;  // fused mode: cos, sin, q_norm, k_norm
+  // fused mode: the new k and v rows (cache format), then the tables (cos,
+  // sin, q_norm, k_norm) at a fixed offset of 2*D floats
+  KT* new_k = reinterpret_cast<KT*>(smem + SM::kStageBytes + SM::kMergeO + SM::kMergeML);
+  KT* new_v = new_k + D;
+  float* tab = reinterpret_cast<float*>(smem + SM::kStageBytes + SM::kMergeO + SM::kMergeML +
+                                        2 * D * 4);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + SM::kStageBytes + SM::kMergeO +
                                                    SM::kMergeML + SM::kNewRow);
   uint64_t* empty_bar = full_bar + STAGES;
@@ -688,7 +760,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
             const int hi = min(tok0 + (q + 1) * QR, pt1c);
             qa[q] = lo;
             qn[q] = hi > lo ? hi - lo : 0;
-            bytes += (uint32_t)qn[q] * D * 4u * 2u;
+            bytes += (uint32_t)qn[q] * D * EB * 2u;
           }
           if (*abort_flag) {
             // Consumers skip waits once aborted; complete the phase without data.
@@ -703,20 +775,21 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
               const int q = lane & 3;
               const int kv = lane >> 2;
               if (qn[q] > 0) {
-                const float* base = kv ? a.V : a.K;
-                const float* src;
+                const unsigned char* base = static_cast<const unsigned char*>(kv ? a.V : a.K);
+                long long off;  // elements
                 if (a.block_table) {
                   const int p =
                       __ldg(a.block_table + (long long)sv.b * a.bt_stride + qa[q] / a.page_size);
-                  src = base + (long long)p * a.page_stride + (long long)sv.g * a.page_hstride +
+                  off = (long long)p * a.page_stride + (long long)sv.g * a.page_hstride +
                         (long long)(qa[q] % a.page_size) * D;
                 } else {
-                  src = base + (long long)sv.b * a.kv_bstride + (long long)qa[q] * a.stride_t +
+                  off = (long long)sv.b * a.kv_bstride + (long long)qa[q] * a.stride_t +
                         (long long)sv.g * a.stride_h;
                 }
                 unsigned char* dst = st_base + kv * TS::KQ + q * TS::QSTRIDE +
-                                     (qa[q] - (tok0 + q * QR)) * D * 4;
-                ptx::bulk_g2s(dst, src, (uint32_t)qn[q] * D * 4u, full_bar + stage, pol);
+                                     (qa[q] - (tok0 + q * QR)) * D * EB;
+                ptx::bulk_g2s(dst, base + off * EB, (uint32_t)qn[q] * D * EB, full_bar + stage,
+                              pol);
               }
             }
           } else {
@@ -727,11 +800,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
               const int r = rem - q * QR;
               const int t = tok0 + q * QR + r;
               if (t >= qa[q] && t < qa[q] + qn[q]) {
-                const float* base = kv ? a.V : a.K;
-                const float* src = base + (long long)sv.b * a.kv_bstride +
-                                   (long long)t * a.stride_t + (long long)sv.g * a.stride_h;
-                unsigned char* dst = st_base + kv * TS::KQ + q * TS::QSTRIDE + r * D * 4;
-                ptx::bulk_g2s(dst, src, (uint32_t)D * 4u, full_bar + stage, pol);
+                const unsigned char* base = static_cast<const unsigned char*>(kv ? a.V : a.K);
+                const long long off = (long long)sv.b * a.kv_bstride + (long long)t * a.stride_t +
+                                      (long long)sv.g * a.stride_h;
+                unsigned char* dst = st_base + kv * TS::KQ + q * TS::QSTRIDE + r * D * EB;
+                ptx::bulk_g2s(dst, base + off * EB, (uint32_t)D * EB, full_bar + stage, pol);
               }
             }
           }
@@ -795,15 +868,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       const int head0 = sv.g * a.G + set * GS;  // first query head of this warp's set
 
       {
-        const float* qb = a.Q + (long long)sv.b * a.q_bstride + (long long)head0 * D + l8;
+        const float* qb = a.Q + (long long)sv.b * a.q_bstride + (long long)head0 * D;
 #pragma unroll
         for (int h = 0; h < GS; ++h) {
 #pragma unroll
-          for (int mm = 0; mm < DV; ++mm) {
-            q[h][2 * mm] = ptx::ld_nc_issue(qb + h * D + 16 * mm);
-            q[h][2 * mm + 1] = ptx::ld_nc_issue(qb + h * D + 16 * mm + 8);
-            o[h][2 * mm] = 0.f;
-            o[h][2 * mm + 1] = 0.f;
+          for (int i = 0; i < 2 * DV; ++i) {
+            q[h][i] = ptx::ld_nc_issue(qb + h * D + E::dim(i, l8));
+            o[h][i] = 0.f;
           }
           m[h] = -CUDART_INF_F;
           l[h] = 0.f;
@@ -829,9 +900,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
             vx = merge_o + D;
           }
         }
-        fused_rotate_q<D, GS>(a, q, l8, tab);
+        fused_rotate_q<D, GS, KT>(a, q, l8, tab);
         if (newrow) {
-          if (warp < 2) fused_new_row<D>(a, sv, warp, lane, new_k, new_v, tab, kx, vx);
+          if (warp < 2) fused_new_row<D, KT>(a, sv, warp, lane, new_k, new_v, tab, kx, vx);
           ptx::named_bar_sync(1, kConsumerWarps * 32);
         }
       }
@@ -845,11 +916,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         }
         __syncwarp();
         if (!*abort_flag) {
-          const float* kq = reinterpret_cast<const float*>(stages + (size_t)stage * TS::STAGE +
-                                                           grp * TS::QSTRIDE) + l8;
-          const float* vq = reinterpret_cast<const float*>(
-                                stages + (size_t)stage * TS::STAGE + TS::KQ + grp * TS::QSTRIDE) +
-                            l8;
+          const KT* kq = reinterpret_cast<const KT*>(stages + (size_t)stage * TS::STAGE +
+                                                     grp * TS::QSTRIDE);
+          const KT* vq = reinterpret_cast<const KT*>(stages + (size_t)stage * TS::STAGE +
+                                                     TS::KQ + grp * TS::QSTRIDE);
           const int tok_base = blk * kBlk + grp * QR + wi * R;
           // Only a piece's first and last tiles can hold rows outside
           // [pt0, pt1); the rest take the predicate-free path.
@@ -860,13 +930,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
             for (int r0 = 0; r0 < R; r0 += RC)
               process_rows<D, GS, RC, true>(kq + (wi * R + r0) * D, vq + (wi * R + r0) * D,
                                             tok_base + r0, pt0, pt1, a.scale, q, o, m, l,
-                                            new_tok, new_k + l8, new_v + l8);
+                                            new_tok, new_k, new_v, l8);
           } else {
 #pragma unroll
             for (int r0 = 0; r0 < R; r0 += RC)
               process_rows<D, GS, RC, false>(kq + (wi * R + r0) * D, vq + (wi * R + r0) * D,
                                              tok_base + r0, pt0, pt1, a.scale, q, o, m, l,
-                                             new_tok, new_k + l8, new_v + l8);
+                                             new_tok, new_k, new_v, l8);
           }
         }
         __syncwarp();
@@ -912,12 +982,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
             o[h][j] = keep * fs + recv * fo;
           }
           m[h] = M;
-          // slot j now holds o-value i = grp*DV/2 + j: dim 16*(i/2) + l8 + 8*(i&1)
-          float* dst = merge_o + ((size_t)warp * GS + h) * D + l8;
+          // slot j now holds o-value i = grp*DV/2 + j, i.e. dim E::dim(i, l8)
+          float* dst = merge_o + ((size_t)warp * GS + h) * D;
 #pragma unroll
           for (int j = 0; j < DV / 2; ++j) {
             const int i = (bit1 * 2 + bit0) * (DV / 2) + j;
-            dst[16 * (i >> 1) + 8 * (i & 1)] = o[h][j];
+            dst[E::dim(i, l8)] = o[h][j];
           }
           if (lane == 0) {
             merge_ml[(warp * GS + h) * 2] = m[h];

@@ -20,6 +20,7 @@
 // blocks first.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <math_constants.h>
 
@@ -33,14 +34,26 @@ constexpr int kPrefillConsumers = 256;  // 16 x 16: ty owns 4 rows, tx a column 
 constexpr int kPrefillThreads = kPrefillConsumers + 32;  // + one producer warp
 constexpr int kPrefillRows = 64;      // query rows (position, head) per CTA
 
-template <int D>
+// Four consecutive cache elements as floats (FP32 or BF16 storage).
+__device__ __forceinline__ float4 load4(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+__device__ __forceinline__ float4 load4(const __nv_bfloat16* p) {
+  const uint2 w = *reinterpret_cast<const uint2*>(p);
+  return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u),
+                     __uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u));
+}
+
+template <int D, class KT = float>
 struct PrefillTile {
+  static constexpr int EB = sizeof(KT);
   static constexpr int BN = D > 128 ? 32 : 64;  // keys per tile
   static constexpr int NJ = BN / 16;            // score columns per thread
-  static constexpr int LD = D + 4;              // padded K/V/Q row pitch (floats)
+  static constexpr int LD = D + 4;              // padded Q row pitch (floats)
+  static constexpr int LDK = D + 16 / EB;       // padded K/V row pitch (elements, +16 B)
   static constexpr int PLD = BN + 4;            // P row pitch (floats)
   static constexpr int kQ = kPrefillRows * LD * 4;
-  static constexpr int kKV = BN * LD * 4;  // one K or V tile
+  static constexpr int kKV = BN * LDK * EB;  // one K or V tile
   static constexpr int kP = kPrefillRows * PLD * 4;
   static constexpr int kBars = 5 * 8;  // full[2], empty[2], q
   static constexpr int kTotal = kQ + 4 * kKV + kP + kBars + 16;
@@ -53,8 +66,8 @@ struct PrefillArgs {
   long long q_tstride;
   float* O;  // same layout, o_tstride
   long long o_tstride;
-  const float* K;  // slot t of kv head g: K + t*stride_t + g*stride_h
-  const float* V;
+  const void* K;  // slot t of kv head g: K + t*stride_t + g*stride_h (elements)
+  const void* V;
   long long stride_t, stride_h;
   int nq, nkv, G, M, N, pos0, window;
   float scale;
@@ -70,17 +83,18 @@ __device__ __forceinline__ float prefill_ex2(float x) {
   return y;
 }
 
-template <int D>
+template <int D, class KT = float>
 __global__ void __launch_bounds__(kPrefillThreads, 1)
     gqa_prefill_kernel(const __grid_constant__ PrefillArgs a) {
-  using TP = PrefillTile<D>;
-  constexpr int BN = TP::BN, NJ = TP::NJ, LD = TP::LD, PLD = TP::PLD;
+  using TP = PrefillTile<D, KT>;
+  constexpr int BN = TP::BN, NJ = TP::NJ, LD = TP::LD, LDK = TP::LDK, PLD = TP::PLD;
+  constexpr int EB = TP::EB;
   constexpr int DJ = D / 64;  // float4 groups of output columns per thread
   constexpr float kLog2e = 1.4426950408889634f;
 
   extern __shared__ __align__(128) unsigned char smem[];
   float* Qs = reinterpret_cast<float*>(smem);
-  float* KVs = reinterpret_cast<float*>(smem + TP::kQ);  // [stage][K,V][BN][LD]
+  KT* KVs = reinterpret_cast<KT*>(smem + TP::kQ);  // [stage][K,V][BN][LDK]
   float* Ps = reinterpret_cast<float*>(smem + TP::kQ + 4 * TP::kKV);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + TP::kQ + 4 * TP::kKV + TP::kP);
   uint64_t* empty = full + 2;
@@ -143,14 +157,16 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       __syncwarp();
       const int ts = t_lo + i * BN;
       const int rows = min(BN, t_hi - ts);
-      float* Kd = KVs + (size_t)(stage * 2) * BN * LD;
-      float* Vd = Kd + (size_t)BN * LD;
-      if (lane == 0) ptx::mbar_arrive_expect_tx(full + stage, (uint32_t)rows * D * 4u * 2u);
+      KT* Kd = KVs + (size_t)(stage * 2) * BN * LDK;
+      KT* Vd = Kd + (size_t)BN * LDK;
+      if (lane == 0) ptx::mbar_arrive_expect_tx(full + stage, (uint32_t)rows * D * EB * 2u);
       __syncwarp();
       for (int c = lane; c < rows; c += 32) {
         const long long off = (long long)(ts + c) * a.stride_t + (long long)g * a.stride_h;
-        ptx::bulk_g2s(Kd + (size_t)c * LD, a.K + off, D * 4u, full + stage, pol);
-        ptx::bulk_g2s(Vd + (size_t)c * LD, a.V + off, D * 4u, full + stage, pol);
+        ptx::bulk_g2s(Kd + (size_t)c * LDK, static_cast<const KT*>(a.K) + off, D * EB,
+                      full + stage, pol);
+        ptx::bulk_g2s(Vd + (size_t)c * LDK, static_cast<const KT*>(a.V) + off, D * EB,
+                      full + stage, pol);
       }
     }
     return;
@@ -180,8 +196,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     // A timed-out wait leaves this thread computing on stale data; the
     // results are then discarded (status word) and every loop still ends.
     ok_waits &= ptx::mbar_wait_bounded(full + stage, (i >> 1) & 1, a.timeout_ns);
-    const float* Kt = KVs + (size_t)(stage * 2) * BN * LD;
-    const float* Vt = Kt + (size_t)BN * LD;
+    const KT* Kt = KVs + (size_t)(stage * 2) * BN * LDK;
+    const KT* Vt = Kt + (size_t)BN * LDK;
     const int ts = t_lo + i * BN;
     const int kc = min(BN, t_hi - ts);
 
@@ -192,7 +208,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
 #pragma unroll
       for (int j = 0; j < NJ; ++j) s[ii][j] = 0.f;
     const float* qb = Qs + (size_t)(ty * 4) * LD;
-    const float* kb = Kt + (size_t)tx * LD;
+    const KT* kb = Kt + (size_t)tx * LDK;
 #pragma unroll 4
     for (int k = 0; k < D; k += 4) {
       float4 qv[4], kv[NJ];
@@ -200,7 +216,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       for (int ii = 0; ii < 4; ++ii) qv[ii] = *reinterpret_cast<const float4*>(qb + ii * LD + k);
 #pragma unroll
       for (int j = 0; j < NJ; ++j)
-        kv[j] = *reinterpret_cast<const float4*>(kb + (size_t)(16 * j) * LD + k);
+        kv[j] = load4(kb + (size_t)(16 * j) * LDK + k);
 #pragma unroll
       for (int ii = 0; ii < 4; ++ii)
 #pragma unroll
@@ -252,10 +268,10 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       for (int ii = 0; ii < 4; ++ii) pv[ii] = *reinterpret_cast<const float4*>(pb + ii * PLD + c);
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
-        const float* vr = Vt + (size_t)(c + cc) * LD + tx * 4;
+        const KT* vr = Vt + (size_t)(c + cc) * LDK + tx * 4;
 #pragma unroll
         for (int jj = 0; jj < DJ; ++jj) {
-          const float4 v4 = *reinterpret_cast<const float4*>(vr + 64 * jj);
+          const float4 v4 = load4(vr + 64 * jj);
 #pragma unroll
           for (int ii = 0; ii < 4; ++ii) {
             const float p = cc == 0 ? pv[ii].x : cc == 1 ? pv[ii].y : cc == 2 ? pv[ii].z : pv[ii].w;
@@ -268,10 +284,10 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       }
     }
     for (; c < kc; ++c) {  // ragged end of the last tile
-      const float* vr = Vt + (size_t)c * LD + tx * 4;
+      const KT* vr = Vt + (size_t)c * LDK + tx * 4;
 #pragma unroll
       for (int jj = 0; jj < DJ; ++jj) {
-        const float4 v4 = *reinterpret_cast<const float4*>(vr + 64 * jj);
+        const float4 v4 = load4(vr + 64 * jj);
 #pragma unroll
         for (int ii = 0; ii < 4; ++ii) {
           const float p = pb[ii * PLD + c];
