@@ -377,7 +377,8 @@ def run_single(args, cfg):
     dev = torch.device("cuda", local)
     stream = torch.cuda.current_stream()
 
-    cache = mb.KVCache(L, nkv, d, n)
+    bf16 = args.kv == "bf16"
+    cache = mb.KVCache(L, nkv, d, n, dtype=args.kv)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
     for layer in range(L):
@@ -494,13 +495,13 @@ def run_single(args, cfg):
     cache.check(stream)
     del graph, dgraph
 
-    kv_bytes_layer = 2 * nkv * n * d * 4
+    kv_bytes_layer = 2 * nkv * n * d * (2 if bf16 else 4)
     total_bytes = kv_bytes_layer * L * world
     value = total_bytes / (ms * 1e-3) / 1e9
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
     peak, peak_kind = hbm_peak()
     achieved = kv_bytes_layer / (dec_avg_ms * 1e-3) / 1e9
-    traffic = read_traffic("gqa_decode_kernel", args.config)
+    traffic = read_traffic("gqa_decode_kernel", args.config + ("-bf16" if bf16 else ""))
 
     result = None
     if rank == 0:
@@ -511,8 +512,10 @@ def run_single(args, cfg):
             "data": "synthetic (seeded N(0,1) K/V and q/k/v generated on device)",
             "config": {"workload": f"{args.config}: {cfg['desc']}", "layers": L, "nq": nq,
                        "nkv": nkv, "head_dim": d, "n": n, "rope_theta": cfg["theta"],
+                       "kv_dtype": args.kv,
                        "parallelism": f"replicas x{world} (one sequence per GPU)",
-                       "l2": "inputs larger than L2 (4.3 GB KV per GPU)"},
+                       "l2": f"inputs larger than L2 ({total_bytes / world / 1e9:.1f} GB KV "
+                             "per GPU)"},
             "tok_per_s": round(world * 1000.0 / ms, 2),
             "pct_hbm_peak": round(100.0 * value / world / peak, 2),
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
@@ -525,7 +528,8 @@ def run_single(args, cfg):
             "gpu_launches": (1 if fused else 2) * L * args.steps,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": traffic, "kernel": "gqa_decode_kernel<128,4,1>",
+                         "traffic": traffic,
+                         "kernel": "gqa_decode_kernel<128,4,1%s>" % (",bf16" if bf16 else ""),
                          "timed": ("fused step launches (prologue + append + decode)" if fused
                                    else "decode launches alone"),
                          "peak_source": f"{peak_kind} hbm_gbs",
@@ -1017,6 +1021,8 @@ def main(argv=None):
     ap.add_argument("--path", choices=["fused", "split"], default="fused",
                     help="fused: molot_attn_step (one launch per layer); split: "
                          "molot_attn_append_rope + molot_attn_decode")
+    ap.add_argument("--kv", choices=["f32", "bf16"], default="f32",
+                    help="KV-cache storage of cfg1/cfg2 (bf16: half the bytes, FP32 math)")
     ap.add_argument("--resident-gb", type=float, default=40.0,
                     help="cfg4/cfg5: device memory for distinct layer pools per rank")
     ap.add_argument("--layers", type=int, default=0,
