@@ -21,6 +21,8 @@
 #ifndef MOLOT_B200_H
 #define MOLOT_B200_H
 
+#include <stdint.h>
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -126,6 +128,24 @@ int molot_attn_prefill_strided_dev(const float* Q, const float* K, const float* 
                                    int nq, int nkv, int M, int N, int d, long long stride_t,
                                    long long stride_h, float scale, int pos0, int window,
                                    void* stream);
+
+/* ------------------------------------------------------------------------
+ * Q4 GEMV (the projections either side of attention, forward.h:543-553,600)
+ * ---------------------------------------------------------------------- */
+
+/* Replaces molot::gemv_q4 (gemm.h:223-254) on host buffers: a Q4Matrix
+ * (quant.h:70-80) given as its arrays -- scales [rows][cols/32] FP32, zeros
+ * [rows][cols/32] int8, data [rows][cols/2] packed nibbles (element 2j in
+ * the low nibble of byte j), wsums (accepted, unused) -- times x [cols];
+ * y [rows].  Activations are quantized to int8 per 32 values as
+ * quantize_act_q8 does (gemm.h:44-70).  cols must be a multiple of 32. */
+int molot_gemv_q4(const float* scales, const int8_t* zeros, const uint8_t* data,
+                  const int16_t* wsums, int rows, int cols, const float* x, float* y);
+
+/* molot_gemv_q4 on device buffers (data and scales 16-byte aligned),
+ * stream-ordered; two launches (activation quantization, then the GEMV). */
+int molot_gemv_q4_dev(const float* scales, const int8_t* zeros, const uint8_t* data, int rows,
+                      int cols, const float* x, float* y, void* stream);
 
 /* forward.h:554-575 on device buffers for a [cap][nkv*d] cache: q (nq heads)
  * and k (nkv heads) get per-head weighted RMSNorm when q_norm / k_norm are

@@ -105,6 +105,8 @@ _decl("molot_attn_prefill_strided_dev",
 _decl("molot_attn_append_rope_tokens",
       [_p, _i, _p, _p, _p, _p, _p, _p, _i, _f, _p, _i, _i, _i, _p])
 _decl("molot_attn_prefill", [_p, _i, _p, _p, _i, _i, _f, _i, _i, _p])
+_decl("molot_gemv_q4", [_p, _p, _p, _p, _i, _i, _p, _p])
+_decl("molot_gemv_q4_dev", [_p, _p, _p, _i, _i, _p, _p, _p])
 _decl("molot_paged_plan_create", [_pp])
 _decl("molot_paged_plan_destroy", [_p], None)
 _decl("molot_paged_plan_build", [_p, _i, _i, _i, _i, _p, _p, _i, _p])
@@ -214,6 +216,27 @@ def prefill_strided(Q, K, V, O, nq, nkv, M, N, d, stride_t, stride_h, scale, pos
     check(_lib.molot_attn_prefill_strided_dev(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), nq, nkv, M, N,
                                               d, stride_t, stride_h, scale, pos0, window,
                                               _stream_ptr(stream)))
+
+
+def gemv_q4(q4, x) -> np.ndarray:
+    """gemm.h:223-254 on host arrays: q4 = (scales f32 [rows][cols/32], zeros
+    i8, data u8 [rows][cols/2], wsums i16) as quant.h lays a Q4Matrix out;
+    returns y = W x [rows]."""
+    sc, z, data, ws = (np.ascontiguousarray(a) for a in q4)
+    rows, ng = sc.shape
+    x = _host_f32(x)
+    y = np.zeros(rows, np.float32)
+    check(_lib.molot_gemv_q4(_ptr(sc), _ptr(z), _ptr(data), _ptr(ws), rows, ng * 32, _ptr(x),
+                             _ptr(y)))
+    return y
+
+
+def gemv_q4_dev(scales, zeros, data, x, y, stream=None) -> None:
+    """molot_gemv_q4_dev on device tensors (scales [rows][cols/32] f32, zeros
+    int8, data uint8 [rows][cols/2], x [cols], y [rows])."""
+    rows, ng = scales.shape
+    check(_lib.molot_gemv_q4_dev(_ptr(scales), _ptr(zeros), _ptr(data), rows, ng * 32, _ptr(x),
+                                 _ptr(y), _stream_ptr(stream)))
 
 
 def attn_decode_gqa(Q, K, V, nq, nkv, n, d, scale) -> np.ndarray:

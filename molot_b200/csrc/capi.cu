@@ -13,6 +13,7 @@
 
 #include "append.cuh"
 #include "decode.cuh"
+#include "gemv.cuh"
 #include "molot_b200.h"
 #include "prefill.cuh"
 
@@ -552,6 +553,40 @@ int host_prefill(const float* Qm, const float* K, const float* V, float* Om, int
   return c.ws.check(c.stream, true);
 }
 
+// ------------------------------------------------------------- Q4 GEMV
+
+// Quantize x, then y = W x; the packed activations live in the workspace.
+int gemv_q4_launch(Workspace& ws, const float* scales, const int8_t* zeros, const uint8_t* data,
+                   int rows, int cols, const float* x, float* y, cudaStream_t st) {
+  if (!scales || !zeros || !data || !x || !y) return fail(MOLOT_ERR_INVALID, "null pointer");
+  if (rows <= 0 || cols <= 0 || cols % 32)
+    return fail(MOLOT_ERR_INVALID, "rows > 0 and cols a positive multiple of 32 required");
+  if (!aligned16(data) || !aligned16(scales))
+    return fail(MOLOT_ERR_INVALID, "data and scales must be 16-byte aligned");
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  const int ng = cols / 32;
+  // scratch: ng packed groups (8 ints), then ng scales, then ng sums
+  if ((rc = ws.ensure(dev, (size_t)ng * 10 + 16, 0, 0))) return rc;
+  GemvQ4Args a = {};
+  a.scales = scales;
+  a.zeros = zeros;
+  a.data = data;
+  a.x = x;
+  a.y = y;
+  a.xq = reinterpret_cast<Q8Packed*>(ws.partials);
+  a.xs = ws.partials + (size_t)ng * 8;
+  a.xsum = reinterpret_cast<int*>(ws.partials + (size_t)ng * 9);
+  a.rows = rows;
+  a.cols = cols;
+  a.ng = ng;
+  if ((rc = launch(reinterpret_cast<const void*>(&q8_quantize_kernel),
+                   dim3((ng + kGemvWarps - 1) / kGemvWarps), dim3(kGemvWarps * 32), 0, st, &a)))
+    return rc;
+  return launch(reinterpret_cast<const void*>(&gemv_q4_kernel),
+                dim3((rows + kGemvWarps - 1) / kGemvWarps), dim3(kGemvWarps * 32), 0, st, &a);
+}
+
 }  // namespace
 
 // Lets other translation units of the library report through
@@ -1055,6 +1090,48 @@ int molot_attn_prefill_strided_dev(const float* Q, const float* K, const float* 
 int molot_attn_prefill_gqa(const float* Qm, const float* K, const float* V, float* Om, int nq,
                            int nkv, int M, int N, int d, float scale, int pos0, int window) {
   return host_prefill(Qm, K, V, Om, nq, nkv, M, N, d, scale, pos0, window);
+}
+
+int molot_gemv_q4_dev(const float* scales, const int8_t* zeros, const uint8_t* data, int rows,
+                      int cols, const float* x, float* y, void* stream) {
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  HostCtx& c = host_ctx(dev);
+  std::lock_guard<std::mutex> lk(c.mu);
+  return gemv_q4_launch(c.ws, scales, zeros, data, rows, cols, x, y, (cudaStream_t)stream);
+}
+
+int molot_gemv_q4(const float* scales, const int8_t* zeros, const uint8_t* data,
+                  const int16_t* wsums, int rows, int cols, const float* x, float* y) {
+  (void)wsums;  // the VNNI bias correction of the CPU path; not needed here
+  if (!scales || !zeros || !data || !x || !y) return fail(MOLOT_ERR_INVALID, "null pointer");
+  if (rows <= 0 || cols <= 0 || cols % 32)
+    return fail(MOLOT_ERR_INVALID, "rows > 0 and cols a positive multiple of 32 required");
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  HostCtx& c = host_ctx(dev);
+  std::lock_guard<std::mutex> lk(c.mu);
+  if ((rc = c.init(dev))) return rc;
+  const size_t ng = cols / 32, nsc = rows * ng;
+  // staging (floats): scales, x, y, then zeros and nibbles as bytes
+  const size_t o_sc = 0, o_x = round4(nsc), o_y = o_x + round4(cols), o_b = o_y + round4(rows);
+  const size_t bytes = nsc + (size_t)rows * cols / 2;
+  if ((rc = c.reserve(o_b + round4((bytes + 3) / 4) + 16))) return rc;
+  float* dsc = c.buf + o_sc;
+  float* dx = c.buf + o_x;
+  float* dy = c.buf + o_y;
+  uint8_t* dz = reinterpret_cast<uint8_t*>(c.buf + o_b);
+  uint8_t* dd = dz + ((nsc + 15) & ~size_t(15));
+  MOLOT_CUDA(cudaMemcpyAsync(dsc, scales, nsc * 4, cudaMemcpyHostToDevice, c.stream));
+  MOLOT_CUDA(cudaMemcpyAsync(dx, x, (size_t)cols * 4, cudaMemcpyHostToDevice, c.stream));
+  MOLOT_CUDA(cudaMemcpyAsync(dz, zeros, nsc, cudaMemcpyHostToDevice, c.stream));
+  MOLOT_CUDA(cudaMemcpyAsync(dd, data, (size_t)rows * cols / 2, cudaMemcpyHostToDevice, c.stream));
+  rc = gemv_q4_launch(c.ws, dsc, reinterpret_cast<const int8_t*>(dz), dd, rows, cols, dx, dy,
+                      c.stream);
+  if (rc) return rc;
+  MOLOT_CUDA(cudaMemcpyAsync(y, dy, (size_t)rows * 4, cudaMemcpyDeviceToHost, c.stream));
+  MOLOT_CUDA(cudaStreamSynchronize(c.stream));
+  return c.ws.check(c.stream, true);
 }
 
 int molot_kv_check(molot_kv_cache* kv, void* stream) {

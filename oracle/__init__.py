@@ -92,6 +92,9 @@ def port():
                  [_p, _p, _p, _p, _p, _i, _p, _p, _i, _i, _i, _i, _i, _f, _i])
         _declare(lib, "oracle_attn_prefill_gqa",
                  [_p, _p, _p, _p, _i, _i, _i, _i, _i, _f, _i, _i])
+        _declare(lib, "oracle_quantize_q4", [_p, _i, _i, _p, _p, _p, _p])
+        _declare(lib, "oracle_quantize_act_q8", [_p, _i, _p, _p])
+        _declare(lib, "oracle_gemv_q4", [_p, _p, _p, _i, _i, _p, _p])
         _port = lib
     return _port
 
@@ -123,6 +126,11 @@ def ref():
             _declare(lib, "ref_dot", [_p, _p, _i], _f)
             _declare(lib, "ref_attn_layer_step",
                      [_p, _p, _p, _p, _p, _i, _f, _p, _i, _p, _p, _p, _i, _p, _i, _i, _i, _f, _i, _i], _i)
+            for name, args in (("ref_quantize_q4", [_p, _i, _i, _p, _p, _p, _p]),
+                               ("ref_quantize_act_q8", [_p, _i, _p, _p]),
+                               ("ref_gemv_q4", [_p, _p, _p, _p, _i, _i, _p, _p, _i])):
+                if hasattr(lib, name):
+                    _declare(lib, name, args)
             if hasattr(lib, "ref_attn_prefill_gqa"):
                 _declare(lib, "ref_attn_prefill_gqa",
                          [_p, _p, _p, _p, _i, _i, _i, _i, _i, _f, _i, _i, _i])
@@ -237,6 +245,46 @@ def attn_prefill_gqa(Qm, K, V, nq, nkv, M, N, d, scale, pos0, window, impl="port
         lib.ref_attn_prefill_gqa(_ptr(Qm), _ptr(K), _ptr(V), _ptr(Om), nq, nkv, M, N, d, scale,
                                  pos0, window, nthreads or (os.cpu_count() or 1))
     return Om
+
+
+def quantize_q4(W, impl="port"):
+    """quant.h:112-123: FP32 [rows][cols] -> (scales f32 [rows][ng], zeros i8,
+    data u8 [rows][cols/2], wsums i16), ng = cols/32."""
+    W = _f32(W)
+    rows, cols = W.shape
+    ng = cols // 32
+    sc = np.zeros((rows, ng), np.float32)
+    z = np.zeros((rows, ng), np.int8)
+    data = np.zeros((rows, cols // 2), np.uint8)
+    ws = np.zeros((rows, ng), np.int16)
+    fn = port().oracle_quantize_q4 if impl == "port" else ref().ref_quantize_q4
+    fn(_ptr(W), rows, cols, _ptr(sc), _ptr(z), _ptr(data), _ptr(ws))
+    return sc, z, data, ws
+
+
+def quantize_act_q8(x, impl="port"):
+    """gemm.h:44-70: x [n] -> (q i8 [n], scales f32 [ceil(n/32)])."""
+    x = _f32(x)
+    q = np.zeros(x.size, np.int8)
+    sc = np.zeros((x.size + 31) // 32, np.float32)
+    fn = port().oracle_quantize_act_q8 if impl == "port" else ref().ref_quantize_act_q8
+    fn(_ptr(x), x.size, _ptr(q), _ptr(sc))
+    return q, sc
+
+
+def gemv_q4(q4, x, impl="port", nthreads=0):
+    """gemm.h:223-254: y = W x for a Q4 matrix from quantize_q4."""
+    sc, z, data, ws = q4
+    rows, ng = sc.shape
+    cols = ng * 32
+    x = _f32(x)
+    y = np.zeros(rows, np.float32)
+    if impl == "port":
+        port().oracle_gemv_q4(_ptr(sc), _ptr(z), _ptr(data), rows, cols, _ptr(x), _ptr(y))
+    else:
+        ref().ref_gemv_q4(_ptr(sc), _ptr(z), _ptr(data), _ptr(ws), rows, cols, _ptr(x), _ptr(y),
+                          nthreads or (os.cpu_count() or 1))
+    return y
 
 
 def rope_apply(x, d, pos, inv_freq, impl="port"):

@@ -278,3 +278,91 @@ void oracle_attn_prefill_gqa(const float* Qm, const float* K, const float* V, fl
   }
   free(scores);
 }
+
+/* ---- Q4 GEMV (gemm.h:36-70, 174-254; quant.h:70-123) ------------------ */
+
+/* quant.h:84-110 quantize_q4_row for every row: per 32-group min/max, scale
+ * (max-min)/15 (1 when not positive), zero nearbyint(-min/s) in [0,15],
+ * nibbles nearbyint(x/s)+zero in [0,15], element 2j in the low nibble of
+ * byte j, wsums = sum(nibble - zero). */
+void oracle_quantize_q4(const float* W, int rows, int cols, float* scales, int8_t* zeros,
+                        uint8_t* data, int16_t* wsums) {
+  int ng = cols / 32;
+  for (int r = 0; r < rows; ++r)
+    for (int g = 0; g < ng; ++g) {
+      const float* grp = W + (long)r * cols + (long)g * 32;
+      float mn = grp[0], mx = grp[0];
+      for (int k = 0; k < 32; ++k) {
+        if (grp[k] < mn) mn = grp[k];
+        if (grp[k] > mx) mx = grp[k];
+      }
+      /* the reference's -ffast-math build multiplies by the reciprocal of
+       * the constant: (mx - mn) / 15 becomes (mx - mn) * (1/15) */
+      float s = (mx - mn) * (1.0f / 15.0f);
+      if (!(s > 0)) s = 1.0f;
+      int z = (int)nearbyintf(-mn / s);
+      z = z < 0 ? 0 : (z > 15 ? 15 : z);
+      scales[(long)r * ng + g] = s;
+      zeros[(long)r * ng + g] = (int8_t)z;
+      int wsum = 0;
+      for (int k = 0; k < 32; k += 2) {
+        int v0 = (int)nearbyintf(grp[k] / s) + z;
+        int v1 = (int)nearbyintf(grp[k + 1] / s) + z;
+        v0 = v0 < 0 ? 0 : (v0 > 15 ? 15 : v0);
+        v1 = v1 < 0 ? 0 : (v1 > 15 ? 15 : v1);
+        data[(long)r * cols / 2 + (long)g * 16 + k / 2] = (uint8_t)(v0 | (v1 << 4));
+        wsum += (v0 - z) + (v1 - z);
+      }
+      wsums[(long)r * ng + g] = (int16_t)wsum;
+    }
+}
+
+/* gemm.h:44-70 quantize_act_q8: per 32 values, xs = amax/127 (1 when not
+ * positive) rounded to fp16 (nearest even, as F16C's _cvtss_sh); q =
+ * round-half-away(x/xs) clamped to [-127, 127]. */
+void oracle_quantize_act_q8(const float* x, int n, int8_t* q, float* scales) {
+  for (int s = 0; s < n; s += 32) {
+    int e = s + 32 < n ? s + 32 : n;
+    float amax = 0;
+    for (int i = s; i < e; ++i) {
+      float v = fabsf(x[i]);
+      if (v > amax) amax = v;
+    }
+    float xs = amax / 127.0f;
+    if (!(xs > 0)) xs = 1.0f;
+    xs = (float)(_Float16)xs;
+    scales[s / 32] = xs;
+    for (int i = s; i < e; ++i) {
+      int v = (int)roundf(x[i] / xs);
+      v = v > 127 ? 127 : (v < -127 ? -127 : v);
+      q[i] = (int8_t)v;
+    }
+  }
+}
+
+/* gemm.h:174-254 gemv_q4: activations quantized once; per row and group
+ * the exact integer sum G = sum((nibble - zero) * q); y = sum over groups,
+ * in group order, of (float)G * scale_w * scale_x. */
+void oracle_gemv_q4(const float* scales, const int8_t* zeros, const uint8_t* data, int rows,
+                    int cols, const float* x, float* y) {
+  int ng = cols / 32;
+  int8_t* q = (int8_t*)malloc((size_t)cols);
+  float* xs = (float*)malloc(sizeof(float) * (size_t)ng);
+  oracle_quantize_act_q8(x, cols, q, xs);
+  for (int r = 0; r < rows; ++r) {
+    float acc = 0.0f;
+    for (int g = 0; g < ng; ++g) {
+      const uint8_t* pp = data + (long)r * cols / 2 + (long)g * 16;
+      int z = zeros[(long)r * ng + g];
+      int isum = 0;
+      for (int k = 0; k < 32; ++k) {
+        int w = ((k & 1) ? (pp[k / 2] >> 4) : (pp[k / 2] & 15)) - z;
+        isum += w * q[g * 32 + k];
+      }
+      acc += (float)isum * scales[(long)r * ng + g] * xs[g];
+    }
+    y[r] = acc;
+  }
+  free(q);
+  free(xs);
+}

@@ -22,6 +22,8 @@
 #ifndef MOLOT_ATTN_ORACLE_H
 #define MOLOT_ATTN_ORACLE_H
 
+#include <stdint.h>
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -80,6 +82,13 @@ void oracle_attn_decode_paged(const float* Q, const float* Kpool, const float* V
  * [N][nkv*d]; query m sits at position pos0+m. */
 void oracle_attn_prefill_gqa(const float* Qm, const float* K, const float* V, float* Om, int nq,
                              int nkv, int M, int N, int d, float scale, int pos0, int window);
+
+/* Q4 weights (quant.h:70-123) and the Q4 GEMV of gemm.h:174-254. */
+void oracle_quantize_q4(const float* W, int rows, int cols, float* scales, int8_t* zeros,
+                        uint8_t* data, int16_t* wsums);
+void oracle_quantize_act_q8(const float* x, int n, int8_t* q, float* scales);
+void oracle_gemv_q4(const float* scales, const int8_t* zeros, const uint8_t* data, int rows,
+                    int cols, const float* x, float* y);
 
 #ifdef __cplusplus
 }

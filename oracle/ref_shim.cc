@@ -149,3 +149,40 @@ void ref_attn_prefill_gqa(const float* Qm, const float* K, const float* V, float
 }
 
 }  // extern "C"
+
+extern "C" {
+
+// quant.h:112-123 quantize_q4: rows x cols FP32 -> the Q4Matrix arrays.
+void ref_quantize_q4(const float* W, int rows, int cols, float* scales, int8_t* zeros,
+                     uint8_t* data, int16_t* wsums) {
+  molot::Q4Matrix m = molot::quantize_q4(W, rows, cols);
+  std::memcpy(scales, m.scales.data(), m.scales.size() * sizeof(float));
+  std::memcpy(zeros, m.zeros.data(), m.zeros.size());
+  std::memcpy(data, m.data.data(), m.data.size());
+  std::memcpy(wsums, m.wsums.data(), m.wsums.size() * sizeof(int16_t));
+}
+
+// gemm.h:44-70 quantize_act_q8: per-32 absmax/127 scales (fp16-rounded), q.
+void ref_quantize_act_q8(const float* x, int n, int8_t* q, float* scales) {
+  molot::QAct8 a = molot::quantize_act_q8(x, n);
+  std::memcpy(q, a.q.data(), a.q.size());
+  std::memcpy(scales, a.scales.data(), a.scales.size() * sizeof(float));
+}
+
+// gemm.h:223-254 gemv_q4 on a Q4Matrix given as its arrays.
+void ref_gemv_q4(const float* scales, const int8_t* zeros, const uint8_t* data,
+                 const int16_t* wsums, int rows, int cols, const float* x, float* y,
+                 int nthreads) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  molot::Q4Matrix m;
+  m.rows = rows;
+  m.cols = cols;
+  m.ngroups = cols / molot::Q4Matrix::GS;
+  m.scales.assign(scales, scales + (size_t)rows * m.ngroups);
+  m.zeros.assign(zeros, zeros + (size_t)rows * m.ngroups);
+  m.data.assign(data, data + (size_t)rows * cols / 2);
+  m.wsums.assign(wsums, wsums + (size_t)rows * m.ngroups);
+  molot::gemv_q4(m, x, y, pool_for(nthreads));
+}
+
+}  // extern "C"

@@ -140,6 +140,29 @@ def prefill_cases():
     return out
 
 
+def gemv_q4_cases():
+    """quant.h:112-123 weight quantization, gemm.h:44-70 activation
+    quantization and gemm.h:223-254 gemv_q4, all run by the reference."""
+    rng = np.random.default_rng(77)
+    out = {}
+    W = (rng.standard_normal((16, 256)) * 0.05).astype(np.float32)
+    W[3, 32:64] = 0.0  # a flat group: scale 1, zero 0
+    sc, z, data, ws = oracle.quantize_q4(W, impl="ref")
+    out["quant"] = dict(W=W, scales=sc, zeros=z, data=data, wsums=ws)
+    x = (rng.standard_normal(2048) * rng.uniform(0.1, 20, 2048)).astype(np.float32)
+    x[64:96] = 0.0  # an all-zero activation block
+    q, xs = oracle.quantize_act_q8(x, impl="ref")
+    out["act"] = dict(x=x, q=q, scales=xs)
+    for name, (rows, cols) in (("gemv_a", (96, 1024)), ("gemv_b", (33, 4096))):
+        Wm = (rng.standard_normal((rows, cols)) * 0.03).astype(np.float32)
+        q4 = oracle.quantize_q4(Wm, impl="ref")
+        xv = (rng.standard_normal(cols) * 2).astype(np.float32)
+        xv[:32] *= 50.0  # an outlier block
+        y = oracle.gemv_q4(q4, xv, impl="ref", nthreads=4)
+        out[name] = dict(scales=q4[0], zeros=q4[1], data=q4[2], wsums=q4[3], x=xv, y=y)
+    return out
+
+
 def flatten(cases):
     flat = {}
     for name, case in cases.items():
@@ -155,6 +178,7 @@ FIXTURES = {
     "norm_rope.npz": lambda: flatten(norm_rope_case()),
     "layer_step.npz": layer_step_case,
     "prefill.npz": lambda: flatten(prefill_cases()),
+    "gemv_q4.npz": lambda: flatten(gemv_q4_cases()),
 }
 
 

@@ -171,3 +171,20 @@ def test_prefill_oracle_matches_reference_golden():
         got = oracle.attn_prefill_gqa(z[f"{name}/Q"], z[f"{name}/K"], z[f"{name}/V"], nq, nkv, M,
                                       N, d, float(z[f"{name}/scale"]), pos0, window)
         assert oracle.rel_err(got, z[f"{name}/O"]) < 1e-6, name
+
+
+def test_q4_oracle_matches_reference_golden():
+    """The restated Q4 weight / activation quantizers and gemv_q4 against the
+    reference's own outputs (tests/golden/gemv_q4.npz)."""
+    import oracle
+    z = np.load(os.path.join(GOLDEN, "gemv_q4.npz"))
+    got = oracle.quantize_q4(z["quant/W"])
+    for i, key in enumerate(("scales", "zeros", "data", "wsums")):
+        assert np.array_equal(got[i], z[f"quant/{key}"]), key
+    q, xs = oracle.quantize_act_q8(z["act/x"])
+    assert np.array_equal(q, z["act/q"]) and np.array_equal(xs, z["act/scales"])
+    for name in ("gemv_a", "gemv_b"):
+        q4 = tuple(z[f"{name}/{k}"] for k in ("scales", "zeros", "data", "wsums"))
+        y = oracle.gemv_q4(q4, z[f"{name}/x"])
+        # same integers; float sums differ only by the reference's FMA contraction
+        assert oracle.rel_err(y, z[f"{name}/y"]) < 1e-6, name
