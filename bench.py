@@ -73,6 +73,10 @@ CONFIGS = {
     "prefill": dict(kind="prefill", layers=32, nq=32, nkv=8, d=128, prompt=4096, theta=5e5,
                     window=0, desc="prefill of a 4096-token prompt, Llama-3-8B attention shape "
                                    "(not a BASELINE config: the next row after decode)"),
+    "gemv": dict(kind="gemv", layers=32, hidden=4096, nq=32, nkv=8, d=128,
+                 desc="Q4 projections around attention per decode token, Llama-3-8B: fused "
+                      "QKV (6144x4096) and O (4096x4096) GEMVs per layer, 32 layers (not a "
+                      "BASELINE config: item 3 after decode)"),
     "cfg5": dict(kind="paged_head", layers=80, nq=64, nkv=8, d=128, batch=32, len_lo=8192,
                  len_hi=131072, page=16, theta=5e5, seed=5,
                  desc="Llama-3-70B shape, B=32, n~U[8192,131072], kv-head sharded"),
@@ -190,8 +194,25 @@ def prefill_flops(cfg):
 PREFILL_METRIC = "prefill attention TFLOP/s (FP32), 4096-token prompt"
 
 
+GEMV_METRIC = "Q4 projection GEMV GB/s (weights streamed per decode token)"
+
+
+def gemv_shapes(cfg):
+    """(rows, cols) of the per-layer GEMVs: fused QKV, then O."""
+    h, d = cfg["hidden"], cfg["d"]
+    return [((cfg["nq"] + 2 * cfg["nkv"]) * d, h), (h, cfg["nq"] * d)]
+
+
+def gemv_bytes(rows, cols):
+    """HBM bytes of one Q4 GEMV: nibbles, FP32 scales, int8 zeros, x, y."""
+    return rows * cols // 2 + rows * (cols // 32) * 5 + cols * 4 + rows * 4
+
+
 def step_work(cfg):
     """(metric, unit, amount per step, divisor to the unit's base) of a config."""
+    if cfg["kind"] == "gemv":
+        return (GEMV_METRIC, "GB/s",
+                cfg["layers"] * sum(gemv_bytes(r, c) for r, c in gemv_shapes(cfg)), 1e9)
     if cfg["kind"] == "prefill":
         return PREFILL_METRIC, "TFLOP/s", cfg["layers"] * prefill_flops(cfg), 1e12
     return METRIC, "GB/s", step_bytes(cfg), 1e9
@@ -219,6 +240,21 @@ class RefWorkload:
         import oracle
         self.oracle, self.impl, self.cores, self.cfg = oracle, impl, cores, cfg
         kind, nq, nkv, d = cfg["kind"], cfg["nq"], cfg["nkv"], cfg["d"]
+        if kind == "gemv":
+            self.items = [(0, 0, 0)]
+            self.q4 = []
+            rng0 = np.random.default_rng(3)
+            for r, c in gemv_shapes(cfg):
+                self.q4.append((rng0.uniform(1e-3, 1e-2, (r, c // 32)).astype(np.float32),
+                                rng0.integers(0, 16, (r, c // 32), dtype=np.int8),
+                                rng0.integers(0, 256, (r, c // 2), dtype=np.uint8),
+                                np.zeros((r, c // 32), np.int16),
+                                rng0.standard_normal(c).astype(np.float32)))
+            self.t = [0.0]
+            self.c = [0]
+            self.bytes = 0
+            self.seconds = 0.0
+            return
         if kind == "prefill":
             self.items = [(cfg["prompt"], 0, cfg["window"])]
         elif kind == "single":
@@ -249,9 +285,22 @@ class RefWorkload:
         nq, nkv, d = cfg["nq"], cfg["nkv"], cfg["d"]
         j = i % len(self.items)
         n, pos, w = self.items[j]
+        scale = 1.0 / math.sqrt(d)
+        if cfg["kind"] == "gemv":  # one layer's GEMVs per call
+            t0 = time.perf_counter()
+            for sc, z, data, ws, x in self.q4:
+                self.oracle.gemv_q4((sc, z, data, ws), x,
+                                    impl="ref" if self.impl == "reference" else "port",
+                                    nthreads=self.cores)
+            dt = time.perf_counter() - t0
+            if record:
+                self.t[0] += dt
+                self.c[0] += 1
+                self.bytes += sum(gemv_bytes(r, c) for r, c in gemv_shapes(cfg))
+                self.seconds += dt
+            return dt
         buf = i % len(self.K)
         K, V = self.K[buf][:n], self.V[buf][:n]
-        scale = 1.0 / math.sqrt(d)
         if cfg["kind"] == "prefill":  # n = prompt length, pos0 = 0
             Qm = self.Qm
             t0 = time.perf_counter()
@@ -282,7 +331,7 @@ class RefWorkload:
     def step_seconds(self):
         cfg = self.cfg
         mean = [t / c if c else 0.0 for t, c in zip(self.t, self.c)]
-        if cfg["kind"] in ("single", "prefill"):
+        if cfg["kind"] in ("single", "prefill", "gemv"):
             return cfg["layers"] * mean[0]
         if cfg["kind"] == "gemma":
             ng = sum(1 for w, _ in gemma_layers(cfg) if w == 0)
@@ -290,7 +339,8 @@ class RefWorkload:
         return step_bytes(cfg) / (self.bytes / self.seconds)
 
     def describe(self, what):
-        fn = "attn_prefill_gqa" if self.cfg["kind"] == "prefill" else "attn_decode_gqa_cache"
+        fn = {"prefill": "attn_prefill_gqa", "gemv": "gemv_q4"}.get(self.cfg["kind"],
+                                                                    "attn_decode_gqa_cache")
         return (f"{sum(self.c)} calls of {fn} ({what}), "
                 f"{self.seconds:.1f}s; per-step time extrapolated from per-call means")
 
@@ -322,12 +372,13 @@ def run_reference(args, cfg):
     what = {"single": f"one layer, n={cfg.get('ctx', 0) + 1}",
             "gemma": "a global and a 1024-slot SWA layer, alternating",
             "prefill": f"one layer's attn_prefill_gqa over a {cfg.get('prompt')}-token prompt",
+            "gemv": "one layer's fused-QKV and O gemv_q4",
             }.get(cfg["kind"], "one sequence per call, lengths from the config's seeded draw")
     line = {
         "impl": "reference", "metric": metric, "value": round(value, 3), "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak" if cfg["kind"] in ("single", "gemma", "prefill") else "strong",
+        "scaling": "weak" if cfg["kind"] in ("single", "gemma", "prefill", "gemv") else "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
         "config": {"workload": f"{args.config}: {cfg['desc']} (reference CPU sample)",
                    "layers": cfg["layers"], "nq": cfg["nq"], "nkv": cfg["nkv"],
@@ -848,6 +899,118 @@ def run_prefill(args, cfg):
     return 0
 
 
+def run_gemv(args, cfg):
+    """Q4 projection GEMVs of one decode token (molot_gemv_q4_dev), distinct
+    synthetic weights per layer (seeded random nibbles, scales, zeros)."""
+    rt = Rt()
+    torch = rt.torch
+    import molot_b200 as mb
+
+    L = cfg["layers"]
+    gen = torch.Generator(device=rt.dev)
+    gen.manual_seed(99 + rt.rank)
+    mats = []
+    for _ in range(L):
+        layer = []
+        for r, c in gemv_shapes(cfg):
+            sc = (torch.rand((r, c // 32), device=rt.dev, generator=gen) * 9e-3 + 1e-3).contiguous()
+            z = torch.randint(0, 16, (r, c // 32), device=rt.dev, generator=gen, dtype=torch.int8)
+            data = torch.randint(0, 256, (r, c // 2), device=rt.dev, generator=gen,
+                                 dtype=torch.uint8)
+            layer.append((sc, z, data))
+        mats.append(layer)
+    (r0, c0), (r1, c1) = gemv_shapes(cfg)
+    x = torch.randn((L, c0), device=rt.dev, generator=gen)
+    qkv = torch.empty((L, r0), device=rt.dev)
+    ao = torch.randn((L, c1), device=rt.dev, generator=gen)
+    out = torch.empty((L, r1), device=rt.dev)
+
+    def step(xx, a_in):
+        st = torch.cuda.current_stream()
+        for l in range(L):
+            (s0, z0, d0), (s1, z1, d1) = mats[l]
+            mb.gemv_q4_dev(s0, z0, d0, xx[l], qkv[l], st)
+            mb.gemv_q4_dev(s1, z1, d1, a_in[l], out[l], st)
+
+    for _ in range(args.warmup):
+        step(x, ao)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step(x, ao)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step(x, ao)
+    graph.replay()
+    clocks = ClockSampler(rt.local)
+    clocks.start()
+    time.sleep(0.3)
+    ms = rt.max(rt.timed(graph.replay, args.steps))
+    clk = clocks.stop()
+    # the largest GEMV alone: L back-to-back QKV launches pairs
+    qgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(qgraph):
+        for l in range(L):
+            mb.gemv_q4_dev(mats[l][0][0], mats[l][0][1], mats[l][0][2], x[l], qkv[l])
+    qgraph.replay()
+    q_ms = rt.timed(qgraph.replay, args.steps) / L
+
+    hx = pinned_like(torch, x, 5)
+    ha = pinned_like(torch, ao, 6)
+    ho = torch.empty(out.shape).pin_memory()
+    hq = torch.empty(qkv.shape).pin_memory()
+    dx, da = torch.empty_like(x), torch.empty_like(ao)
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        da.copy_(ha, non_blocking=True)
+        step(dx, da)
+        hq.copy_(qkv, non_blocking=True)
+        ho.copy_(out, non_blocking=True)
+
+    e2e_step()
+    e2e_ms = rt.max(rt.timed(e2e_step, args.steps))
+    del graph, qgraph
+    metric, unit, amount, div = step_work(cfg)
+    peak, peak_kind = hbm_peak()
+    qbytes = gemv_bytes(r0, c0)
+    if rt.rank == 0:
+        value = amount * rt.world / (ms * 1e-3) / div
+        line = {
+            "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": rt.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/f32",
+            "data": "synthetic (seeded random Q4 nibbles, scales, zeros; N(0,1) activations)",
+            "config": {"workload": f"gemv: {cfg['desc']}", "layers": L,
+                       "shapes": [list(s_) for s_ in gemv_shapes(cfg)],
+                       "parallelism": f"replicas x{rt.world}",
+                       "l2": f"{amount / 1e6:.0f} MB of weights per step > L2"},
+            "tok_per_s": round(rt.world * 1000.0 / ms, 1),
+            "pct_hbm_peak": round(100.0 * value / rt.world / peak, 2),
+            "e2e": {"value": round(amount * rt.world / (e2e_ms * 1e-3) / div, 2), "unit": unit,
+                    "h2d_bytes_per_step": int(4 * (x.numel() + ao.numel())),
+                    "d2h_bytes_per_step": int(4 * (qkv.numel() + out.numel())),
+                    "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": 4 * L * args.steps,
+            "roofline": {"bound": "hbm", "achieved": round(qbytes / (q_ms * 1e-3) / 1e9, 1),
+                         "peak": peak, "unit": "GB/s",
+                         "frac": round(qbytes / (q_ms * 1e-3) / 1e9 / peak, 4), "traffic": None,
+                         "kernel": "q8_quantize_kernel + gemv_q4_kernel (fused QKV, 6144x4096)",
+                         "peak_source": f"{peak_kind} hbm_gbs", "bytes_per_launch": qbytes,
+                         "avg_launch_ms": round(q_ms, 5)},
+            "clocks": clk,
+            "path": "molot_gemv_q4_dev x2 per layer",
+        }
+        if rt.world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_sample(cfg)
+        print(json.dumps(line), flush=True)
+    rt.close()
+    return 0
+
+
 def fill_normal(torch, dst, template):
     """Fill a device tensor with N(0,1) values by tiling a seeded template
     (generating tens of GB of normals directly takes too long)."""
@@ -1041,6 +1204,8 @@ def main(argv=None):
         return run_gemma(args, cfg)
     if cfg["kind"] == "prefill":
         return run_prefill(args, cfg)
+    if cfg["kind"] == "gemv":
+        return run_gemv(args, cfg)
     return run_paged(args, cfg)
 
 

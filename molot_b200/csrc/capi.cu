@@ -555,36 +555,33 @@ int host_prefill(const float* Qm, const float* K, const float* V, float* Om, int
 
 // ------------------------------------------------------------- Q4 GEMV
 
-// Quantize x, then y = W x; the packed activations live in the workspace.
+// y = W x in one launch (x is quantized inside it).
 int gemv_q4_launch(Workspace& ws, const float* scales, const int8_t* zeros, const uint8_t* data,
                    int rows, int cols, const float* x, float* y, cudaStream_t st) {
+  (void)ws;
   if (!scales || !zeros || !data || !x || !y) return fail(MOLOT_ERR_INVALID, "null pointer");
   if (rows <= 0 || cols <= 0 || cols % 32)
     return fail(MOLOT_ERR_INVALID, "rows > 0 and cols a positive multiple of 32 required");
-  if (!aligned16(data) || !aligned16(scales))
-    return fail(MOLOT_ERR_INVALID, "data and scales must be 16-byte aligned");
+  if (!aligned16(data) || !aligned16(x))
+    return fail(MOLOT_ERR_INVALID, "data and x must be 16-byte aligned");
+  const int ng = cols / 32;
+  const int smem = gemv_smem_bytes(ng);
+  if (smem > 200 * 1024) return fail(MOLOT_ERR_UNSUPPORTED, "cols too large for the Q4 GEMV");
   int dev, rc;
   if ((rc = current_device(&dev))) return rc;
-  const int ng = cols / 32;
-  // scratch: ng packed groups (8 ints), then ng scales, then ng sums
-  if ((rc = ws.ensure(dev, (size_t)ng * 10 + 16, 0, 0))) return rc;
+  if ((rc = prepare_kernel({reinterpret_cast<const void*>(&gemv_q4_kernel), 200 * 1024}, dev)))
+    return rc;
   GemvQ4Args a = {};
   a.scales = scales;
   a.zeros = zeros;
   a.data = data;
   a.x = x;
   a.y = y;
-  a.xq = reinterpret_cast<Q8Packed*>(ws.partials);
-  a.xs = ws.partials + (size_t)ng * 8;
-  a.xsum = reinterpret_cast<int*>(ws.partials + (size_t)ng * 9);
   a.rows = rows;
   a.cols = cols;
   a.ng = ng;
-  if ((rc = launch(reinterpret_cast<const void*>(&q8_quantize_kernel),
-                   dim3((ng + kGemvWarps - 1) / kGemvWarps), dim3(kGemvWarps * 32), 0, st, &a)))
-    return rc;
   return launch(reinterpret_cast<const void*>(&gemv_q4_kernel),
-                dim3((rows + kGemvWarps - 1) / kGemvWarps), dim3(kGemvWarps * 32), 0, st, &a);
+                dim3((rows + kGemvRows - 1) / kGemvRows), dim3(kGemvWarps * 32), smem, st, &a);
 }
 
 }  // namespace
