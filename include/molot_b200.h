@@ -142,8 +142,11 @@ int molot_attn_prefill_strided_dev(const float* Q, const float* K, const float* 
 int molot_gemv_q4(const float* scales, const int8_t* zeros, const uint8_t* data,
                   const int16_t* wsums, int rows, int cols, const float* x, float* y);
 
-/* molot_gemv_q4 on device buffers (data and scales 16-byte aligned),
- * stream-ordered; two launches (activation quantization, then the GEMV). */
+/* molot_gemv_q4 on device buffers (data and x 16-byte aligned),
+ * stream-ordered, one launch.  The launch fetches weights before it waits
+ * for its predecessor on the stream: do not write W in a kernel that
+ * releases its dependents early (programmatic dependent launch) right
+ * before this call. */
 int molot_gemv_q4_dev(const float* scales, const int8_t* zeros, const uint8_t* data, int rows,
                       int cols, const float* x, float* y, void* stream);
 

@@ -9,13 +9,17 @@
 // own groups and the warp adds the lanes, a reassociation of the same terms.
 //
 // One launch: every CTA first issues the loads of its rows' first weight
-// groups (the weights do not depend on the preceding launch), then waits for
-// that launch (x may be its output), quantizes x into shared memory (per
-// group the 16 even and the 16 odd int8 values, the scale, the sum of the 32
-// values; every CTA repeats this small step, which keeps the GEMV one
-// launch), and finishes its rows: one warp per row, each lane one 16-byte
-// group of nibbles per step (a warp reads 512 contiguous bytes), 8 dp4a per
-// group.  HBM-bound: cols/2 + 5*cols/32 bytes per row.
+// groups, then waits for the preceding launch (x may be its output),
+// quantizes x into shared memory (per group the 16 even and the 16 odd int8
+// values, the scale, the sum of the 32 values; every CTA repeats this small
+// step, which keeps the GEMV one launch), and finishes its rows: a warp owns
+// two rows, each lane one 16-byte group of nibbles per row and step (a warp
+// reads 512 contiguous bytes per row), 8 dp4a per group.  Reading weights
+// before the wait is safe because the launch that precedes a GEMV on the
+// stream does not write weights: the library's kernels release their
+// dependents only after their own wait, and a kernel without that release
+// completes before this one starts.  HBM-bound: cols/2 + 5*cols/32 bytes per
+// row.
 #pragma once
 
 #include <cuda_fp16.h>
