@@ -282,6 +282,35 @@ int molot_paged_append(molot_paged_plan* plan, const float* q, const float* k, c
 /* Synchronises and reports device-side timeouts of the plan's launches. */
 int molot_paged_check(molot_paged_plan* plan, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Continuous-batching page manager: page ids, per-sequence page lists and
+ * lengths, block tables for a batch; optionally the per-layer K/V page pools
+ * ([num_pages][nkv][page_size][d] FP32 each) in HBM.  The reference
+ * specifies this (its DESIGN.md:47-48,101-105) and implements none of it.
+ * Pages come from a LIFO free list, lowest id first in a fresh pager.  One
+ * host thread at a time per call (internally locked).
+ * ---------------------------------------------------------------------- */
+typedef struct molot_pager molot_pager;
+
+/* n_layers = 0: tables only, no device memory (and no CUDA call). */
+int molot_pager_create(int n_layers, int nkv, int d, int page_size, int num_pages, int max_seqs,
+                       int max_pages_per_seq, molot_pager** out);
+void molot_pager_destroy(molot_pager* p);
+/* A new sequence with `slots` slots reserved (its prompt); id in *seq.
+ * MOLOT_ERR_CACHE_FULL when no sequence slot or not enough pages. */
+int molot_pager_add(molot_pager* p, int slots, int* seq);
+/* Reserves n_new more slots (the tokens of the next step); length += n_new. */
+int molot_pager_grow(molot_pager* p, int seq, int n_new);
+/* Returns the sequence's pages to the pool. */
+int molot_pager_free(molot_pager* p, int seq);
+int molot_pager_length(const molot_pager* p, int seq);
+int molot_pager_free_pages(const molot_pager* p);
+/* Host block table [B][max_pages_per_seq] (unused entries 0) and lengths of
+ * the batch `seqs`, ready for molot_paged_plan_build / molot_paged_decode. */
+int molot_pager_tables(molot_pager* p, const int* seqs, int B, int* block_table, int* seq_lens);
+/* Device K/V pools of one layer. */
+int molot_pager_layer_pools(molot_pager* p, int layer, float** k_pool, float** v_pool);
+
 #ifdef __cplusplus
 }
 #endif

@@ -106,6 +106,15 @@ _decl("molot_attn_append_rope_tokens",
       [_p, _i, _p, _p, _p, _p, _p, _p, _i, _f, _p, _i, _i, _i, _p])
 _decl("molot_attn_prefill", [_p, _i, _p, _p, _i, _i, _f, _i, _i, _p])
 _decl("molot_gemv_q4", [_p, _p, _p, _p, _i, _i, _p, _p])
+_decl("molot_pager_create", [_i, _i, _i, _i, _i, _i, _i, _pp])
+_decl("molot_pager_destroy", [_p], None)
+_decl("molot_pager_add", [_p, _i, _p])
+_decl("molot_pager_grow", [_p, _i, _i])
+_decl("molot_pager_free", [_p, _i])
+_decl("molot_pager_length", [_p, _i])
+_decl("molot_pager_free_pages", [_p])
+_decl("molot_pager_tables", [_p, _p, _i, _p, _p])
+_decl("molot_pager_layer_pools", [_p, _i, _pp, _pp])
 _decl("molot_gemv_q4_dev", [_p, _p, _p, _i, _i, _p, _p, _p])
 _decl("molot_paged_plan_create", [_pp])
 _decl("molot_paged_plan_destroy", [_p], None)
@@ -416,6 +425,68 @@ class KVCache:
 
     def check(self, stream=None) -> None:
         check(_lib.molot_kv_check(self._h, _stream_ptr(stream)))
+
+
+class Pager:
+    """Continuous-batching page manager (molot_pager_*): sequences, their
+    pages and lengths, block tables for a batch, optional HBM page pools."""
+
+    def __init__(self, n_layers, nkv, d, page_size, num_pages, max_seqs, max_pages_per_seq):
+        h = ctypes.c_void_p()
+        check(_lib.molot_pager_create(n_layers, nkv, d, page_size, num_pages, max_seqs,
+                                      max_pages_per_seq, ctypes.byref(h)))
+        self._h = h
+        self.n_layers, self.nkv, self.d, self.page_size = n_layers, nkv, d, page_size
+        self.num_pages, self.max_pages = num_pages, max_pages_per_seq
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.molot_pager_destroy(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def add(self, slots: int) -> int:
+        s = ctypes.c_int()
+        check(_lib.molot_pager_add(self._h, slots, ctypes.byref(s)))
+        return s.value
+
+    def grow(self, seq: int, n_new: int = 1) -> None:
+        check(_lib.molot_pager_grow(self._h, seq, n_new))
+
+    def free(self, seq: int) -> None:
+        check(_lib.molot_pager_free(self._h, seq))
+
+    def length(self, seq: int) -> int:
+        r = _lib.molot_pager_length(self._h, seq)
+        if r < 0:
+            check(r)
+        return r
+
+    def free_pages(self) -> int:
+        return _lib.molot_pager_free_pages(self._h)
+
+    def tables(self, seqs):
+        """(block_table int32 [B][max_pages], seq_lens int32 [B]) on the host."""
+        sq = np.ascontiguousarray(seqs, dtype=np.int32)
+        bt = np.zeros((sq.size, self.max_pages), np.int32)
+        lens = np.zeros(sq.size, np.int32)
+        check(_lib.molot_pager_tables(self._h, _ptr(sq), sq.size, _ptr(bt), _ptr(lens)))
+        return bt, lens
+
+    def layer_pools(self, layer: int):
+        """(K, V) torch views [num_pages][nkv][page_size][d] of a layer's pools."""
+        import torch
+        k = ctypes.c_void_p()
+        v = ctypes.c_void_p()
+        check(_lib.molot_pager_layer_pools(self._h, layer, ctypes.byref(k), ctypes.byref(v)))
+        shape = (self.num_pages, self.nkv, self.page_size, self.d)
+        return (torch.as_tensor(_CudaArray(k.value, shape), device="cuda"),
+                torch.as_tensor(_CudaArray(v.value, shape), device="cuda"))
 
 
 class PagedPlan:
