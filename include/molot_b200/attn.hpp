@@ -70,6 +70,12 @@ inline void attn_prefill_gqa(const float* Qm, const float* K, const float* V, fl
   check(molot_attn_prefill_gqa(Qm, K, V, Om, nq, nkv, M, N, d, scale, pos0, window));
 }
 
+// gemm.h:223-254 (Q4 GEMV) on a Q4Matrix given as its arrays, host buffers
+inline void gemv_q4(const float* scales, const int8_t* zeros, const uint8_t* data,
+                    const int16_t* wsums, int rows, int cols, const float* x, float* y) {
+  check(molot_gemv_q4(scales, zeros, data, wsums, rows, cols, x, y));
+}
+
 // forward.h:554-558 for a shared-KV layer's query only: per-head RMSNorm
 // (q_norm may be null) and NEOX RoPE (freq may be null: NoPE), device
 // buffers, stream-ordered.

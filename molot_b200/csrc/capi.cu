@@ -556,9 +556,8 @@ int host_prefill(const float* Qm, const float* K, const float* V, float* Om, int
 // ------------------------------------------------------------- Q4 GEMV
 
 // y = W x in one launch (x is quantized inside it).
-int gemv_q4_launch(Workspace& ws, const float* scales, const int8_t* zeros, const uint8_t* data,
-                   int rows, int cols, const float* x, float* y, cudaStream_t st) {
-  (void)ws;
+int gemv_q4_launch(const float* scales, const int8_t* zeros, const uint8_t* data, int rows,
+                   int cols, const float* x, float* y, cudaStream_t st) {
   if (!scales || !zeros || !data || !x || !y) return fail(MOLOT_ERR_INVALID, "null pointer");
   if (rows <= 0 || cols <= 0 || cols % 32)
     return fail(MOLOT_ERR_INVALID, "rows > 0 and cols a positive multiple of 32 required");
@@ -1091,11 +1090,7 @@ int molot_attn_prefill_gqa(const float* Qm, const float* K, const float* V, floa
 
 int molot_gemv_q4_dev(const float* scales, const int8_t* zeros, const uint8_t* data, int rows,
                       int cols, const float* x, float* y, void* stream) {
-  int dev, rc;
-  if ((rc = current_device(&dev))) return rc;
-  HostCtx& c = host_ctx(dev);
-  std::lock_guard<std::mutex> lk(c.mu);
-  return gemv_q4_launch(c.ws, scales, zeros, data, rows, cols, x, y, (cudaStream_t)stream);
+  return gemv_q4_launch(scales, zeros, data, rows, cols, x, y, (cudaStream_t)stream);
 }
 
 int molot_gemv_q4(const float* scales, const int8_t* zeros, const uint8_t* data,
@@ -1123,7 +1118,7 @@ int molot_gemv_q4(const float* scales, const int8_t* zeros, const uint8_t* data,
   MOLOT_CUDA(cudaMemcpyAsync(dx, x, (size_t)cols * 4, cudaMemcpyHostToDevice, c.stream));
   MOLOT_CUDA(cudaMemcpyAsync(dz, zeros, nsc, cudaMemcpyHostToDevice, c.stream));
   MOLOT_CUDA(cudaMemcpyAsync(dd, data, (size_t)rows * cols / 2, cudaMemcpyHostToDevice, c.stream));
-  rc = gemv_q4_launch(c.ws, dsc, reinterpret_cast<const int8_t*>(dz), dd, rows, cols, dx, dy,
+  rc = gemv_q4_launch(dsc, reinterpret_cast<const int8_t*>(dz), dd, rows, cols, dx, dy,
                       c.stream);
   if (rc) return rc;
   MOLOT_CUDA(cudaMemcpyAsync(y, dy, (size_t)rows * 4, cudaMemcpyDeviceToHost, c.stream));

@@ -175,6 +175,39 @@ int main() {
     cudaFree(dkn);
     cudaFree(dfreq);
   }
+  // ---- attn_prefill_gqa on host buffers (gemm.h:409-446)
+  {
+    const int nq = 16, nkv = 4, d = 128, M = 50, pos0 = 30, N = pos0 + M;
+    std::vector<float> Q((size_t)M * nq * d), K((size_t)N * nkv * d), V(K.size()),
+        O(Q.size()), R(Q.size());
+    for (auto& x : Q) x = frand();
+    for (auto& x : K) x = frand();
+    for (auto& x : V) x = frand();
+    molot_b200::attn_prefill_gqa(Q.data(), K.data(), V.data(), O.data(), nq, nkv, M, N, d, 0.0884f,
+                                 pos0, 24);
+    oracle_attn_prefill_gqa(Q.data(), K.data(), V.data(), R.data(), nq, nkv, M, N, d, 0.0884f,
+                            pos0, 24);
+    const double e = rel_err(O, R);
+    CHECK(e <= 1e-5, "attn_prefill_gqa rel err %g", e);
+    std::printf("[ok] attn_prefill_gqa M=%d rel_err=%.2e\n", M, e);
+  }
+  // ---- gemv_q4 on host buffers (gemm.h:223-254)
+  {
+    const int rows = 512, cols = 2048, ng = cols / 32;
+    std::vector<float> W((size_t)rows * cols), x(cols), y(rows), r(rows), sc((size_t)rows * ng);
+    std::vector<int8_t> z((size_t)rows * ng);
+    std::vector<uint8_t> data((size_t)rows * cols / 2);
+    std::vector<int16_t> ws((size_t)rows * ng);
+    for (auto& v : W) v = 0.02f * frand();
+    for (auto& v : x) v = frand();
+    oracle_quantize_q4(W.data(), rows, cols, sc.data(), z.data(), data.data(), ws.data());
+    molot_b200::gemv_q4(sc.data(), z.data(), data.data(), ws.data(), rows, cols, x.data(),
+                        y.data());
+    oracle_gemv_q4(sc.data(), z.data(), data.data(), rows, cols, x.data(), r.data());
+    const double e = rel_err(y, r);
+    CHECK(e <= 1e-6, "gemv_q4 rel err %g", e);
+    std::printf("[ok] gemv_q4 %dx%d rel_err=%.2e\n", rows, cols, e);
+  }
   if (failures) {
     std::printf("CORRECTNESS: %d FAILURES\n", failures);
     return 1;
