@@ -429,10 +429,17 @@ def run_single(args, cfg):
     stream = torch.cuda.current_stream()
 
     bf16 = args.kv == "bf16"
+    q8 = args.kv == "q8"
     cache = mb.KVCache(L, nkv, d, n, dtype=args.kv)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
     for layer in range(L):
+        if q8:  # rows enter through the library's quantizing write
+            rows_k = torch.randn((ctx, nkv * d), device=dev, generator=gen)
+            rows_v = torch.randn((ctx, nkv * d), device=dev, generator=gen)
+            cache.write(layer, 0, rows_k, rows_v)
+            del rows_k, rows_v
+            continue
         kt, vt = cache.layer_tensors(layer)  # head-major [nkv][cap][hd]
         kt[:, :ctx].normal_(generator=gen)
         vt[:, :ctx].normal_(generator=gen)
@@ -546,13 +553,15 @@ def run_single(args, cfg):
     cache.check(stream)
     del graph, dgraph
 
-    kv_bytes_layer = 2 * nkv * n * d * (2 if bf16 else 4)
+    row_bytes = mb.q8_row_bytes(d) if q8 else d * (2 if bf16 else 4)
+    kv_bytes_layer = 2 * nkv * n * row_bytes
     total_bytes = kv_bytes_layer * L * world
     value = total_bytes / (ms * 1e-3) / 1e9
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
     peak, peak_kind = hbm_peak()
     achieved = kv_bytes_layer / (dec_avg_ms * 1e-3) / 1e9
-    traffic = read_traffic("gqa_decode_kernel", args.config + ("-bf16" if bf16 else ""))
+    traffic = read_traffic("gqa_decode_kernel",
+                           args.config + ("-" + args.kv if args.kv != "f32" else ""))
 
     result = None
     if rank == 0:
@@ -580,7 +589,8 @@ def run_single(args, cfg):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic,
-                         "kernel": "gqa_decode_kernel<128,4,1%s>" % (",bf16" if bf16 else ""),
+                         "kernel": "gqa_decode_kernel<128,4,1%s>" % (
+                             "," + args.kv if args.kv != "f32" else ""),
                          "timed": ("fused step launches (prologue + append + decode)" if fused
                                    else "decode launches alone"),
                          "peak_source": f"{peak_kind} hbm_gbs",
@@ -1184,8 +1194,9 @@ def main(argv=None):
     ap.add_argument("--path", choices=["fused", "split"], default="fused",
                     help="fused: molot_attn_step (one launch per layer); split: "
                          "molot_attn_append_rope + molot_attn_decode")
-    ap.add_argument("--kv", choices=["f32", "bf16"], default="f32",
-                    help="KV-cache storage of cfg1/cfg2 (bf16: half the bytes, FP32 math)")
+    ap.add_argument("--kv", choices=["f32", "bf16", "q8"], default="f32",
+                    help="KV-cache storage of cfg1/cfg2 (bf16: half the bytes; q8: int8 "
+                         "codes + per-32 scales, 0.28x the bytes; FP32 math throughout)")
     ap.add_argument("--resident-gb", type=float, default=40.0,
                     help="cfg4/cfg5: device memory for distinct layer pools per rank")
     ap.add_argument("--layers", type=int, default=0,

@@ -175,24 +175,36 @@ typedef struct molot_kv_cache molot_kv_cache;
 /* KV element types of the handle. */
 enum molot_kv_dtype {
   MOLOT_KV_F32 = 0, /* the reference's format (bit-exact QK scores) */
-  MOLOT_KV_BF16 = 1 /* half the bytes; the reference specifies but does not
-                       implement it: results match the reference run on the
-                       bf16-rounded cache */
+  MOLOT_KV_BF16 = 1, /* half the bytes; the reference specifies but does not
+                        implement it: results match the reference run on the
+                        bf16-rounded cache */
+  MOLOT_KV_Q8 = 2 /* ~0.28x the bytes (the Q8 KV of the reference's design,
+                     DESIGN.md:48,87-88, deferred at exp/README.md:36-39): a
+                     row is hd int8 codes then hd/32 FP32 scales, padded to
+                     16 bytes; each 32-value block quantized by the rule of
+                     quant.h:33-43 (s = absmax/127, q = nearbyint(x/s)).
+                     Results match the reference run on the dequantized
+                     cache (q*s) within the parity tolerance.  Decode, step,
+                     append and write only: prefill returns
+                     MOLOT_ERR_UNSUPPORTED. */
 };
 
 int molot_kv_create(int n_layers, int nkv, int hd, int cap, molot_kv_cache** out);
 /* molot_kv_create with a storage type.  With MOLOT_KV_BF16 every row that
  * enters the cache (write, append, step, prefill prologue) is rounded to
- * bf16 (nearest even); attention math stays FP32. */
+ * bf16 (nearest even), with MOLOT_KV_Q8 quantized per 32 values; attention
+ * math stays FP32. */
 int molot_kv_create_ex(int n_layers, int nkv, int hd, int cap, int kv_dtype,
                        molot_kv_cache** out);
-/* MOLOT_KV_F32 or MOLOT_KV_BF16 (or a negative status). */
+/* MOLOT_KV_F32, MOLOT_KV_BF16 or MOLOT_KV_Q8 (or a negative status). */
 int molot_kv_dtype(const molot_kv_cache* kv);
 void molot_kv_destroy(molot_kv_cache* kv);
 int molot_kv_length(const molot_kv_cache* kv, int layer);
 int molot_kv_set_length(molot_kv_cache* kv, int layer, int n);
 /* Device base of a layer's K and V ([nkv][cap][hd]); the elements are
- * uint16 bf16 bit patterns for MOLOT_KV_BF16 handles despite the type. */
+ * uint16 bf16 bit patterns for MOLOT_KV_BF16 handles despite the type, and
+ * a MOLOT_KV_Q8 layer is bytes, [nkv][cap][row] with row = hd codes, hd/32
+ * float scales, padding to a multiple of 16 bytes. */
 int molot_kv_layer_data(molot_kv_cache* kv, int layer, float** k, float** v);
 
 /* Copies nrows rows of K and V (each [nrows][nkv*hd] FP32, host or device

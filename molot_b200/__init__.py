@@ -42,6 +42,24 @@ ERR_NO_DEVICE = -8
 
 KV_F32 = 0   # molot_kv_dtype: the reference's FP32 cache
 KV_BF16 = 1  # BF16 storage (rounded on entry), FP32 math
+KV_Q8 = 2    # int8 codes + per-32 FP32 scales per row, FP32 math
+_KV_DTYPES = {"f32": KV_F32, "bf16": KV_BF16, "q8": KV_Q8}
+
+
+def q8_row_bytes(hd: int) -> int:
+    """Bytes of one Q8 cache row: hd int8 codes, hd/32 float32 scales,
+    padded to a multiple of 16."""
+    return (hd + hd // 8 + 15) & ~15
+
+
+def q8_unpack(rows, hd: int):
+    """Q8 cache rows (uint8 [..., q8_row_bytes(hd)], numpy) -> (codes int8
+    [..., hd], scales float32 [..., hd/32]); values read back as
+    codes * scales repeated over each 32-value block."""
+    rows = np.ascontiguousarray(rows, dtype=np.uint8)
+    codes = rows[..., :hd].view(np.int8)
+    scales = np.ascontiguousarray(rows[..., hd:hd + hd // 8]).view(np.float32)
+    return codes, scales
 
 
 class MolotError(RuntimeError):
@@ -325,11 +343,11 @@ class KVCache:
     """HBM-resident per-layer KV cache (replaces forward.h's Runner::KVC)."""
 
     def __init__(self, n_layers: int, nkv: int, hd: int, cap: int, dtype: str = "f32"):
-        if dtype not in ("f32", "bf16"):
-            raise ValueError("dtype must be 'f32' or 'bf16'")
+        if dtype not in _KV_DTYPES:
+            raise ValueError("dtype must be 'f32', 'bf16' or 'q8'")
         h = ctypes.c_void_p()
-        check(_lib.molot_kv_create_ex(n_layers, nkv, hd, cap,
-                                      KV_BF16 if dtype == "bf16" else KV_F32, ctypes.byref(h)))
+        check(_lib.molot_kv_create_ex(n_layers, nkv, hd, cap, _KV_DTYPES[dtype],
+                                      ctypes.byref(h)))
         self._h = h
         self.n_layers, self.nkv, self.hd, self.cap = n_layers, nkv, hd, cap
         self.dtype = dtype
@@ -366,10 +384,15 @@ class KVCache:
 
     def layer_tensors(self, layer: int):
         """(K, V) torch views [nkv][cap][hd] (head-major) of the layer's
-        device memory: float32, or bfloat16 for a bf16 cache."""
+        device memory: float32, or bfloat16 for a bf16 cache; a q8 cache
+        gives uint8 [nkv][cap][q8_row_bytes(hd)] (see q8_unpack)."""
         import torch
         kp, vp = self.layer_ptrs(layer)
         shape = (self.nkv, self.cap, self.hd)
+        if self.dtype == "q8":
+            shape = (self.nkv, self.cap, q8_row_bytes(self.hd))
+            return (torch.as_tensor(_CudaArray(kp, shape, "|u1"), device="cuda"),
+                    torch.as_tensor(_CudaArray(vp, shape, "|u1"), device="cuda"))
         if self.dtype == "bf16":
             return (torch.as_tensor(_CudaArray(kp, shape, "<i2"), device="cuda").view(torch.bfloat16),
                     torch.as_tensor(_CudaArray(vp, shape, "<i2"), device="cuda").view(torch.bfloat16))

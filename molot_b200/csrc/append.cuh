@@ -14,10 +14,60 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <type_traits>
 
 #include "ptx.cuh"
 
 namespace molot {
+
+// Q8 KV storage (the reduced format the reference's design names for its
+// KV cache, DESIGN.md:48,87-88, left unimplemented there): a row of D
+// values is D int8 followed by D/32 FP32 scales, one per 32 consecutive
+// values, padded to a multiple of 16 bytes.  Each 32-value block is
+// quantized with the reference's Q8 rule (quant.h:33-43, quantize_q8_row:
+// s = absmax/127, 1 when that is not > 0; q = nearbyint(x/s) clamped to
+// [-127, 127]) as the reference's -ffast-math build evaluates it: s =
+// absmax * (1/127) and x/s = x * (127/absmax), each a correctly rounded FP32
+// operation.  A value reads back as (float)q * s.  Strides and offsets of a
+// Q8 cache count bytes.
+struct Q8Row {};
+static_assert(sizeof(Q8Row) == 1, "Q8 row pointers step in bytes");
+__host__ __device__ constexpr int q8_row_bytes(int D) { return (D + D / 8 + 15) & ~15; }
+
+// Row pitch of a cache in its stride units (elements; bytes for Q8).
+template <class CT>
+__host__ __device__ constexpr int row_pitch(int D) {
+  return std::is_same<CT, Q8Row>::value ? q8_row_bytes(D) : D;
+}
+
+// One 32-value block held by a full warp (lane = element of the block):
+// returns this lane's code, the block's scale in s.
+__device__ __forceinline__ int q8_quantize(float x, float& s) {
+  float amax = fabsf(x);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  s = __fmul_rn(amax, 0x1.020408p-7f);  // the FP32 value of 1/127
+  if (!(s > 0.f)) {  // an all-zero block
+    s = 1.0f;
+    return 0;
+  }
+  const int v = __float2int_rn(__fmul_rn(x, __fdiv_rn(127.0f, amax)));  // ties to even
+  return v > 127 ? 127 : (v < -127 ? -127 : v);
+}
+
+__device__ __forceinline__ void q8_put(unsigned char* row, int D, int block, int lane, int q,
+                                       float s) {
+  row[32 * block + lane] = (unsigned char)(signed char)q;
+  if (lane == 0) *reinterpret_cast<float*>(row + D + 4 * block) = s;
+}
+
+// Quantizes block `block` of a row from one value per lane and stores it.
+__device__ __forceinline__ void q8_store_block(float x, unsigned char* row, int D, int block,
+                                               int lane) {
+  float s;
+  const int q = q8_quantize(x, s);
+  q8_put(row, D, block, lane, q, s);
+}
 
 struct AppendArgs {
   // Inputs of sequence b: q [nq][D] at q_in + b*q_bstride; k, v [nkv][D] at
@@ -82,7 +132,7 @@ __device__ __forceinline__ CT* cache_row(const AppendArgs& a, CT* base, int b, i
   if (a.block_table) {
     const int p = a.block_table[(long long)b * a.bt_stride + slot / a.page_size];
     return base + (long long)p * a.page_stride + (long long)g * a.page_hstride +
-           (long long)(slot % a.page_size) * D;
+           (long long)(slot % a.page_size) * row_pitch<CT>(D);
   }
   return base + (long long)b * a.kv_bstride + (long long)slot * a.stride_t +
          (long long)g * a.stride_h;
@@ -92,6 +142,8 @@ template <int D, class CT = float>
 __global__ void __launch_bounds__(kAppendWarps * 32)
     norm_rope_append_kernel(const __grid_constant__ AppendArgs a) {
   static_assert(D % 16 == 0, "head dim must be a multiple of 16");
+  constexpr bool kQ8 = std::is_same<CT, Q8Row>::value;
+  static_assert(!kQ8 || D % 64 == 0, "Q8 rows: both halves must be whole 32-value blocks");
   constexpr int H = D / 2;
   // Programmatic dependent launch: the next launch (the decode) may start at
   // once -- it streams only KV rows older than the one written here until it
@@ -138,6 +190,10 @@ __global__ void __launch_bounds__(kAppendWarps * 32)
     if (is_q) {
       qdst[i] = y0;
       qdst[i + H] = y1;
+    } else if constexpr (kQ8) {  // H % 32 == 0: the loop is warp-uniform
+      unsigned char* row = reinterpret_cast<unsigned char*>(kdst);
+      q8_store_block(y0, row, D, i >> 5, lane);
+      q8_store_block(y1, row, D, (i + H) >> 5, lane);
     } else {
       cache_store(kdst + i, y0);
       cache_store(kdst + i + H, y1);
@@ -154,8 +210,13 @@ __global__ void __launch_bounds__(kAppendWarps * 32)
     }
     CT* vdst = cache_row(a, static_cast<CT*>(a.V), b, g, slot, D);
     const float* vh = vin + (long long)g * D;
-    for (int i = lane; i < D; i += 32)
-      cache_store(vdst + i, a.v_norm ? __fmul_rn(vh[i], vinv) : vh[i]);
+    for (int i = lane; i < D; i += 32) {
+      const float y = a.v_norm ? __fmul_rn(vh[i], vinv) : vh[i];
+      if constexpr (kQ8)
+        q8_store_block(y, reinterpret_cast<unsigned char*>(vdst), D, i >> 5, lane);
+      else
+        cache_store(vdst + i, y);
+    }
   }
 }
 
@@ -178,6 +239,22 @@ __global__ void kv_rows_to_cache_kernel(const float* __restrict__ k, const float
     cache_store(kc + off + j, ks[j]);
     cache_store(vc + off + j, vs[j]);
   }
+}
+
+// The same bulk write into a Q8 cache (row pitch q8_row_bytes(D), stride_h
+// in bytes): one CTA of D threads per (row, head), warp w quantizes block w.
+template <class CT>
+__global__ void kv_rows_to_cache_q8_kernel(const float* __restrict__ k,
+                                           const float* __restrict__ v, unsigned char* kc,
+                                           unsigned char* vc, int slot0, int nkv, int D,
+                                           long long stride_h) {
+  static_assert(std::is_same<CT, Q8Row>::value, "Q8 caches only");
+  const int r = blockIdx.x, g = blockIdx.y;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long src = ((long long)r * nkv + g) * D + threadIdx.x;
+  const long long off = (long long)g * stride_h + (long long)(slot0 + r) * q8_row_bytes(D);
+  q8_store_block(k[src], kc + off, D, w, lane);
+  q8_store_block(v[src], vc + off, D, w, lane);
 }
 
 }  // namespace molot

@@ -165,92 +165,71 @@ KernelRef decode_ref() {
           DecodeSmem<D, GS, KT>::kTotal};
 }
 
-// BF16 caches (the KV handle's storage option): the same group splits.
-bool pick_decode_bf16(int D, int G, KernelRef* k) {
-  using B = __nv_bfloat16;
+// Kernel of a head_dim / group size, for every cache storage type (the
+// same group splits throughout).
+template <class KT>
+bool pick_decode_t(int D, int G, KernelRef* k) {
   switch (D) {
     case 64:
       switch (G) {
-        case 1: *k = decode_ref<64, 1, 1, B>(); return true;
-        case 2: *k = decode_ref<64, 2, 1, B>(); return true;
-        case 4: *k = decode_ref<64, 4, 1, B>(); return true;
-        case 8: *k = decode_ref<64, 8, 1, B>(); return true;
-        case 16: *k = decode_ref<64, 8, 2, B>(); return true;
-        case 32: *k = decode_ref<64, 8, 4, B>(); return true;
+        case 1: *k = decode_ref<64, 1, 1, KT>(); return true;
+        case 2: *k = decode_ref<64, 2, 1, KT>(); return true;
+        case 4: *k = decode_ref<64, 4, 1, KT>(); return true;
+        case 8: *k = decode_ref<64, 8, 1, KT>(); return true;
+        case 16: *k = decode_ref<64, 8, 2, KT>(); return true;
+        case 32: *k = decode_ref<64, 8, 4, KT>(); return true;
       }
       return false;
     case 128:
       switch (G) {
-        case 1: *k = decode_ref<128, 1, 1, B>(); return true;
-        case 2: *k = decode_ref<128, 2, 1, B>(); return true;
-        case 4: *k = decode_ref<128, 4, 1, B>(); return true;
-        case 8: *k = decode_ref<128, 4, 2, B>(); return true;
-        case 16: *k = decode_ref<128, 4, 4, B>(); return true;
-        case 32: *k = decode_ref<128, 4, 8, B>(); return true;
+        case 1: *k = decode_ref<128, 1, 1, KT>(); return true;
+        case 2: *k = decode_ref<128, 2, 1, KT>(); return true;
+        case 4: *k = decode_ref<128, 4, 1, KT>(); return true;
+        case 8: *k = decode_ref<128, 4, 2, KT>(); return true;
+        case 16: *k = decode_ref<128, 4, 4, KT>(); return true;
+        case 32: *k = decode_ref<128, 4, 8, KT>(); return true;
       }
       return false;
     case 256:
       switch (G) {
-        case 1: *k = decode_ref<256, 1, 1, B>(); return true;
-        case 2: *k = decode_ref<256, 2, 1, B>(); return true;
-        case 4: *k = decode_ref<256, 2, 2, B>(); return true;
-        case 8: *k = decode_ref<256, 2, 4, B>(); return true;
-        case 16: *k = decode_ref<256, 2, 8, B>(); return true;
+        case 1: *k = decode_ref<256, 1, 1, KT>(); return true;
+        case 2: *k = decode_ref<256, 2, 1, KT>(); return true;
+        case 4: *k = decode_ref<256, 2, 2, KT>(); return true;
+        case 8: *k = decode_ref<256, 2, 4, KT>(); return true;
+        case 16: *k = decode_ref<256, 2, 8, KT>(); return true;
       }
       return false;
   }
   return false;
 }
 
-bool pick_decode(int D, int G, KernelRef* k) {
-  switch (D) {
-    case 64:
-      switch (G) {
-        case 1: *k = decode_ref<64, 1, 1>(); return true;
-        case 2: *k = decode_ref<64, 2, 1>(); return true;
-        case 4: *k = decode_ref<64, 4, 1>(); return true;
-        case 8: *k = decode_ref<64, 8, 1>(); return true;
-        case 16: *k = decode_ref<64, 8, 2>(); return true;
-        case 32: *k = decode_ref<64, 8, 4>(); return true;
-      }
-      return false;
-    case 128:
-      switch (G) {
-        case 1: *k = decode_ref<128, 1, 1>(); return true;
-        case 2: *k = decode_ref<128, 2, 1>(); return true;
-        case 4: *k = decode_ref<128, 4, 1>(); return true;
-        case 8: *k = decode_ref<128, 4, 2>(); return true;
-        case 16: *k = decode_ref<128, 4, 4>(); return true;
-        case 32: *k = decode_ref<128, 4, 8>(); return true;
-      }
-      return false;
-    case 256:
-      switch (G) {
-        case 1: *k = decode_ref<256, 1, 1>(); return true;
-        case 2: *k = decode_ref<256, 2, 1>(); return true;
-        case 4: *k = decode_ref<256, 2, 2>(); return true;
-        case 8: *k = decode_ref<256, 2, 4>(); return true;
-        case 16: *k = decode_ref<256, 2, 8>(); return true;
-      }
-      return false;
+bool pick_decode(int D, int G, KernelRef* k) { return pick_decode_t<float>(D, G, k); }
+
+// kvt: the cache's molot_kv_dtype.
+bool pick_decode_kv(int D, int G, int kvt, KernelRef* k) {
+  switch (kvt) {
+    case MOLOT_KV_BF16: return pick_decode_t<__nv_bfloat16>(D, G, k);
+    case MOLOT_KV_Q8: return pick_decode_t<Q8Row>(D, G, k);
   }
-  return false;
+  return pick_decode_t<float>(D, G, k);
 }
 
-const void* pick_append(int D, bool bf16 = false) {
-  using B = __nv_bfloat16;
+template <class CT>
+const void* pick_append_t(int D) {
   switch (D) {
-    case 64:
-      return bf16 ? reinterpret_cast<const void*>(&norm_rope_append_kernel<64, B>)
-                  : reinterpret_cast<const void*>(&norm_rope_append_kernel<64>);
-    case 128:
-      return bf16 ? reinterpret_cast<const void*>(&norm_rope_append_kernel<128, B>)
-                  : reinterpret_cast<const void*>(&norm_rope_append_kernel<128>);
-    case 256:
-      return bf16 ? reinterpret_cast<const void*>(&norm_rope_append_kernel<256, B>)
-                  : reinterpret_cast<const void*>(&norm_rope_append_kernel<256>);
+    case 64: return reinterpret_cast<const void*>(&norm_rope_append_kernel<64, CT>);
+    case 128: return reinterpret_cast<const void*>(&norm_rope_append_kernel<128, CT>);
+    case 256: return reinterpret_cast<const void*>(&norm_rope_append_kernel<256, CT>);
   }
   return nullptr;
+}
+
+const void* pick_append(int D, int kvt = MOLOT_KV_F32) {
+  switch (kvt) {
+    case MOLOT_KV_BF16: return pick_append_t<__nv_bfloat16>(D);
+    case MOLOT_KV_Q8: return pick_append_t<Q8Row>(D);
+  }
+  return pick_append_t<float>(D);
 }
 
 int prepare_kernel(const KernelRef& k, int dev) {
@@ -290,10 +269,10 @@ int window_start(int pos_cur, int window) {
   return (window > 0 && pos_cur - window + 1 > 0) ? pos_cur - window + 1 : 0;
 }
 
-int check_shape(int nq, int nkv, int d, KernelRef* k, bool bf16 = false) {
+int check_shape(int nq, int nkv, int d, KernelRef* k, int kvt = MOLOT_KV_F32) {
   if (nq <= 0 || nkv <= 0 || d <= 0) return fail(MOLOT_ERR_INVALID, "nq, nkv and d must be > 0");
   if (nq % nkv) return fail(MOLOT_ERR_INVALID, "nq must be a multiple of nkv");
-  if (!(bf16 ? pick_decode_bf16(d, nq / nkv, k) : pick_decode(d, nq / nkv, k)))
+  if (!pick_decode_kv(d, nq / nkv, kvt, k))
     return fail(MOLOT_ERR_UNSUPPORTED, "head_dim / group size combination not built: d=" +
                                            std::to_string(d) +
                                            " group=" + std::to_string(nq / nkv));
@@ -312,9 +291,9 @@ int decode_uniform(Workspace& ws, const float* Q, float* O, const void* K, const
                    int nq, int nkv, int n, int d, long long stride_t, long long stride_h,
                    float scale, int pos_cur, int window, cudaStream_t st,
                    bool prefetch_old_rows = false, const DecodeArgs* fused = nullptr,
-                   bool bf16 = false) {
+                   int kvt = MOLOT_KV_F32) {
   KernelRef k;
-  int rc = check_shape(nq, nkv, d, &k, bf16);
+  int rc = check_shape(nq, nkv, d, &k, kvt);
   if (rc) return rc;
   if (!Q || !O || !K || !V) return fail(MOLOT_ERR_INVALID, "null pointer");
   if (n < 0) return fail(MOLOT_ERR_INVALID, "n must be >= 0");
@@ -378,8 +357,8 @@ int decode_uniform(Workspace& ws, const float* Q, float* O, const void* K, const
   return launch_decode(k, a, st);
 }
 
-int append_launch(const AppendArgs& a, int d, int B, cudaStream_t st, bool bf16 = false) {
-  const void* fn = pick_append(d, bf16);
+int append_launch(const AppendArgs& a, int d, int B, cudaStream_t st, int kvt = MOLOT_KV_F32) {
+  const void* fn = pick_append(d, kvt);
   if (!fn) return fail(MOLOT_ERR_UNSUPPORTED, "head_dim not built: " + std::to_string(d));
   const int heads = a.nq + a.nkv;
   AppendArgs copy = a;
@@ -599,12 +578,13 @@ struct molot_kv_cache {
   int device = -1;
   int n_layers = 0, nkv = 0, hd = 0, cap = 0;
   int dtype = MOLOT_KV_F32;
-  size_t elem = 4;          // bytes per cache element
-  size_t layer_floats = 0;  // elements per K (or V) of one layer, padded
+  size_t elem = 4;         // bytes per stride unit (element; 1 for Q8)
+  size_t layer_units = 0;  // stride units per K (or V) of one layer, padded
   unsigned char* base = nullptr;
-  float* staging = nullptr;  // device copy of host rows for BF16 writes
+  float* staging = nullptr;  // device copy of host rows for BF16 / Q8 writes
   size_t staging_cap = 0;    // floats
-  bool bf16() const { return dtype == MOLOT_KV_BF16; }
+  // Row pitch in stride units: hd elements, or a Q8 row's bytes.
+  int rs() const { return dtype == MOLOT_KV_Q8 ? q8_row_bytes(hd) : hd; }
   std::vector<int> len;
   Workspace ws;
   // The handle's two most recent kernel launches on its stream (index 0 =
@@ -769,7 +749,7 @@ int append_strided(const float* q, const float* k, const float* v, float* q_out,
                    const float* q_norm, const float* k_norm, int v_norm, float eps,
                    const float* freq, int pos, float* kc, float* vc, int slot, int nq, int nkv,
                    int d, long long stride_t, long long stride_h, cudaStream_t st,
-                   bool bf16 = false) {
+                   int kvt = MOLOT_KV_F32) {
   // k, v, kc and vc all null: q only (a shared-KV layer's query, forward.h:554-558)
   const bool q_only = !k && !v && !kc && !vc;
   if (!q || !q_out || (!q_only && (!k || !v || !kc || !vc)))
@@ -793,7 +773,7 @@ int append_strided(const float* q, const float* k, const float* v, float* q_out,
   a.V = vc;
   a.stride_t = stride_t;
   a.stride_h = stride_h;
-  return append_launch(a, d, 1, st, bf16);
+  return append_launch(a, d, 1, st, kvt);
 }
 }  // namespace
 }  // namespace molot
@@ -823,9 +803,9 @@ int molot_kv_create_ex(int n_layers, int nkv, int hd, int cap, int kv_dtype,
   *out = nullptr;
   if (n_layers <= 0 || nkv <= 0 || hd <= 0 || cap <= 0)
     return fail(MOLOT_ERR_INVALID, "sizes must be positive");
-  if (kv_dtype != MOLOT_KV_F32 && kv_dtype != MOLOT_KV_BF16)
-    return fail(MOLOT_ERR_INVALID, "kv_dtype must be MOLOT_KV_F32 or MOLOT_KV_BF16");
-  if (!pick_append(hd)) return fail(MOLOT_ERR_UNSUPPORTED, "head_dim not built");
+  if (kv_dtype != MOLOT_KV_F32 && kv_dtype != MOLOT_KV_BF16 && kv_dtype != MOLOT_KV_Q8)
+    return fail(MOLOT_ERR_INVALID, "kv_dtype must be MOLOT_KV_F32, MOLOT_KV_BF16 or MOLOT_KV_Q8");
+  if (!pick_append(hd, kv_dtype)) return fail(MOLOT_ERR_UNSUPPORTED, "head_dim not built");
   int dev, rc;
   if ((rc = current_device(&dev))) return rc;
   auto* kv = new molot_kv_cache();
@@ -835,10 +815,11 @@ int molot_kv_create_ex(int n_layers, int nkv, int hd, int cap, int kv_dtype,
   kv->hd = hd;
   kv->cap = cap;
   kv->dtype = kv_dtype;
-  kv->elem = kv_dtype == MOLOT_KV_BF16 ? 2 : 4;
-  kv->layer_floats = ((size_t)cap * nkv * hd + 127) & ~size_t(127);  // 256-byte aligned layers
+  kv->elem = kv_dtype == MOLOT_KV_BF16 ? 2 : (kv_dtype == MOLOT_KV_Q8 ? 1 : 4);
+  const size_t align = 256 / kv->elem;  // 256-byte aligned layers
+  kv->layer_units = ((size_t)cap * nkv * kv->rs() + align - 1) & ~(align - 1);
   kv->len.assign(n_layers, 0);
-  cudaError_t e = cudaMalloc(&kv->base, kv->layer_floats * 2 * n_layers * kv->elem);
+  cudaError_t e = cudaMalloc(&kv->base, kv->layer_units * 2 * n_layers * kv->elem);
   if (e != cudaSuccess) {
     delete kv;
     return cuda_fail(e, "cudaMalloc(kv cache)");
@@ -874,8 +855,8 @@ int molot_kv_set_length(molot_kv_cache* kv, int layer, int n) {
 
 int molot_kv_layer_data(molot_kv_cache* kv, int layer, float** k, float** v) {
   if (!kv || layer < 0 || layer >= kv->n_layers) return fail(MOLOT_ERR_INVALID, "bad layer");
-  if (k) *k = reinterpret_cast<float*>(kv->base + (size_t)(2 * layer) * kv->layer_floats * kv->elem);
-  if (v) *v = reinterpret_cast<float*>(kv->base + (size_t)(2 * layer + 1) * kv->layer_floats * kv->elem);
+  if (k) *k = reinterpret_cast<float*>(kv->base + (size_t)(2 * layer) * kv->layer_units * kv->elem);
+  if (v) *v = reinterpret_cast<float*>(kv->base + (size_t)(2 * layer + 1) * kv->layer_units * kv->elem);
   return MOLOT_OK;
 }
 
@@ -888,7 +869,7 @@ int molot_kv_write(molot_kv_cache* kv, int layer, int slot0, int nrows, const fl
   kv->ordered();
   float *kc, *vc;
   molot_kv_layer_data(kv, layer, &kc, &vc);
-  if (kv->bf16()) {
+  if (kv->dtype != MOLOT_KV_F32) {
     // Rows are converted on the device; host rows are staged there first.
     const size_t n = (size_t)nrows * kv->nkv * kv->hd;
     cudaPointerAttributes pa{};
@@ -911,9 +892,14 @@ int molot_kv_write(molot_kv_cache* kv, int layer, int slot0, int nrows, const fl
       ks = kv->staging;
       vs = kv->staging + n;
     }
-    kv_rows_to_cache_kernel<__nv_bfloat16><<<dim3(nrows, kv->nkv), 128, 0, st>>>(
-        ks, vs, reinterpret_cast<__nv_bfloat16*>(kc), reinterpret_cast<__nv_bfloat16*>(vc), slot0,
-        kv->nkv, kv->hd, (long long)kv->cap * kv->hd);
+    if (kv->dtype == MOLOT_KV_Q8)
+      kv_rows_to_cache_q8_kernel<Q8Row><<<dim3(nrows, kv->nkv), kv->hd, 0, st>>>(
+          ks, vs, reinterpret_cast<unsigned char*>(kc), reinterpret_cast<unsigned char*>(vc),
+          slot0, kv->nkv, kv->hd, (long long)kv->cap * kv->rs());
+    else
+      kv_rows_to_cache_kernel<__nv_bfloat16><<<dim3(nrows, kv->nkv), 128, 0, st>>>(
+          ks, vs, reinterpret_cast<__nv_bfloat16*>(kc), reinterpret_cast<__nv_bfloat16*>(vc),
+          slot0, kv->nkv, kv->hd, (long long)kv->cap * kv->hd);
     MOLOT_CUDA(cudaGetLastError());
     return MOLOT_OK;
   }
@@ -940,8 +926,8 @@ int molot_attn_append_rope(molot_kv_cache* kv, int layer, const float* q, const 
   float *kc, *vc;
   molot_kv_layer_data(kv, layer, &kc, &vc);
   int rc = append_strided(q, k, v, q_out, q_norm, k_norm, v_norm, eps, freq, pos, kc, vc,
-                          kv->len[layer], nq, kv->nkv, kv->hd, kv->hd, (long long)kv->cap * kv->hd,
-                          (cudaStream_t)stream, kv->bf16());
+                          kv->len[layer], nq, kv->nkv, kv->hd, kv->rs(), (long long)kv->cap * kv->rs(),
+                          (cudaStream_t)stream, kv->dtype);
   if (rc) return rc;
   kv->len[layer]++;
   kv->record(molot_kv_cache::kAppend, layer);
@@ -957,9 +943,9 @@ int molot_attn_decode(molot_kv_cache* kv, int src_layer, const float* q, float* 
   float *kc, *vc;
   molot_kv_layer_data(kv, src_layer, &kc, &vc);
   const bool prefetch = kv->decode_may_prefetch(src_layer);
-  int rc = decode_uniform(kv->ws, q, o, kc, vc, nq, kv->nkv, n, kv->hd, kv->hd,
-                          (long long)kv->cap * kv->hd, scale, pos_cur, window,
-                          (cudaStream_t)stream, prefetch, nullptr, kv->bf16());
+  int rc = decode_uniform(kv->ws, q, o, kc, vc, nq, kv->nkv, n, kv->hd, kv->rs(),
+                          (long long)kv->cap * kv->rs(), scale, pos_cur, window,
+                          (cudaStream_t)stream, prefetch, nullptr, kv->dtype);
   if (rc == MOLOT_OK) kv->record(molot_kv_cache::kDecode, -1);
   return rc;
 }
@@ -989,8 +975,8 @@ int molot_attn_step(molot_kv_cache* kv, int layer, const float* q, const float* 
     // Nothing to attend to (attn.h:163 leaves zeros); still append the row.
     // The rotated q goes to o, which the memset then clears.
     int rc = append_strided(q, k, v, o, q_norm, k_norm, v_norm, eps, freq, pos, kc, vc,
-                            n - 1, nq, kv->nkv, kv->hd, kv->hd, (long long)kv->cap * kv->hd,
-                            (cudaStream_t)stream, kv->bf16());
+                            n - 1, nq, kv->nkv, kv->hd, kv->rs(), (long long)kv->cap * kv->rs(),
+                            (cudaStream_t)stream, kv->dtype);
     if (rc) return rc;
     MOLOT_CUDA(cudaMemsetAsync(o, 0, sizeof(float) * (size_t)nq * kv->hd, (cudaStream_t)stream));
     kv->len[layer] = n;
@@ -998,9 +984,9 @@ int molot_attn_step(molot_kv_cache* kv, int layer, const float* q, const float* 
     return MOLOT_OK;
   }
   const bool prefetch = kv->step_may_prefetch(layer);
-  int rc = decode_uniform(kv->ws, q, o, kc, vc, nq, kv->nkv, n, kv->hd, kv->hd,
-                          (long long)kv->cap * kv->hd, scale, pos, window, (cudaStream_t)stream,
-                          prefetch, &f, kv->bf16());
+  int rc = decode_uniform(kv->ws, q, o, kc, vc, nq, kv->nkv, n, kv->hd, kv->rs(),
+                          (long long)kv->cap * kv->rs(), scale, pos, window, (cudaStream_t)stream,
+                          prefetch, &f, kv->dtype);
   if (rc) return rc;
   kv->len[layer] = n;
   kv->record(molot_kv_cache::kDecode, layer);
@@ -1044,9 +1030,9 @@ int molot_attn_append_rope_tokens(molot_kv_cache* kv, int layer, const float* q,
   a.K = kc;
   a.V = vc;
   a.kv_bstride = 0;
-  a.stride_t = kv->hd;
-  a.stride_h = (long long)kv->cap * kv->hd;
-  int rc = append_launch(a, kv->hd, M, (cudaStream_t)stream, kv->bf16());
+  a.stride_t = kv->rs();
+  a.stride_h = (long long)kv->cap * kv->rs();
+  int rc = append_launch(a, kv->hd, M, (cudaStream_t)stream, kv->dtype);
   if (rc) return rc;
   kv->len[layer] = n + M;
   kv->record(molot_kv_cache::kAppend, layer);
@@ -1060,12 +1046,15 @@ int molot_attn_prefill(molot_kv_cache* kv, int src_layer, const float* q, float*
   if (!kv || src_layer < 0 || src_layer >= kv->n_layers)
     return fail(MOLOT_ERR_INVALID, "bad layer");
   if (nq <= 0 || nq % kv->nkv) return fail(MOLOT_ERR_INVALID, "nq must be a multiple of nkv");
+  if (kv->dtype == MOLOT_KV_Q8)
+    return fail(MOLOT_ERR_UNSUPPORTED, "prefill over a Q8 cache is not built");
   float *kc, *vc;
   molot_kv_layer_data(kv, src_layer, &kc, &vc);
   const int hd = kv->hd;
   int rc = prefill_strided(kv->ws, q, (long long)nq * hd, o, (long long)nq * hd, kc, vc, nq,
                            kv->nkv, M, kv->len[src_layer], hd, hd, (long long)kv->cap * hd,
-                           scale, pos0, window, (cudaStream_t)stream, kv->bf16());
+                           scale, pos0, window, (cudaStream_t)stream,
+                           kv->dtype == MOLOT_KV_BF16);
   if (rc) return rc;
   kv->record(molot_kv_cache::kDecode, -1);  // releases its successor after its own wait
   return MOLOT_OK;

@@ -34,6 +34,7 @@
 #include <math_constants.h>
 
 #include <cstdint>
+#include <type_traits>
 
 #include "append.cuh"
 #include "ptx.cuh"
@@ -70,6 +71,7 @@ struct KvElem<float> {
   __device__ __forceinline__ static int dim(int i, int l8) {
     return 16 * (i >> 1) + l8 + 8 * (i & 1);
   }
+  template <int D>
   __device__ __forceinline__ static void load2(const float* row, int m, int l8, float& x0,
                                                float& x1) {
     x0 = row[16 * m + l8];
@@ -91,6 +93,7 @@ struct KvElem<__nv_bfloat16> {
   __device__ __forceinline__ static int dim(int i, int l8) {
     return 16 * (i >> 1) + 2 * l8 + (i & 1);
   }
+  template <int D>
   __device__ __forceinline__ static void load2(const __nv_bfloat16* row, int m, int l8,
                                                float& x0, float& x1) {
     const uint32_t w = *reinterpret_cast<const uint32_t*>(row + 16 * m + 2 * l8);
@@ -110,6 +113,79 @@ struct KvElem<__nv_bfloat16> {
     return __fadd_rn(a0, a1);
   }
 };
+// Q8 (Q8Row rows, see append.cuh): lane l8 owns dims {32m + 4*l8 + e},
+// e = 0..3, of each 32-value block m -- one 32-bit word of codes per block
+// -- so a row costs a lane D/32 word loads plus the block scales.  Index i
+// of a lane's values is block i/4, e = i%4.
+template <>
+struct KvElem<Q8Row> {
+  static constexpr int kBytes = 1;  // strides count bytes
+  __device__ __forceinline__ static int dim(int i, int l8) {
+    return 32 * (i >> 2) + 4 * l8 + (i & 3);
+  }
+  // Values 2m and 2m+1 of this lane: codes e, e+1 (e = 2*(m&1)) of block
+  // m/2, each read back as (float)q * s exactly as the quantizer defines.
+  // Bytes become floats through the 2^23 mantissa trick: with the sign bit
+  // flipped, code q sits as q + 128 in the low mantissa bits of 2^23.
+  template <int D>
+  __device__ __forceinline__ static void load2(const Q8Row* row, int m, int l8, float& x0,
+                                               float& x1) {
+    const unsigned char* r = reinterpret_cast<const unsigned char*>(row);
+    const int blk = m >> 1;
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(r + 32 * blk + 4 * l8) ^ 0x80808080u;
+    const float s = *reinterpret_cast<const float*>(r + D + 4 * blk);
+    const uint32_t e = (uint32_t)(m & 1) * 2u;
+    const float c0 = __fsub_rn(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650u + e)),
+                               8388736.0f);  // 2^23 + 128
+    const float c1 = __fsub_rn(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7651u + e)),
+                               8388736.0f);
+    x0 = __fmul_rn(c0, s);
+    x1 = __fmul_rn(c1, s);
+  }
+};
+
+// Sum of squares of one q head held in a row group's lane layout, equal bit
+// for bit to the reference's (norm.h:10-18: 16 FMA accumulators, accumulator
+// j taking dims j, j+16, j+32, ... in order, then the _mm512_reduce_add_ps
+// tree pairing j with j+8, then j+4, j+2, j+1).  Every lane of the group
+// returns it.
+template <int D, class KT>
+__device__ __forceinline__ float q_sumsq(const float (&x)[D / 8], int l8) {
+  constexpr int DV = D / 16;
+  if constexpr (std::is_same<KT, Q8Row>::value) {
+    // Accumulator 4*(l8&3)+e takes its even terms (dims 32m + 4*(l8&3) + e)
+    // from lane l8&3 and its odd ones (16 further) from lane (l8&3)+4: the
+    // two lanes swap values and both run the same chain.
+    const bool hi = l8 >= 4;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int mb = 0; mb < D / 32; ++mb) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float own = x[4 * mb + e];
+        const float other = __shfl_xor_sync(0xffffffffu, own, 4);
+        const float ev = hi ? other : own, od = hi ? own : other;
+        acc[e] = __fmaf_rn(ev, ev, acc[e]);
+        acc[e] = __fmaf_rn(od, od, acc[e]);
+      }
+    }
+    // j + (j+8): lanes l8 and l8^2; j + (j+4): l8^1; then e + (e+2), e + (e+1).
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      acc[e] = __fadd_rn(acc[e], __shfl_xor_sync(0xffffffffu, acc[e], 2));
+      acc[e] = __fadd_rn(acc[e], __shfl_xor_sync(0xffffffffu, acc[e], 1));
+    }
+    return __fadd_rn(__fadd_rn(acc[0], acc[2]), __fadd_rn(acc[1], acc[3]));
+  } else {
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int mm = 0; mm < DV; ++mm) {
+      a0 = __fmaf_rn(x[2 * mm], x[2 * mm], a0);
+      a1 = __fmaf_rn(x[2 * mm + 1], x[2 * mm + 1], a1);
+    }
+    return KvElem<KT>::tree16(a0, a1);
+  }
+}
 
 // Status codes written into the device status word.
 constexpr int kDevErrConsumerTimeout = 1;
@@ -183,11 +259,16 @@ struct DecodeArgs {
 
 template <int D, class KT = float>
 struct TileShape {
-  static constexpr int EB = KvElem<KT>::kBytes;
-  static constexpr int QR = ((D > 128) ? 8 : 16) * (4 / EB);  // rows per quarter
+  static constexpr bool kQ8 = std::is_same<KT, Q8Row>::value;
+  static constexpr int EB = KvElem<KT>::kBytes;  // bytes per stride unit
+  static constexpr int RB = kQ8 ? q8_row_bytes(D) : D * EB;  // bytes per row
+  static constexpr int RS = RB / (int)sizeof(KT);            // row pitch in KT units
+  // rows per quarter (a quarter holds 4.5-8 KB)
+  static constexpr int QR =
+      kQ8 ? (D > 128 ? 16 : (D > 64 ? 32 : 64)) : ((D > 128) ? 8 : 16) * (4 / EB);
   static constexpr int T = 4 * QR;                            // rows per tile
   static constexpr int TB = T / kBlk;                         // blocks per tile
-  static constexpr int QB = QR * D * EB;                      // quarter bytes
+  static constexpr int QB = QR * RB;                          // quarter bytes
   static constexpr int QSTRIDE = QB + kQuarterPadBytes;  // quarter pitch (bytes)
   static constexpr int KQ = 4 * QSTRIDE;                 // K (or V) part of a stage
   static constexpr int STAGE = 2 * KQ;
@@ -310,6 +391,7 @@ __device__ __forceinline__ void process_rows(const KT* kr, const KT* vr, int tok
                                              float (&l)[GS], int new_tok, const KT* nk,
                                              const KT* nv, int l8) {
   constexpr int DV = D / 16;
+  constexpr int RS = TileShape<D, KT>::RS;
   using E = KvElem<KT>;
   float sc[RC][GS];
   bool ok[RC];
@@ -318,7 +400,7 @@ __device__ __forceinline__ void process_rows(const KT* kr, const KT* vr, int tok
     ok[r] = FULL || (tok + r >= pt0 && tok + r < pt1);
     // The fused step's new row (slot new_tok) is not in the stage; its k and
     // v sit in shared memory (nk, nv).  Full tiles never contain it.
-    const KT* k = (!FULL && tok + r == new_tok) ? nk : kr + r * D;
+    const KT* k = (!FULL && tok + r == new_tok) ? nk : kr + r * RS;
     float a0[GS], a1[GS];
 #pragma unroll
     for (int h = 0; h < GS; ++h) {
@@ -328,7 +410,7 @@ __device__ __forceinline__ void process_rows(const KT* kr, const KT* vr, int tok
 #pragma unroll
     for (int mm = 0; mm < DV; ++mm) {
       float k0, k1;
-      E::load2(k, mm, l8, k0, k1);
+      E::template load2<D>(k, mm, l8, k0, k1);
 #pragma unroll
       for (int h = 0; h < GS; ++h) {
         a0[h] = __fmaf_rn(q[h][2 * mm], k0, a0[h]);
@@ -380,11 +462,11 @@ __device__ __forceinline__ void process_rows(const KT* kr, const KT* vr, int tok
   }
 #pragma unroll
   for (int r = 0; r < RC; ++r) {
-    const KT* v = (!FULL && tok + r == new_tok) ? nv : vr + r * D;
+    const KT* v = (!FULL && tok + r == new_tok) ? nv : vr + r * RS;
 #pragma unroll
     for (int mm = 0; mm < DV; ++mm) {
       float v0, v1;
-      E::load2(v, mm, l8, v0, v1);
+      E::template load2<D>(v, mm, l8, v0, v1);
       if (!FULL && !ok[r]) {
         v0 = 0.f;
         v1 = 0.f;
@@ -467,13 +549,7 @@ __device__ __forceinline__ void fused_rotate_q(const DecodeArgs& a, float (&q)[G
   if (a.q_norm) {
 #pragma unroll
     for (int h = 0; h < GS; ++h) {
-      float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-      for (int mm = 0; mm < DV; ++mm) {
-        a0 = __fmaf_rn(q[h][2 * mm], q[h][2 * mm], a0);
-        a1 = __fmaf_rn(q[h][2 * mm + 1], q[h][2 * mm + 1], a1);
-      }
-      const float t = E::tree16(a0, a1);
+      const float t = q_sumsq<D, KT>(q[h], l8);
       const float inv = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)D), a.eps)));
 #pragma unroll
       for (int i = 0; i < 2 * DV; ++i) {
@@ -534,12 +610,24 @@ __device__ __forceinline__ void fused_new_row(const DecodeArgs& a, const SegView
         y0 = z0;
         y1 = z1;
       }
-      // the cache's format (bf16 rounds here), the same value in both copies
-      const KT z0 = E::store(y0), z1 = E::store(y1);
-      new_k[i] = z0;
-      new_k[i + H] = z1;
-      K_w[row + i] = z0;
-      K_w[row + i + H] = z1;
+      // the cache's format (bf16 rounds, Q8 quantizes here), the same
+      // value in both copies
+      if constexpr (std::is_same<KT, Q8Row>::value) {  // H % 32 == 0: warp-uniform
+        unsigned char* sk = reinterpret_cast<unsigned char*>(new_k);
+        unsigned char* gk = reinterpret_cast<unsigned char*>(K_w + row);
+        float s0, s1;
+        const int c0 = q8_quantize(y0, s0), c1 = q8_quantize(y1, s1);
+        q8_put(sk, D, i >> 5, lane, c0, s0);
+        q8_put(sk, D, (i + H) >> 5, lane, c1, s1);
+        q8_put(gk, D, i >> 5, lane, c0, s0);
+        q8_put(gk, D, (i + H) >> 5, lane, c1, s1);
+      } else {
+        const KT z0 = E::store(y0), z1 = E::store(y1);
+        new_k[i] = z0;
+        new_k[i + H] = z1;
+        K_w[row + i] = z0;
+        K_w[row + i + H] = z1;
+      }
     }
   } else {
     float vinv = 1.f;
@@ -551,9 +639,17 @@ __device__ __forceinline__ void fused_new_row(const DecodeArgs& a, const SegView
     const float* vh = vx + (long long)sv.g * D;
 #pragma unroll
     for (int i = lane; i < D; i += 32) {
-      const KT val = E::store(a.v_norm ? __fmul_rn(vh[i], vinv) : vh[i]);
-      new_v[i] = val;
-      V_w[row + i] = val;
+      const float y = a.v_norm ? __fmul_rn(vh[i], vinv) : vh[i];
+      if constexpr (std::is_same<KT, Q8Row>::value) {
+        float sv;
+        const int c = q8_quantize(y, sv);
+        q8_put(reinterpret_cast<unsigned char*>(new_v), D, i >> 5, lane, c, sv);
+        q8_put(reinterpret_cast<unsigned char*>(V_w + row), D, i >> 5, lane, c, sv);
+      } else {
+        const KT val = E::store(y);
+        new_v[i] = val;
+        V_w[row + i] = val;
+      }
     }
   }
 }
@@ -680,6 +776,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   static_assert(kConsumerWarps % HS == 0, "head sets must divide the consumer warps");
   static_assert(QR % WPS == 0 && R >= 1, "rows per quarter must divide among warps");
   static_assert(D % 16 == 0, "head dim must be a multiple of 16");
+  static_assert(!TS::kQ8 || D % 64 == 0, "Q8 rows: both halves must be whole 32-value blocks");
   static_assert(R % RC == 0, "row chunks must tile the rows");
 
   extern __shared__ __align__(128) unsigned char smem[];
@@ -689,7 +786,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   // fused mode: the new k and v rows (cache format), then the tables (cos,
   // sin, q_norm, k_norm) at a fixed offset of 2*D floats
   KT* new_k = reinterpret_cast<KT*>(smem + SM::kStageBytes + SM::kMergeO + SM::kMergeML);
-  KT* new_v = new_k + D;
+  KT* new_v = new_k + TS::RS;
   float* tab = reinterpret_cast<float*>(smem + SM::kStageBytes + SM::kMergeO + SM::kMergeML +
                                         2 * D * 4);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + SM::kStageBytes + SM::kMergeO +
@@ -721,7 +818,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     ptx::setmaxnreg_dec<kProducerRegs>();
     if (warp != kConsumerWarps) return;
     const uint64_t pol = ptx::policy_evict_first();
-    const bool rows_contig = (a.block_table != nullptr) || (a.stride_t == D);
+    const bool rows_contig = (a.block_table != nullptr) || (a.stride_t * EB == TS::RB);
     bool waited = false;  // griddepcontrol.wait done by this warp
     int it = 0;
     long long pos = cbeg;
@@ -760,7 +857,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
             const int hi = min(tok0 + (q + 1) * QR, pt1c);
             qa[q] = lo;
             qn[q] = hi > lo ? hi - lo : 0;
-            bytes += (uint32_t)qn[q] * D * EB * 2u;
+            bytes += (uint32_t)qn[q] * TS::RB * 2u;
           }
           if (*abort_flag) {
             // Consumers skip waits once aborted; complete the phase without data.
@@ -776,19 +873,19 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
               const int kv = lane >> 2;
               if (qn[q] > 0) {
                 const unsigned char* base = static_cast<const unsigned char*>(kv ? a.V : a.K);
-                long long off;  // elements
+                long long off;  // stride units
                 if (a.block_table) {
                   const int p =
                       __ldg(a.block_table + (long long)sv.b * a.bt_stride + qa[q] / a.page_size);
                   off = (long long)p * a.page_stride + (long long)sv.g * a.page_hstride +
-                        (long long)(qa[q] % a.page_size) * D;
+                        (long long)(qa[q] % a.page_size) * TS::RS;
                 } else {
                   off = (long long)sv.b * a.kv_bstride + (long long)qa[q] * a.stride_t +
                         (long long)sv.g * a.stride_h;
                 }
                 unsigned char* dst = st_base + kv * TS::KQ + q * TS::QSTRIDE +
-                                     (qa[q] - (tok0 + q * QR)) * D * EB;
-                ptx::bulk_g2s(dst, base + off * EB, (uint32_t)qn[q] * D * EB, full_bar + stage,
+                                     (qa[q] - (tok0 + q * QR)) * TS::RB;
+                ptx::bulk_g2s(dst, base + off * EB, (uint32_t)qn[q] * TS::RB, full_bar + stage,
                               pol);
               }
             }
@@ -803,8 +900,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
                 const unsigned char* base = static_cast<const unsigned char*>(kv ? a.V : a.K);
                 const long long off = (long long)sv.b * a.kv_bstride + (long long)t * a.stride_t +
                                       (long long)sv.g * a.stride_h;
-                unsigned char* dst = st_base + kv * TS::KQ + q * TS::QSTRIDE + r * D * EB;
-                ptx::bulk_g2s(dst, base + off * EB, (uint32_t)D * EB, full_bar + stage, pol);
+                unsigned char* dst = st_base + kv * TS::KQ + q * TS::QSTRIDE + r * TS::RB;
+                ptx::bulk_g2s(dst, base + off * EB, (uint32_t)TS::RB, full_bar + stage, pol);
               }
             }
           }
@@ -925,16 +1022,18 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
           // [pt0, pt1); the rest take the predicate-free path.
           const bool full = blk * kBlk >= pt0 && blk * kBlk + TS::T <= pt1 &&
                             !(new_tok >= blk * kBlk && new_tok < blk * kBlk + TS::T);
+          // One copy of each chunk body: the chunk loops stay rolled so the
+          // instruction working set fits the SM's instruction cache.
           if (full) {
-#pragma unroll
+#pragma unroll 1
             for (int r0 = 0; r0 < R; r0 += RC)
-              process_rows<D, GS, RC, true>(kq + (wi * R + r0) * D, vq + (wi * R + r0) * D,
+              process_rows<D, GS, RC, true>(kq + (wi * R + r0) * TS::RS, vq + (wi * R + r0) * TS::RS,
                                             tok_base + r0, pt0, pt1, a.scale, q, o, m, l,
                                             new_tok, new_k, new_v, l8);
           } else {
-#pragma unroll
+#pragma unroll 1
             for (int r0 = 0; r0 < R; r0 += RC)
-              process_rows<D, GS, RC, false>(kq + (wi * R + r0) * D, vq + (wi * R + r0) * D,
+              process_rows<D, GS, RC, false>(kq + (wi * R + r0) * TS::RS, vq + (wi * R + r0) * TS::RS,
                                              tok_base + r0, pt0, pt1, a.scale, q, o, m, l,
                                              new_tok, new_k, new_v, l8);
           }

@@ -94,6 +94,7 @@ def port():
                  [_p, _p, _p, _p, _i, _i, _i, _i, _i, _f, _i, _i])
         _declare(lib, "oracle_quantize_q4", [_p, _i, _i, _p, _p, _p, _p])
         _declare(lib, "oracle_quantize_act_q8", [_p, _i, _p, _p])
+        _declare(lib, "oracle_quantize_q8_blocks", [_p, ctypes.c_long, _p, _p])
         _declare(lib, "oracle_gemv_q4", [_p, _p, _p, _i, _i, _p, _p])
         _port = lib
     return _port
@@ -128,6 +129,7 @@ def ref():
                      [_p, _p, _p, _p, _p, _i, _f, _p, _i, _p, _p, _p, _i, _p, _i, _i, _i, _f, _i, _i], _i)
             for name, args in (("ref_quantize_q4", [_p, _i, _i, _p, _p, _p, _p]),
                                ("ref_quantize_act_q8", [_p, _i, _p, _p]),
+                               ("ref_quantize_q8_blocks", [_p, ctypes.c_long, _p, _p]),
                                ("ref_gemv_q4", [_p, _p, _p, _p, _i, _i, _p, _p, _i])):
                 if hasattr(lib, name):
                     _declare(lib, name, args)
@@ -270,6 +272,24 @@ def quantize_act_q8(x, impl="port"):
     fn = port().oracle_quantize_act_q8 if impl == "port" else ref().ref_quantize_act_q8
     fn(_ptr(x), x.size, _ptr(q), _ptr(sc))
     return q, sc
+
+
+def quantize_q8_blocks(x, impl="port"):
+    """quant.h:33-43 per 32-value block (the Q8 KV row rule): x [..., m*32]
+    -> (codes int8 [..., m*32], scales float32 [..., m])."""
+    x = _f32(x)
+    q = np.zeros(x.shape, np.int8)
+    sc = np.zeros(x.shape[:-1] + (x.shape[-1] // 32,), np.float32)
+    fn = port().oracle_quantize_q8_blocks if impl == "port" else ref().ref_quantize_q8_blocks
+    fn(_ptr(x), x.size, _ptr(q), _ptr(sc))
+    return q, sc
+
+
+def dequantize_q8_blocks(q, sc):
+    """Codes and per-32 scales back to float32: (float)q * s, one rounding."""
+    q = np.asarray(q, np.int8)
+    s = np.repeat(np.asarray(sc, np.float32), 32, axis=-1)
+    return (q.astype(np.float32) * s).astype(np.float32)
 
 
 def gemv_q4(q4, x, impl="port", nthreads=0):

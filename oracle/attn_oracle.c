@@ -340,6 +340,30 @@ void oracle_quantize_act_q8(const float* x, int n, int8_t* q, float* scales) {
   }
 }
 
+/* The Q8 KV row format: quant.h:33-43 quantize_q8_row applied to each
+ * 32-value block of x on its own (n a multiple of 32): s = amax/127 (1 when
+ * not positive), q = nearbyint(x/s) clamped to [-127, 127].  The reference's
+ * -ffast-math build evaluates s as amax * (1/127) and x/s as x * (127/amax);
+ * those are the operations spelled out here (checked bit for bit against the
+ * compiled reference). */
+void oracle_quantize_q8_blocks(const float* x, long n, int8_t* q, float* scales) {
+  for (long b = 0; b < n / 32; ++b) {
+    const float* blk = x + 32 * b;
+    float amax = 0;
+    for (int i = 0; i < 32; ++i) {
+      float v = fabsf(blk[i]);
+      if (v > amax) amax = v;
+    }
+    const float s = amax * (1.0f / 127.0f);
+    const float inv = 127.0f / amax;
+    scales[b] = s > 0 ? s : 1.0f;
+    for (int i = 0; i < 32; ++i) {
+      int v = s > 0 ? (int)nearbyintf(blk[i] * inv) : 0;
+      q[32 * b + i] = (int8_t)(v > 127 ? 127 : (v < -127 ? -127 : v));
+    }
+  }
+}
+
 /* gemm.h:174-254 gemv_q4: activations quantized once; per row and group
  * the exact integer sum G = sum((nibble - zero) * q); y = sum over groups,
  * in group order, of (float)G * scale_w * scale_x. */

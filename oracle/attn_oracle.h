@@ -87,6 +87,8 @@ void oracle_attn_prefill_gqa(const float* Qm, const float* K, const float* V, fl
 void oracle_quantize_q4(const float* W, int rows, int cols, float* scales, int8_t* zeros,
                         uint8_t* data, int16_t* wsums);
 void oracle_quantize_act_q8(const float* x, int n, int8_t* q, float* scales);
+/* The Q8 KV row format's block rule (quant.h:33-43 per 32 values). */
+void oracle_quantize_q8_blocks(const float* x, long n, int8_t* q, float* scales);
 void oracle_gemv_q4(const float* scales, const int8_t* zeros, const uint8_t* data, int rows,
                     int cols, const float* x, float* y);
 

@@ -20,6 +20,7 @@
 
 #include "molot/attn.h"
 #include "molot/norm.h"
+#include "molot/quant.h"
 #include "molot/thread_pool.h"
 
 namespace {
@@ -167,6 +168,15 @@ void ref_quantize_act_q8(const float* x, int n, int8_t* q, float* scales) {
   molot::QAct8 a = molot::quantize_act_q8(x, n);
   std::memcpy(q, a.q.data(), a.q.size());
   std::memcpy(scales, a.scales.data(), a.scales.size() * sizeof(float));
+}
+
+// quant.h:33-50 quantize_q8_row applied to each 32-value block of x on its
+// own (n a multiple of 32): the block rule of the Q8 KV row format.
+void ref_quantize_q8_blocks(const float* x, long n, int8_t* q, float* scales) {
+  for (long b = 0; b < n / 32; ++b) {
+    int32_t bsum = 0;
+    molot::quantize_q8_row(x + 32 * b, 32, 1, scales + b, q + 32 * b, &bsum);
+  }
 }
 
 // gemm.h:223-254 gemv_q4 on a Q4Matrix given as its arrays.

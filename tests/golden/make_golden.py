@@ -163,6 +163,22 @@ def gemv_q4_cases():
     return out
 
 
+def kv_q8_case():
+    """quant.h:33-50 quantize_q8_row run by the reference on each 32-value
+    block: the block rule of the Q8 KV rows.  Rows of head_dim 128 with
+    mixed magnitudes and outliers, an all-zero block, and a block whose
+    absmax is 127 (so x/s is x itself) holding exact half-integers, which
+    pins the ties-to-even rounding."""
+    rng = np.random.default_rng(88)
+    x = (rng.standard_normal((96, 128)) * rng.uniform(1e-3, 30, (96, 1))).astype(np.float32)
+    x[::9, 7] *= 40.0
+    x[5, 32:64] = 0.0
+    tie = np.array([127.0] + [k + 0.5 for k in range(-15, 15)] + [-126.5], np.float32)
+    x[6, :32] = tie
+    q, sc = oracle.quantize_q8_blocks(x, impl="ref")
+    return dict(x=x, q=q, scales=sc)
+
+
 def flatten(cases):
     flat = {}
     for name, case in cases.items():
@@ -179,6 +195,7 @@ FIXTURES = {
     "layer_step.npz": layer_step_case,
     "prefill.npz": lambda: flatten(prefill_cases()),
     "gemv_q4.npz": lambda: flatten(gemv_q4_cases()),
+    "kv_q8.npz": kv_q8_case,
 }
 
 

@@ -188,3 +188,30 @@ def test_q4_oracle_matches_reference_golden():
         y = oracle.gemv_q4(q4, z[f"{name}/x"])
         # same integers; float sums differ only by the reference's FMA contraction
         assert oracle.rel_err(y, z[f"{name}/y"]) < 1e-6, name
+
+
+def test_q8_block_quantizer_matches_reference_golden():
+    """The Q8 KV block rule (quant.h:33-43 per 32 values) restated in
+    oracle/attn_oracle.c against the reference's own quantize_q8_row
+    (tests/golden/kv_q8.npz): codes and scales bit for bit, including an
+    all-zero block and exact half-integer ties."""
+    import oracle
+    z = np.load(os.path.join(GOLDEN, "kv_q8.npz"))
+    q, sc = oracle.quantize_q8_blocks(z["x"])
+    assert np.array_equal(q, z["q"])
+    assert np.array_equal(sc.view(np.uint32), z["scales"].view(np.uint32))
+    back = oracle.dequantize_q8_blocks(q, sc)
+    assert np.all(np.abs(back - z["x"]) <= 0.5 * np.repeat(sc, 32, axis=-1) * (1 + 1e-6))
+
+
+@pytest.mark.parametrize("magnitude", [1e-4, 1.0, 300.0])
+def test_q8_block_quantizer_equals_reference_random(orc, magnitude):
+    """Beyond the fixture: 2M random values against the live reference."""
+    if orc.ref() is None:
+        pytest.skip("reference shim not built or no AVX-512 on this host")
+    rng = np.random.default_rng(int(magnitude * 1e4) % 997)
+    x = (rng.standard_normal((4096, 512)) * magnitude).astype(np.float32)
+    x[::13, 9] *= 60.0
+    a = orc.quantize_q8_blocks(x)
+    b = orc.quantize_q8_blocks(x, impl="ref")
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1].view(np.uint32), b[1].view(np.uint32))
