@@ -316,6 +316,12 @@ int decode_uniform(Workspace& ws, const float* Q, float* O, const void* K, const
   DecodeArgs a = {};
   a.grid = grid;
   a.aligned = grid >= nkv ? 1 : 0;  // one segment per CTA (see DecodeArgs)
+  // The last CTA of a segment holds slot n-1: in a fused step it also
+  // builds that row, in a decode right after the append that wrote it, it
+  // can only stream that row once the append has completed.  Half a share
+  // of slots for it measured best (cfg2 fused step, FP32 and BF16 caches);
+  // the two forms keep one partition, so their results stay bit-identical.
+  a.tail_w = (fused || prefetch_old_rows) ? kShareW / 2 : 0;
   a.prefetch_old_rows = prefetch_old_rows ? 1 : 0;
   if (fused) {  // per-token prologue fused into this launch (slot n-1 is new)
     a.fused = 1;

@@ -228,6 +228,10 @@ struct DecodeArgs {
   // (which stalls its stream and made segment-straddling CTAs the slowest).
   // Otherwise the blocks of all segments are split evenly (stream-K).
   int aligned;
+  // Aligned partition: the last CTA of each segment takes a share of
+  // (kShareW - tail_w) / kShareW of the others' (it also builds the fused
+  // step's new row, which holds slot n-1).  0: equal shares.
+  int tail_w;
   // Programmatic dependent launch.  When set, the producer may stream each
   // segment's slots below its newest one (n-1) before the preceding launch
   // has completed: they were written two or more launches earlier (the
@@ -310,14 +314,19 @@ __device__ __forceinline__ int aligned_seg_of_cta(const DecodeArgs& a, int c) {
   return c < r * (q + 1) ? c / (q + 1) : r + (c - r * (q + 1)) / q;
 }
 
-// First block (global index) of CTA c's range; c == grid gives NB.
+constexpr int kShareW = 16;  // weight of a full CTA share in the aligned partition
+
+// First block (global index) of CTA c's range; c == grid gives NB.  In the
+// aligned partition local CTA j of a segment (cs CTAs) starts at
+// floor(nblk_u * j * kShareW / T), T = cs * kShareW - tail_w.
 __device__ __forceinline__ long long range_begin(const DecodeArgs& a, int c) {
   if (!a.aligned) return (long long)c * a.NB / a.grid;
   if (c >= a.grid) return a.NB;
   const int s = aligned_seg_of_cta(a, c);
   const int c0 = aligned_first_cta(a, s);
   const int cs = aligned_first_cta(a, s + 1) - c0;
-  return (long long)s * a.nblk_u + (long long)a.nblk_u * (c - c0) / cs;
+  const long long T = (long long)cs * kShareW - a.tail_w;
+  return (long long)s * a.nblk_u + (long long)a.nblk_u * (c - c0) * kShareW / T;
 }
 
 // CTA whose range holds block x: the largest c with range_begin(c) <= x.
@@ -327,7 +336,11 @@ __device__ __forceinline__ long long cta_of_block(const DecodeArgs& a, long long
   const long long local = x - (long long)s * a.nblk_u;
   const int c0 = aligned_first_cta(a, s);
   const int cs = aligned_first_cta(a, s + 1) - c0;
-  return c0 + ((local + 1) * cs + a.nblk_u - 1) / a.nblk_u - 1;
+  // largest j < cs with floor(A*j/T) <= local, A = nblk_u * kShareW
+  const long long T = (long long)cs * kShareW - a.tail_w;
+  const long long A = (long long)a.nblk_u * kShareW;
+  const long long j = ((local + 1) * T + A - 1) / A - 1;
+  return c0 + (j < cs - 1 ? j : cs - 1);
 }
 
 struct SegView {
@@ -809,9 +822,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   }
   __syncthreads();
 
-  const long long cbeg = range_begin(a, blockIdx.x);
-  const long long cend = range_begin(a, blockIdx.x + 1);
-  const int s_first = first_seg_of_cta(a, blockIdx.x);
+  // Partition index: blocks in reverse.  The block scheduler hands out
+  // blocks in index order, so the highest blocks of a launch start last,
+  // on the SMs that the preceding launch's last CTAs free; they take the
+  // lightest ranges (the first CTAs of a segment, never the new row's).
+  const int cta = a.grid - 1 - (int)blockIdx.x;
+  const long long cbeg = range_begin(a, cta);
+  const long long cend = range_begin(a, cta + 1);
+  const int s_first = first_seg_of_cta(a, cta);
 
   if (warp >= kConsumerWarps) {
     // ------------------------------------------------------------ producer
@@ -1098,7 +1116,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
 
       const int G = a.G;
       const int psz = partial_record_floats(G, D);
-      const int slot = 2 * blockIdx.x + (pos == cbeg ? 0 : 1);
+      const int slot = 2 * cta + (pos == cbeg ? 0 : 1);
       float* part = a.partials + (size_t)slot * psz;
       float* out_seg = a.O + (long long)sv.b * a.o_bstride + (long long)sv.g * G * D;
       for (int idx = ctid; idx < G * D; idx += kConsumerWarps * 32) {

@@ -45,6 +45,9 @@ def test_step_against_reference_golden(mb, torch_cuda, orc):
     (16, 2, 64, 64, False, 0),        # new slot opens a tile
     (8, 1, 128, 15, True, 0),         # new slot closes a 16-slot block
     (4, 4, 128, 0, True, 0),          # first token: the new row is all there is
+    (32, 8, 128, 300, True, 0),       # ~1 block per CTA: the shortened last share
+    (64, 8, 128, 2500, False, 0),     # G = 8
+    (8, 8, 128, 40000, True, 0),      # G = 1, long
 ])
 def test_step_matches_oracle_and_two_launch_path(mb, torch_cuda, orc, nq, nkv, hd, n0, norms,
                                                   window):
