@@ -811,7 +811,7 @@ def run_prefill(args, cfg):
 
     L, nq, nkv, d, M = cfg["layers"], cfg["nq"], cfg["nkv"], cfg["d"], cfg["prompt"]
     window, scale = cfg["window"], 1.0 / math.sqrt(d)
-    cache = mb.KVCache(L, nkv, d, M)
+    cache = mb.KVCache(L, nkv, d, M, dtype=args.kv)
     gen = torch.Generator(device=rt.dev)
     gen.manual_seed(1234 + rt.rank)
     q_raw = torch.randn((L, M, nq, d), device=rt.dev, generator=gen)
@@ -882,7 +882,8 @@ def run_prefill(args, cfg):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,1) q/k/v generated on device)",
-            "config": {"workload": f"prefill: {cfg['desc']}", "layers": L, "nq": nq, "nkv": nkv,
+            "config": {"workload": f"prefill: {cfg['desc']}", "kv_dtype": args.kv,
+                       "layers": L, "nq": nq, "nkv": nkv,
                        "head_dim": d, "prompt": M, "window": window,
                        "parallelism": f"replicas x{rt.world}",
                        "l2": "K/V of a layer (33.5 MB) stays in L2 across query blocks"},

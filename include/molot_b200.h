@@ -184,9 +184,9 @@ enum molot_kv_dtype {
                      16 bytes; each 32-value block quantized by the rule of
                      quant.h:33-43 (s = absmax/127, q = nearbyint(x/s)).
                      Results match the reference run on the dequantized
-                     cache (q*s) within the parity tolerance.  Decode, step,
-                     append and write only: prefill returns
-                     MOLOT_ERR_UNSUPPORTED. */
+                     cache (q*s) within the parity tolerance.  All handle
+                     calls accept it (write, append, step, decode,
+                     prefill). */
 };
 
 int molot_kv_create(int n_layers, int nkv, int hd, int cap, molot_kv_cache** out);

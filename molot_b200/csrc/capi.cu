@@ -451,14 +451,23 @@ KernelRef prefill_ref() {
   return {reinterpret_cast<const void*>(&gqa_prefill_kernel<D, KT>), PrefillTile<D, KT>::kTotal};
 }
 
-bool pick_prefill(int D, KernelRef* k, bool bf16 = false) {
-  using B = __nv_bfloat16;
+template <class KT>
+bool pick_prefill_t(int D, KernelRef* k) {
   switch (D) {
-    case 64: *k = bf16 ? prefill_ref<64, B>() : prefill_ref<64, float>(); return true;
-    case 128: *k = bf16 ? prefill_ref<128, B>() : prefill_ref<128, float>(); return true;
-    case 256: *k = bf16 ? prefill_ref<256, B>() : prefill_ref<256, float>(); return true;
+    case 64: *k = prefill_ref<64, KT>(); return true;
+    case 128: *k = prefill_ref<128, KT>(); return true;
+    case 256: *k = prefill_ref<256, KT>(); return true;
   }
   return false;
+}
+
+// kvt: the cache's molot_kv_dtype.
+bool pick_prefill(int D, KernelRef* k, int kvt = MOLOT_KV_F32) {
+  switch (kvt) {
+    case MOLOT_KV_BF16: return pick_prefill_t<__nv_bfloat16>(D, k);
+    case MOLOT_KV_Q8: return pick_prefill_t<Q8Row>(D, k);
+  }
+  return pick_prefill_t<float>(D, k);
 }
 
 // gemm.h:409-446 on device buffers: Q/O [M][nq][d] (token stride q_tstride /
@@ -466,7 +475,7 @@ bool pick_prefill(int D, KernelRef* k, bool bf16 = false) {
 int prefill_strided(Workspace& ws, const float* Q, long long q_tstride, float* O,
                     long long o_tstride, const void* K, const void* V, int nq, int nkv, int M,
                     int N, int d, long long stride_t, long long stride_h, float scale, int pos0,
-                    int window, cudaStream_t st, bool bf16 = false) {
+                    int window, cudaStream_t st, int kvt = MOLOT_KV_F32) {
   if (!Q || !O || !K || !V) return fail(MOLOT_ERR_INVALID, "null pointer");
   if (nq <= 0 || nkv <= 0 || nq % nkv || M < 0 || N < 0 || pos0 < 0)
     return fail(MOLOT_ERR_INVALID, "bad sizes (nq must be a multiple of nkv)");
@@ -474,7 +483,7 @@ int prefill_strided(Workspace& ws, const float* Q, long long q_tstride, float* O
   if (G > kPrefillRows || kPrefillRows % G)
     return fail(MOLOT_ERR_UNSUPPORTED, "prefill group size must divide 64");
   KernelRef k;
-  if (!pick_prefill(d, &k, bf16)) return fail(MOLOT_ERR_UNSUPPORTED, "prefill head_dim not built");
+  if (!pick_prefill(d, &k, kvt)) return fail(MOLOT_ERR_UNSUPPORTED, "prefill head_dim not built");
   if (!aligned16(Q) || !aligned16(O) || !aligned16(K) || !aligned16(V) || (q_tstride & 3) ||
       (o_tstride & 3) || (stride_t & 3) || (stride_h & 3))
     return fail(MOLOT_ERR_INVALID, "buffers must be 16-byte aligned with strides multiple of 4");
@@ -1052,15 +1061,13 @@ int molot_attn_prefill(molot_kv_cache* kv, int src_layer, const float* q, float*
   if (!kv || src_layer < 0 || src_layer >= kv->n_layers)
     return fail(MOLOT_ERR_INVALID, "bad layer");
   if (nq <= 0 || nq % kv->nkv) return fail(MOLOT_ERR_INVALID, "nq must be a multiple of nkv");
-  if (kv->dtype == MOLOT_KV_Q8)
-    return fail(MOLOT_ERR_UNSUPPORTED, "prefill over a Q8 cache is not built");
   float *kc, *vc;
   molot_kv_layer_data(kv, src_layer, &kc, &vc);
   const int hd = kv->hd;
   int rc = prefill_strided(kv->ws, q, (long long)nq * hd, o, (long long)nq * hd, kc, vc, nq,
-                           kv->nkv, M, kv->len[src_layer], hd, hd, (long long)kv->cap * hd,
-                           scale, pos0, window, (cudaStream_t)stream,
-                           kv->dtype == MOLOT_KV_BF16);
+                           kv->nkv, M, kv->len[src_layer], hd, kv->rs(),
+                           (long long)kv->cap * kv->rs(), scale, pos0, window,
+                           (cudaStream_t)stream, kv->dtype);
   if (rc) return rc;
   kv->record(molot_kv_cache::kDecode, -1);  // releases its successor after its own wait
   return MOLOT_OK;

@@ -25,7 +25,9 @@
 #include <math_constants.h>
 
 #include <cstdint>
+#include <type_traits>
 
+#include "append.cuh"
 #include "ptx.cuh"
 
 namespace molot {
@@ -44,19 +46,28 @@ __device__ __forceinline__ float4 load4(const __nv_bfloat16* p) {
                      __uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u));
 }
 
+// Q8 caches (Q8Row, append.cuh): the raw rows of a tile (codes and block
+// scales) arrive through the same ring and are expanded once per tile into
+// FP32 tiles by the 256 consumer threads, each value (float)code * scale
+// exactly as the quantizer defines it; the score and output loops then run
+// on those tiles unchanged.
 template <int D, class KT = float>
 struct PrefillTile {
-  static constexpr int EB = sizeof(KT);
+  static constexpr bool kQ8 = std::is_same<KT, Q8Row>::value;
+  static constexpr int EB = sizeof(KT);  // bytes per stride unit
+  static constexpr int RB = kQ8 ? q8_row_bytes(D) : D * EB;  // bytes of a cache row
   static constexpr int BN = D > 128 ? 32 : 64;  // keys per tile
   static constexpr int NJ = BN / 16;            // score columns per thread
   static constexpr int LD = D + 4;              // padded Q row pitch (floats)
-  static constexpr int LDK = D + 16 / EB;       // padded K/V row pitch (elements, +16 B)
+  static constexpr int LDK = (RB + 16) / EB;    // padded K/V row pitch (elements, +16 B)
+  static constexpr int LDF = D + 4;             // Q8: expanded FP32 tile pitch (floats)
   static constexpr int PLD = BN + 4;            // P row pitch (floats)
   static constexpr int kQ = kPrefillRows * LD * 4;
-  static constexpr int kKV = BN * LDK * EB;  // one K or V tile
+  static constexpr int kKV = BN * LDK * EB;  // one K or V tile as it arrives
+  static constexpr int kF = kQ8 ? BN * LDF * 4 : 0;  // Q8: one expanded K or V tile
   static constexpr int kP = kPrefillRows * PLD * 4;
   static constexpr int kBars = 5 * 8;  // full[2], empty[2], q
-  static constexpr int kTotal = kQ + 4 * kKV + kP + kBars + 16;
+  static constexpr int kTotal = kQ + 4 * kKV + 2 * kF + kP + kBars + 16;
   static_assert(kTotal <= 227 * 1024, "prefill CTA exceeds the shared-memory limit");
   static_assert(D % 64 == 0, "head dim must be a multiple of 64");
 };
@@ -88,15 +99,19 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     gqa_prefill_kernel(const __grid_constant__ PrefillArgs a) {
   using TP = PrefillTile<D, KT>;
   constexpr int BN = TP::BN, NJ = TP::NJ, LD = TP::LD, LDK = TP::LDK, PLD = TP::PLD;
-  constexpr int EB = TP::EB;
+  // the type and pitch of the tiles the score / output loops read
+  using CT = typename std::conditional<TP::kQ8, float, KT>::type;
+  constexpr int LDC = TP::kQ8 ? TP::LDF : LDK;
   constexpr int DJ = D / 64;  // float4 groups of output columns per thread
   constexpr float kLog2e = 1.4426950408889634f;
 
   extern __shared__ __align__(128) unsigned char smem[];
   float* Qs = reinterpret_cast<float*>(smem);
   KT* KVs = reinterpret_cast<KT*>(smem + TP::kQ);  // [stage][K,V][BN][LDK]
-  float* Ps = reinterpret_cast<float*>(smem + TP::kQ + 4 * TP::kKV);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TP::kQ + 4 * TP::kKV + TP::kP);
+  float* KVf = reinterpret_cast<float*>(smem + TP::kQ + 4 * TP::kKV);  // Q8: [K,V][BN][LDF]
+  float* Ps = reinterpret_cast<float*>(smem + TP::kQ + 4 * TP::kKV + 2 * TP::kF);
+  uint64_t* full =
+      reinterpret_cast<uint64_t*>(smem + TP::kQ + 4 * TP::kKV + 2 * TP::kF + TP::kP);
   uint64_t* empty = full + 2;
   uint64_t* q_bar = full + 4;
   volatile int* abort_sm = reinterpret_cast<volatile int*>(full + 5);
@@ -159,13 +174,13 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       const int rows = min(BN, t_hi - ts);
       KT* Kd = KVs + (size_t)(stage * 2) * BN * LDK;
       KT* Vd = Kd + (size_t)BN * LDK;
-      if (lane == 0) ptx::mbar_arrive_expect_tx(full + stage, (uint32_t)rows * D * EB * 2u);
+      if (lane == 0) ptx::mbar_arrive_expect_tx(full + stage, (uint32_t)rows * TP::RB * 2u);
       __syncwarp();
       for (int c = lane; c < rows; c += 32) {
         const long long off = (long long)(ts + c) * a.stride_t + (long long)g * a.stride_h;
-        ptx::bulk_g2s(Kd + (size_t)c * LDK, static_cast<const KT*>(a.K) + off, D * EB,
+        ptx::bulk_g2s(Kd + (size_t)c * LDK, static_cast<const KT*>(a.K) + off, TP::RB,
                       full + stage, pol);
-        ptx::bulk_g2s(Vd + (size_t)c * LDK, static_cast<const KT*>(a.V) + off, D * EB,
+        ptx::bulk_g2s(Vd + (size_t)c * LDK, static_cast<const KT*>(a.V) + off, TP::RB,
                       full + stage, pol);
       }
     }
@@ -196,8 +211,38 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     // A timed-out wait leaves this thread computing on stale data; the
     // results are then discarded (status word) and every loop still ends.
     ok_waits &= ptx::mbar_wait_bounded(full + stage, (i >> 1) & 1, a.timeout_ns);
-    const KT* Kt = KVs + (size_t)(stage * 2) * BN * LDK;
-    const KT* Vt = Kt + (size_t)BN * LDK;
+    const CT* Kt;
+    const CT* Vt;
+    if constexpr (TP::kQ8) {
+      // Every consumer is done with the previous expanded tiles; expand
+      // this tile (one 32-bit word of codes per task), publish, and hand the
+      // raw stage back to the producer at once.
+      ptx::named_bar_sync(1, kPrefillConsumers);
+      const unsigned char* raw =
+          reinterpret_cast<const unsigned char*>(KVs + (size_t)(stage * 2) * BN * LDK);
+      constexpr int kWords = BN * D / 4;
+      for (int w = tid; w < 2 * kWords; w += kPrefillConsumers) {
+        const int kv = w / kWords, rem = w - kv * kWords;
+        const int row = rem / (D / 4), c4 = rem - row * (D / 4);
+        const unsigned char* rp = raw + (size_t)(kv * BN + row) * LDK;
+        const uint32_t code = *reinterpret_cast<const uint32_t*>(rp + 4 * c4) ^ 0x80808080u;
+        const float sc = *reinterpret_cast<const float*>(rp + D + 4 * (c4 >> 3));
+        float4 f;  // code + 128 in the low mantissa bits of 2^23, minus 2^23 + 128
+        f.x = __fmul_rn(__fsub_rn(__uint_as_float(__byte_perm(code, 0x4B000000u, 0x7650u)), 8388736.f), sc);
+        f.y = __fmul_rn(__fsub_rn(__uint_as_float(__byte_perm(code, 0x4B000000u, 0x7651u)), 8388736.f), sc);
+        f.z = __fmul_rn(__fsub_rn(__uint_as_float(__byte_perm(code, 0x4B000000u, 0x7652u)), 8388736.f), sc);
+        f.w = __fmul_rn(__fsub_rn(__uint_as_float(__byte_perm(code, 0x4B000000u, 0x7653u)), 8388736.f), sc);
+        *reinterpret_cast<float4*>(KVf + (size_t)(kv * BN + row) * LDC + 4 * c4) = f;
+      }
+      ptx::named_bar_sync(1, kPrefillConsumers);
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(empty + stage);
+      Kt = KVf;
+      Vt = KVf + (size_t)BN * LDC;
+    } else {
+      Kt = KVs + (size_t)(stage * 2) * BN * LDK;
+      Vt = Kt + (size_t)BN * LDK;
+    }
     const int ts = t_lo + i * BN;
     const int kc = min(BN, t_hi - ts);
 
@@ -208,7 +253,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
 #pragma unroll
       for (int j = 0; j < NJ; ++j) s[ii][j] = 0.f;
     const float* qb = Qs + (size_t)(ty * 4) * LD;
-    const KT* kb = Kt + (size_t)tx * LDK;
+    const CT* kb = Kt + (size_t)tx * LDC;
 #pragma unroll 4
     for (int k = 0; k < D; k += 4) {
       float4 qv[4], kv[NJ];
@@ -216,7 +261,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       for (int ii = 0; ii < 4; ++ii) qv[ii] = *reinterpret_cast<const float4*>(qb + ii * LD + k);
 #pragma unroll
       for (int j = 0; j < NJ; ++j)
-        kv[j] = load4(kb + (size_t)(16 * j) * LDK + k);
+        kv[j] = load4(kb + (size_t)(16 * j) * LDC + k);
 #pragma unroll
       for (int ii = 0; ii < 4; ++ii)
 #pragma unroll
@@ -268,7 +313,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       for (int ii = 0; ii < 4; ++ii) pv[ii] = *reinterpret_cast<const float4*>(pb + ii * PLD + c);
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
-        const KT* vr = Vt + (size_t)(c + cc) * LDK + tx * 4;
+        const CT* vr = Vt + (size_t)(c + cc) * LDC + tx * 4;
 #pragma unroll
         for (int jj = 0; jj < DJ; ++jj) {
           const float4 v4 = load4(vr + 64 * jj);
@@ -284,7 +329,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       }
     }
     for (; c < kc; ++c) {  // ragged end of the last tile
-      const KT* vr = Vt + (size_t)c * LDK + tx * 4;
+      const CT* vr = Vt + (size_t)c * LDC + tx * 4;
 #pragma unroll
       for (int jj = 0; jj < DJ; ++jj) {
         const float4 v4 = load4(vr + 64 * jj);
@@ -299,7 +344,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       }
     }
     __syncwarp();  // this warp's P rows may be rewritten by the next tile
-    if (lane == 0) ptx::mbar_arrive(empty + stage);
+    if (!TP::kQ8 && lane == 0) ptx::mbar_arrive(empty + stage);
   }
   if (!ok_waits || *abort_sm) {
     atomicCAS(a.status, 0, 3);

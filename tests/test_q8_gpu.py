@@ -166,12 +166,17 @@ def test_fused_step_on_q8_cache(mb, torch_cuda, orc, nq, nkv, hd, n0, window):
     assert orc.rel_err(outs[0][0].reshape(nq, hd), want) <= PARITY_TOL
 
 
-def test_append_tokens_then_decode_q8(mb, torch_cuda, orc):
-    """The multi-token prologue (prefill's append) writes Q8 rows the decode
-    reads; prefill attention itself is not built for Q8 caches."""
+@pytest.mark.parametrize("nq,nkv,hd,M,window", [
+    (32, 8, 128, 200, 0),   # Llama-shaped prompt
+    (8, 4, 256, 150, 64),   # gemma SWA layer, head_dim 256
+    (16, 2, 64, 100, 0),    # G = 8, head_dim 64
+])
+def test_prefill_on_q8_cache(mb, torch_cuda, orc, nq, nkv, hd, M, window):
+    """The multi-token prologue writes Q8 rows; prefill attention reads them
+    back (codes expanded per tile) and matches the reference's prefill on
+    the dequantized cache; a decode after it reads the same rows."""
     torch = torch_cuda
-    nq, nkv, hd, M = 16, 4, 128, 70
-    rng = np.random.default_rng(9)
+    rng = np.random.default_rng(M + hd)
     q = rng.standard_normal((M, nq, hd)).astype(np.float32)
     k = rng.standard_normal((M, nkv, hd)).astype(np.float32)
     v = rng.standard_normal((M, nkv, hd)).astype(np.float32)
@@ -182,17 +187,18 @@ def test_append_tokens_then_decode_q8(mb, torch_cuda, orc):
         kv.check()
         assert kv.length(0) == M
         assert_cache_equals(mb, orc, kv, 0, M, k.reshape(M, -1), v.reshape(M, -1))
-        out = torch.empty((M, nq, hd), device="cuda")
-        with pytest.raises(mb.MolotError) as e:
-            kv.prefill(0, qr, out, hd ** -0.5, 0)
-        assert e.value.status == mb.ERR_UNSUPPORTED
-        o = torch.empty(nq * hd, device="cuda")
-        kv.decode(0, qr[M - 1].reshape(-1).contiguous(), o, hd ** -0.5, M - 1, 0)
-        kv.check()
         _, _, kd = oracle_q8(orc, k.reshape(M, -1), nkv, hd)
         _, _, vd = oracle_q8(orc, v.reshape(M, -1), nkv, hd)
-        want = orc.attn_decode_gqa_cache(q[M - 1].reshape(-1), kd, vd, nq, nkv, M, hd,
-                                         hd ** -0.5, M - 1, 0)
-        assert orc.rel_err(o.cpu().numpy().reshape(nq, hd), want) <= PARITY_TOL
+        out = torch.full((M, nq, hd), float("nan"), device="cuda")
+        kv.prefill(0, qr, out, hd ** -0.5, 0, window)
+        kv.check()
+        want = orc.attn_prefill_gqa(q, kd, vd, nq, nkv, M, M, hd, hd ** -0.5, 0, window)
+        assert orc.rel_err(out.cpu().numpy(), want) <= PARITY_TOL
+        o = torch.empty(nq * hd, device="cuda")
+        kv.decode(0, qr[M - 1].reshape(-1).contiguous(), o, hd ** -0.5, M - 1, window)
+        kv.check()
+        want1 = orc.attn_decode_gqa_cache(q[M - 1].reshape(-1), kd, vd, nq, nkv, M, hd,
+                                          hd ** -0.5, M - 1, window)
+        assert orc.rel_err(o.cpu().numpy().reshape(nq, hd), want1) <= PARITY_TOL
     finally:
         kv.close()
