@@ -218,15 +218,23 @@ def step_work(cfg):
     return METRIC, "GB/s", step_bytes(cfg), 1e9
 
 
-def step_bytes(cfg):
+def kv_row_bytes(kv, d):
+    """Bytes of one cached row of one kv head in a storage type."""
+    if kv == "q8":
+        return (d + d // 8 + 15) & ~15
+    return d * (2 if kv == "bf16" else 4)
+
+
+def step_bytes(cfg, kv="f32"):
     """Unique KV bytes one decode step reads (all layers, all sequences)."""
     kind, nkv, d = cfg["kind"], cfg["nkv"], cfg["d"]
+    rb = kv_row_bytes(kv, d)
     if kind == "single":
-        return cfg["layers"] * 2 * nkv * (cfg["ctx"] + 1) * d * 4
+        return cfg["layers"] * 2 * nkv * (cfg["ctx"] + 1) * rb
     if kind == "gemma":
         n = cfg["ctx"] + 1
-        return sum(2 * nkv * attended(n, w) * d * 4 for w, _ in gemma_layers(cfg))
-    return cfg["layers"] * sum(2 * nkv * (x + 1) * d * 4 for x in paged_lengths(cfg))
+        return sum(2 * nkv * attended(n, w) * rb for w, _ in gemma_layers(cfg))
+    return cfg["layers"] * sum(2 * nkv * (x + 1) * rb for x in paged_lengths(cfg))
 
 
 class RefWorkload:
@@ -675,7 +683,7 @@ def emit(rt, args, cfg, ms, e2e_ms, clk, h2d, d2h, launches, roof, config, scali
     """The bench JSON line (rank 0)."""
     # weak scaling = replicas (every rank runs the whole step); strong = the
     # step's sequences or kv heads are split over the ranks
-    total = step_bytes(cfg) * (rt.world if scaling == "weak" else 1)
+    total = step_bytes(cfg, args.kv) * (rt.world if scaling == "weak" else 1)
     peak, peak_kind = hbm_peak()
     value = total / (ms * 1e-3) / 1e9
     line = {
@@ -683,7 +691,7 @@ def emit(rt, args, cfg, ms, e2e_ms, clk, h2d, d2h, launches, roof, config, scali
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1) K/V and q/k/v generated on device)",
-        "config": config,
+        "config": dict(config, kv_dtype=args.kv),
         "tok_per_s": round(cfg.get("batch", 1) * (rt.world if scaling == "weak" else 1)
                            * 1000.0 / ms, 2),
         "pct_hbm_peak": round(100.0 * value / rt.world / peak, 2),
@@ -712,12 +720,17 @@ def run_gemma(args, cfg):
     ctx, scale = cfg["ctx"], cfg["scale"]
     n = ctx + 1
     layers = gemma_layers(cfg)
-    cache = mb.KVCache(L, nkv, d, n)
+    cache = mb.KVCache(L, nkv, d, n, dtype=args.kv)
     gen = torch.Generator(device=rt.dev)
     gen.manual_seed(1234 + rt.rank)
     for l, (w, _) in enumerate(layers):
-        kt, vt = cache.layer_tensors(l)  # head-major [nkv][cap][hd]
         lo = max(0, ctx - w + 1) if w else 0
+        if args.kv == "q8":  # rows enter through the library's quantizing write
+            rows = torch.randn((2, ctx - lo, nkv * d), device=rt.dev, generator=gen)
+            cache.write(l, lo, rows[0], rows[1])
+            del rows
+            continue
+        kt, vt = cache.layer_tensors(l)  # head-major [nkv][cap][hd]
         kt[:, lo:ctx].normal_(generator=gen)
         vt[:, lo:ctx].normal_(generator=gen)
     q_raw = torch.randn((L, nq * d), device=rt.dev, generator=gen)
@@ -780,7 +793,7 @@ def run_gemma(args, cfg):
     e2e_ms = rt.max(rt.timed(e2e_step, args.steps))
     cache.check()
     del graph, ggraph
-    gbytes = 2 * nkv * n * d * 4
+    gbytes = 2 * nkv * n * kv_row_bytes(args.kv, d)
     if rt.rank == 0:
         emit(rt, args, cfg, ms, e2e_ms, clk,
              h2d=4 * L * (nq + 2 * nkv) * d, d2h=4 * L * nq * d, launches=L * args.steps,
@@ -1066,17 +1079,28 @@ def run_paged(args, cfg):
         bt[b, :m] = perm[k:k + m]
         k += m
     bt_dev = torch.from_numpy(bt).to(rt.dev)
-    pool_bytes = 2 * P * nkv_l * ps * d * 4
+    # bytes of one row of one kv head in the pools' storage type
+    rb = mb.q8_row_bytes(d) if args.kv == "q8" else d * (2 if args.kv == "bf16" else 4)
+    pool_bytes = 2 * P * nkv_l * ps * rb
     L_res = max(1, min(L, int(args.resident_gb * 1e9 // pool_bytes)))
     gen = torch.Generator(device=rt.dev)
     gen.manual_seed(1234 + rt.rank)
     template = torch.randn(1 << 26, device=rt.dev, generator=gen)
     pools = []
     for _ in range(L_res):
-        K = torch.empty((P, nkv_l, ps, d), device=rt.dev)
-        V = torch.empty((P, nkv_l, ps, d), device=rt.dev)
-        fill_normal(torch, K, template)
-        fill_normal(torch, V, template[7:])
+        if args.kv == "q8":  # random codes, block scales 0.02
+            K = torch.randint(0, 256, (P, nkv_l, ps, rb), dtype=torch.uint8, device=rt.dev,
+                              generator=gen)
+            V = torch.randint(0, 256, (P, nkv_l, ps, rb), dtype=torch.uint8, device=rt.dev,
+                              generator=gen)
+            for t in (K, V):
+                t[..., d:d + d // 8].view(torch.float32).fill_(0.02)
+        else:
+            dt = torch.bfloat16 if args.kv == "bf16" else torch.float32
+            K = torch.empty((P, nkv_l, ps, d), device=rt.dev, dtype=dt)
+            V = torch.empty((P, nkv_l, ps, d), device=rt.dev, dtype=dt)
+            fill_normal(torch, K, template)
+            fill_normal(torch, V, template[7:])
         pools.append((K, V))
     del template
     q_raw = torch.randn((L, Bl, nq_l, d), device=rt.dev, generator=gen)
@@ -1087,7 +1111,7 @@ def run_paged(args, cfg):
     o_full = torch.empty((L, B, nq, d), device=rt.dev) if gather else None
     freq = rope_freq(torch, cfg["theta"], d, rt.dev)
     scale = 1.0 / math.sqrt(d)
-    plan = mb.PagedPlan()
+    plan = mb.PagedPlan(args.kv)
     plan.build(nq_l, nkv_l, d, seq, None, 0)
     comm = torch.cuda.Stream() if gather else None
 
@@ -1159,7 +1183,7 @@ def run_paged(args, cfg):
     e2e_ms = rt.max(rt.timed(e2e_step, args.steps))
     plan.check()
     del graph, dgraph
-    local_layer_bytes = sum(2 * nkv_l * x * d * 4 for x in seq)
+    local_layer_bytes = sum(2 * nkv_l * x * rb for x in seq)
     h2d = rt.sum(4 * L * Bl * (nq_l + 2 * nkv_l) * d)
     d2h = rt.sum(h_o.numel() * 4)
     if rt.rank == 0:

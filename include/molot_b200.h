@@ -266,8 +266,10 @@ int molot_kv_check(molot_kv_cache* kv, void* stream);
  * Paged, batched decode (continuous batching; no counterpart in the
  * reference, which specifies but does not implement paging,
  * DESIGN.md:47-48,103 / README.md:113-114 of the reference).
- * Pools: K and V each [num_pages][nkv][page_size][d] FP32; page_size a
- * multiple of 16.  block_table [B][max_pages] int32 (device).
+ * Pools: K and V each [num_pages][nkv][page_size][d] FP32 (or BF16, or Q8
+ * rows of bytes, per molot_paged_plan_set_kv_dtype; the pool pointers are
+ * then raw bases despite their type); page_size a multiple of 16.
+ * block_table [B][max_pages] int32 (device).
  * ---------------------------------------------------------------------- */
 typedef struct molot_paged_plan molot_paged_plan;
 
@@ -278,6 +280,10 @@ int molot_paged_plan_create(molot_paged_plan** out);
 void molot_paged_plan_destroy(molot_paged_plan* plan);
 int molot_paged_plan_build(molot_paged_plan* plan, int B, int nq, int nkv, int d,
                            const int* seq_lens, const int* positions, int window, void* stream);
+/* Element type of the pools the plan's appends and decodes use: a
+ * molot_kv_dtype (MOLOT_KV_F32 when never set).  The same storage options
+ * as the KV handle; no counterpart in the reference (see molot_kv_dtype). */
+int molot_paged_plan_set_kv_dtype(molot_paged_plan* plan, int kv_dtype);
 
 /* Attention for every sequence of the plan: Q, O [B][nq][d] device. */
 int molot_paged_decode(molot_paged_plan* plan, const float* Q, float* O, const float* k_pool,
@@ -307,6 +313,10 @@ typedef struct molot_pager molot_pager;
 /* n_layers = 0: tables only, no device memory (and no CUDA call). */
 int molot_pager_create(int n_layers, int nkv, int d, int page_size, int num_pages, int max_seqs,
                        int max_pages_per_seq, molot_pager** out);
+/* molot_pager_create with pools of a molot_kv_dtype (rows of d floats, d
+ * bf16, or Q8 rows of q8 bytes: d codes, d/32 float scales, padded to 16). */
+int molot_pager_create_ex(int n_layers, int nkv, int d, int page_size, int num_pages,
+                          int max_seqs, int max_pages_per_seq, int kv_dtype, molot_pager** out);
 void molot_pager_destroy(molot_pager* p);
 /* A new sequence with `slots` slots reserved (its prompt); id in *seq.
  * MOLOT_ERR_CACHE_FULL when no sequence slot or not enough pages. */

@@ -125,6 +125,8 @@ _decl("molot_attn_append_rope_tokens",
 _decl("molot_attn_prefill", [_p, _i, _p, _p, _i, _i, _f, _i, _i, _p])
 _decl("molot_gemv_q4", [_p, _p, _p, _p, _i, _i, _p, _p])
 _decl("molot_pager_create", [_i, _i, _i, _i, _i, _i, _i, _pp])
+_decl("molot_pager_create_ex", [_i, _i, _i, _i, _i, _i, _i, _i, _pp])
+_decl("molot_paged_plan_set_kv_dtype", [_p, _i])
 _decl("molot_pager_destroy", [_p], None)
 _decl("molot_pager_add", [_p, _i, _p])
 _decl("molot_pager_grow", [_p, _i, _i])
@@ -454,11 +456,15 @@ class Pager:
     """Continuous-batching page manager (molot_pager_*): sequences, their
     pages and lengths, block tables for a batch, optional HBM page pools."""
 
-    def __init__(self, n_layers, nkv, d, page_size, num_pages, max_seqs, max_pages_per_seq):
+    def __init__(self, n_layers, nkv, d, page_size, num_pages, max_seqs, max_pages_per_seq,
+                 dtype: str = "f32"):
+        if dtype not in _KV_DTYPES:
+            raise ValueError("dtype must be 'f32', 'bf16' or 'q8'")
         h = ctypes.c_void_p()
-        check(_lib.molot_pager_create(n_layers, nkv, d, page_size, num_pages, max_seqs,
-                                      max_pages_per_seq, ctypes.byref(h)))
+        check(_lib.molot_pager_create_ex(n_layers, nkv, d, page_size, num_pages, max_seqs,
+                                         max_pages_per_seq, _KV_DTYPES[dtype], ctypes.byref(h)))
         self._h = h
+        self.dtype = dtype
         self.n_layers, self.nkv, self.d, self.page_size = n_layers, nkv, d, page_size
         self.num_pages, self.max_pages = num_pages, max_pages_per_seq
 
@@ -502,12 +508,23 @@ class Pager:
         return bt, lens
 
     def layer_pools(self, layer: int):
-        """(K, V) torch views [num_pages][nkv][page_size][d] of a layer's pools."""
+        """(K, V) torch views [num_pages][nkv][page_size][d] of a layer's pools:
+        float32, bfloat16 for bf16 pools, uint8 rows of q8_row_bytes(d) for
+        q8 pools."""
         import torch
         k = ctypes.c_void_p()
         v = ctypes.c_void_p()
         check(_lib.molot_pager_layer_pools(self._h, layer, ctypes.byref(k), ctypes.byref(v)))
         shape = (self.num_pages, self.nkv, self.page_size, self.d)
+        if self.dtype == "q8":
+            shape = shape[:3] + (q8_row_bytes(self.d),)
+            return (torch.as_tensor(_CudaArray(k.value, shape, "|u1"), device="cuda"),
+                    torch.as_tensor(_CudaArray(v.value, shape, "|u1"), device="cuda"))
+        if self.dtype == "bf16":
+            return (torch.as_tensor(_CudaArray(k.value, shape, "<i2"),
+                                    device="cuda").view(torch.bfloat16),
+                    torch.as_tensor(_CudaArray(v.value, shape, "<i2"),
+                                    device="cuda").view(torch.bfloat16))
         return (torch.as_tensor(_CudaArray(k.value, shape), device="cuda"),
                 torch.as_tensor(_CudaArray(v.value, shape), device="cuda"))
 
@@ -515,10 +532,14 @@ class Pager:
 class PagedPlan:
     """Batch shape of one decode step over a paged pool (see molot_b200.h)."""
 
-    def __init__(self):
+    def __init__(self, dtype: str = "f32"):
+        """dtype: element type of the pools it is used with ('f32', 'bf16', 'q8')."""
+        if dtype not in _KV_DTYPES:
+            raise ValueError("dtype must be 'f32', 'bf16' or 'q8'")
         h = ctypes.c_void_p()
         check(_lib.molot_paged_plan_create(ctypes.byref(h)))
         self._h = h
+        check(_lib.molot_paged_plan_set_kv_dtype(h, _KV_DTYPES[dtype]))
 
     def close(self) -> None:
         if getattr(self, "_h", None):

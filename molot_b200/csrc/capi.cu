@@ -649,6 +649,9 @@ struct molot_paged_plan {
   bool all_empty = false;
   // K pool whose newest slots the plan's most recent launch appended.
   const float* appended_pool = nullptr;
+  int kvt = MOLOT_KV_F32;  // element type of the pools it is used with
+  // Row pitch of the pools in stride units: d elements, or a Q8 row's bytes.
+  int rs() const { return kvt == MOLOT_KV_Q8 ? q8_row_bytes(d) : d; }
 };
 
 extern "C" {
@@ -1165,6 +1168,15 @@ void molot_paged_plan_destroy(molot_paged_plan* p) {
   delete p;
 }
 
+int molot_paged_plan_set_kv_dtype(molot_paged_plan* p, int kv_dtype) {
+  if (!p) return fail(MOLOT_ERR_INVALID, "null plan");
+  if (kv_dtype != MOLOT_KV_F32 && kv_dtype != MOLOT_KV_BF16 && kv_dtype != MOLOT_KV_Q8)
+    return fail(MOLOT_ERR_INVALID, "kv_dtype must be MOLOT_KV_F32, MOLOT_KV_BF16 or MOLOT_KV_Q8");
+  p->kvt = kv_dtype;
+  p->appended_pool = nullptr;
+  return MOLOT_OK;
+}
+
 int molot_paged_plan_build(molot_paged_plan* p, int B, int nq, int nkv, int d,
                            const int* seq_lens, const int* positions, int window, void* stream) {
   if (!p || !seq_lens || B <= 0) return fail(MOLOT_ERR_INVALID, "bad plan arguments");
@@ -1261,7 +1273,7 @@ int molot_paged_decode(molot_paged_plan* p, const float* Q, float* O, const floa
   if ((rc = current_device(&dev))) return rc;
   if (dev != p->device) return fail(MOLOT_ERR_INVALID, "plan used on another device");
   KernelRef k;
-  if ((rc = check_shape(p->nq, p->nkv, p->d, &k))) return rc;
+  if ((rc = check_shape(p->nq, p->nkv, p->d, &k, p->kvt))) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   // Sequences with an empty attended range produce zeros (attn.h:163).
   bool any_empty = false;
@@ -1283,8 +1295,8 @@ int molot_paged_decode(molot_paged_plan* p, const float* Q, float* O, const floa
   a.block_table = block_table;
   a.bt_stride = max_pages;
   a.page_size = page_size;
-  a.page_stride = (long long)p->nkv * page_size * p->d;
-  a.page_hstride = (long long)page_size * p->d;
+  a.page_stride = (long long)p->nkv * page_size * p->rs();
+  a.page_hstride = (long long)page_size * p->rs();
   a.nkv = p->nkv;
   a.G = p->nq / p->nkv;
   a.scale = scale;
@@ -1340,9 +1352,9 @@ int molot_paged_append(molot_paged_plan* p, const float* q, const float* k, cons
   a.block_table = block_table;
   a.bt_stride = max_pages;
   a.page_size = page_size;
-  a.page_stride = (long long)p->nkv * page_size * p->d;
-  a.page_hstride = (long long)page_size * p->d;
-  int rc = append_launch(a, p->d, p->B, (cudaStream_t)stream);
+  a.page_stride = (long long)p->nkv * page_size * p->rs();
+  a.page_hstride = (long long)page_size * p->rs();
+  int rc = append_launch(a, p->d, p->B, (cudaStream_t)stream, p->kvt);
   p->appended_pool = rc == MOLOT_OK ? k_pool : nullptr;
   return rc;
 }

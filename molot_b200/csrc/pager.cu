@@ -29,8 +29,9 @@ struct molot_pager {
   std::vector<std::vector<int>> pages;    // per sequence slot
   std::vector<int> len;                   // slots in use per sequence
   std::vector<char> live;
-  float* pools = nullptr;  // [n_layers][2][num_pages][nkv][page_size][d], may be null
-  size_t pool_floats = 0;  // per K (or V) pool of one layer
+  unsigned char* pools = nullptr;  // [n_layers][2][num_pages][nkv][page_size][row], may be null
+  size_t pool_bytes = 0;           // per K (or V) pool of one layer
+  int kvt = MOLOT_KV_F32;
   int device = -1;
   std::mutex mu;
 };
@@ -64,7 +65,17 @@ extern "C" {
 
 int molot_pager_create(int n_layers, int nkv, int d, int page_size, int num_pages, int max_seqs,
                        int max_pages_per_seq, molot_pager** out) {
+  return molot_pager_create_ex(n_layers, nkv, d, page_size, num_pages, max_seqs,
+                               max_pages_per_seq, MOLOT_KV_F32, out);
+}
+
+int molot_pager_create_ex(int n_layers, int nkv, int d, int page_size, int num_pages,
+                          int max_seqs, int max_pages_per_seq, int kv_dtype, molot_pager** out) {
   if (!out) return pager_fail(MOLOT_ERR_INVALID, "null out");
+  if (kv_dtype != MOLOT_KV_F32 && kv_dtype != MOLOT_KV_BF16 && kv_dtype != MOLOT_KV_Q8)
+    return pager_fail(MOLOT_ERR_INVALID, "kv_dtype must be MOLOT_KV_F32, MOLOT_KV_BF16 or MOLOT_KV_Q8");
+  if (kv_dtype == MOLOT_KV_Q8 && d % 64)
+    return pager_fail(MOLOT_ERR_INVALID, "Q8 pools need d a multiple of 64");
   *out = nullptr;
   if (n_layers < 0 || nkv <= 0 || d <= 0 || page_size <= 0 || page_size % 16 || num_pages <= 0 ||
       max_seqs <= 0 || max_pages_per_seq <= 0)
@@ -77,6 +88,7 @@ int molot_pager_create(int n_layers, int nkv, int d, int page_size, int num_page
   p->num_pages = num_pages;
   p->max_seqs = max_seqs;
   p->max_pages_per_seq = max_pages_per_seq;
+  p->kvt = kv_dtype;
   p->free_pages.resize(num_pages);
   for (int i = 0; i < num_pages; ++i) p->free_pages[i] = num_pages - 1 - i;  // 0 handed out first
   p->pages.assign(max_seqs, {});
@@ -84,9 +96,11 @@ int molot_pager_create(int n_layers, int nkv, int d, int page_size, int num_page
   p->live.assign(max_seqs, 0);
   if (n_layers > 0) {
     cudaGetDevice(&p->device);
-    p->pool_floats = (size_t)num_pages * nkv * page_size * d;
-    const cudaError_t e =
-        cudaMalloc(&p->pools, p->pool_floats * 2 * (size_t)n_layers * sizeof(float));
+    // bytes of one row of one kv head: d floats, d bf16, or a Q8 row
+    const size_t row = kv_dtype == MOLOT_KV_Q8 ? (size_t)((d + d / 8 + 15) & ~15)
+                                               : (size_t)d * (kv_dtype == MOLOT_KV_BF16 ? 2 : 4);
+    p->pool_bytes = ((size_t)num_pages * nkv * page_size * row + 255) & ~size_t(255);
+    const cudaError_t e = cudaMalloc(&p->pools, p->pool_bytes * 2 * (size_t)n_layers);
     if (e != cudaSuccess) {
       delete p;
       return pager_fail(MOLOT_ERR_NOMEM, std::string("cudaMalloc(page pools): ") +
@@ -187,8 +201,8 @@ int molot_pager_tables(molot_pager* p, const int* seqs, int B, int* block_table,
 int molot_pager_layer_pools(molot_pager* p, int layer, float** k_pool, float** v_pool) {
   if (!p || layer < 0 || layer >= p->n_layers || !p->pools)
     return pager_fail(MOLOT_ERR_INVALID, "bad layer (or a pager without pools)");
-  if (k_pool) *k_pool = p->pools + (size_t)(2 * layer) * p->pool_floats;
-  if (v_pool) *v_pool = p->pools + (size_t)(2 * layer + 1) * p->pool_floats;
+  if (k_pool) *k_pool = reinterpret_cast<float*>(p->pools + (size_t)(2 * layer) * p->pool_bytes);
+  if (v_pool) *v_pool = reinterpret_cast<float*>(p->pools + (size_t)(2 * layer + 1) * p->pool_bytes);
   return MOLOT_OK;
 }
 
