@@ -46,25 +46,27 @@ __device__ __forceinline__ float4 load4(const __nv_bfloat16* p) {
                      __uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u));
 }
 
-// Q8 caches (Q8Row, append.cuh): the raw rows of a tile (codes and block
-// scales) arrive through the same ring and are expanded once per tile into
-// FP32 tiles by the 256 consumer threads, each value (float)code * scale
-// exactly as the quantizer defines it; the score and output loops then run
-// on those tiles unchanged.
+// BF16 and Q8 caches (Q8Row, append.cuh): the raw rows of a tile arrive
+// through the same ring and are expanded once per tile into FP32 tiles by
+// the 256 consumer threads (bf16 values exactly; Q8 values as
+// (float)code * scale, exactly as the quantizer defines them); the score
+// and output loops then run on those tiles unchanged, instead of converting
+// every value in their inner loops.
 template <int D, class KT = float>
 struct PrefillTile {
   static constexpr bool kQ8 = std::is_same<KT, Q8Row>::value;
+  static constexpr bool kExpand = !std::is_same<KT, float>::value;  // expanded FP32 tiles
   static constexpr int EB = sizeof(KT);  // bytes per stride unit
   static constexpr int RB = kQ8 ? q8_row_bytes(D) : D * EB;  // bytes of a cache row
   static constexpr int BN = D > 128 ? 32 : 64;  // keys per tile
   static constexpr int NJ = BN / 16;            // score columns per thread
   static constexpr int LD = D + 4;              // padded Q row pitch (floats)
   static constexpr int LDK = (RB + 16) / EB;    // padded K/V row pitch (elements, +16 B)
-  static constexpr int LDF = D + 4;             // Q8: expanded FP32 tile pitch (floats)
+  static constexpr int LDF = D + 4;             // expanded FP32 tile pitch (floats)
   static constexpr int PLD = BN + 4;            // P row pitch (floats)
   static constexpr int kQ = kPrefillRows * LD * 4;
   static constexpr int kKV = BN * LDK * EB;  // one K or V tile as it arrives
-  static constexpr int kF = kQ8 ? BN * LDF * 4 : 0;  // Q8: one expanded K or V tile
+  static constexpr int kF = kExpand ? BN * LDF * 4 : 0;  // one expanded K or V tile
   static constexpr int kP = kPrefillRows * PLD * 4;
   static constexpr int kBars = 5 * 8;  // full[2], empty[2], q
   static constexpr int kTotal = kQ + 4 * kKV + 2 * kF + kP + kBars + 16;
@@ -100,15 +102,15 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   using TP = PrefillTile<D, KT>;
   constexpr int BN = TP::BN, NJ = TP::NJ, LD = TP::LD, LDK = TP::LDK, PLD = TP::PLD;
   // the type and pitch of the tiles the score / output loops read
-  using CT = typename std::conditional<TP::kQ8, float, KT>::type;
-  constexpr int LDC = TP::kQ8 ? TP::LDF : LDK;
+  using CT = typename std::conditional<TP::kExpand, float, KT>::type;
+  constexpr int LDC = TP::kExpand ? TP::LDF : LDK;
   constexpr int DJ = D / 64;  // float4 groups of output columns per thread
   constexpr float kLog2e = 1.4426950408889634f;
 
   extern __shared__ __align__(128) unsigned char smem[];
   float* Qs = reinterpret_cast<float*>(smem);
   KT* KVs = reinterpret_cast<KT*>(smem + TP::kQ);  // [stage][K,V][BN][LDK]
-  float* KVf = reinterpret_cast<float*>(smem + TP::kQ + 4 * TP::kKV);  // Q8: [K,V][BN][LDF]
+  float* KVf = reinterpret_cast<float*>(smem + TP::kQ + 4 * TP::kKV);  // [K,V][BN][LDF]
   float* Ps = reinterpret_cast<float*>(smem + TP::kQ + 4 * TP::kKV + 2 * TP::kF);
   uint64_t* full =
       reinterpret_cast<uint64_t*>(smem + TP::kQ + 4 * TP::kKV + 2 * TP::kF + TP::kP);
@@ -213,10 +215,10 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
     ok_waits &= ptx::mbar_wait_bounded(full + stage, (i >> 1) & 1, a.timeout_ns);
     const CT* Kt;
     const CT* Vt;
-    if constexpr (TP::kQ8) {
+    if constexpr (TP::kExpand) {
       // Every consumer is done with the previous expanded tiles; expand
-      // this tile (one 32-bit word of codes per task), publish, and hand the
-      // raw stage back to the producer at once.
+      // this tile (4 values per task), publish, and hand the raw stage back
+      // to the producer at once.
       ptx::named_bar_sync(1, kPrefillConsumers);
       const unsigned char* raw =
           reinterpret_cast<const unsigned char*>(KVs + (size_t)(stage * 2) * BN * LDK);
@@ -224,14 +226,19 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       for (int w = tid; w < 2 * kWords; w += kPrefillConsumers) {
         const int kv = w / kWords, rem = w - kv * kWords;
         const int row = rem / (D / 4), c4 = rem - row * (D / 4);
-        const unsigned char* rp = raw + (size_t)(kv * BN + row) * LDK;
-        const uint32_t code = *reinterpret_cast<const uint32_t*>(rp + 4 * c4) ^ 0x80808080u;
-        const float sc = *reinterpret_cast<const float*>(rp + D + 4 * (c4 >> 3));
-        float4 f;  // code + 128 in the low mantissa bits of 2^23, minus 2^23 + 128
-        f.x = __fmul_rn(__fsub_rn(__uint_as_float(__byte_perm(code, 0x4B000000u, 0x7650u)), 8388736.f), sc);
-        f.y = __fmul_rn(__fsub_rn(__uint_as_float(__byte_perm(code, 0x4B000000u, 0x7651u)), 8388736.f), sc);
-        f.z = __fmul_rn(__fsub_rn(__uint_as_float(__byte_perm(code, 0x4B000000u, 0x7652u)), 8388736.f), sc);
-        f.w = __fmul_rn(__fsub_rn(__uint_as_float(__byte_perm(code, 0x4B000000u, 0x7653u)), 8388736.f), sc);
+        float4 f;
+        if constexpr (TP::kQ8) {
+          const unsigned char* rp = raw + (size_t)(kv * BN + row) * LDK;
+          const uint32_t code = *reinterpret_cast<const uint32_t*>(rp + 4 * c4) ^ 0x80808080u;
+          const float sc = *reinterpret_cast<const float*>(rp + D + 4 * (c4 >> 3));
+          // code + 128 in the low mantissa bits of 2^23, minus 2^23 + 128
+          f.x = __fmul_rn(__fsub_rn(__uint_as_float(__byte_perm(code, 0x4B000000u, 0x7650u)), 8388736.f), sc);
+          f.y = __fmul_rn(__fsub_rn(__uint_as_float(__byte_perm(code, 0x4B000000u, 0x7651u)), 8388736.f), sc);
+          f.z = __fmul_rn(__fsub_rn(__uint_as_float(__byte_perm(code, 0x4B000000u, 0x7652u)), 8388736.f), sc);
+          f.w = __fmul_rn(__fsub_rn(__uint_as_float(__byte_perm(code, 0x4B000000u, 0x7653u)), 8388736.f), sc);
+        } else {  // bf16: 4 values in 8 bytes
+          f = load4(KVs + (size_t)(stage * 2 + kv) * BN * LDK + (size_t)row * LDK + 4 * c4);
+        }
         *reinterpret_cast<float4*>(KVf + (size_t)(kv * BN + row) * LDC + 4 * c4) = f;
       }
       ptx::named_bar_sync(1, kPrefillConsumers);
@@ -344,7 +351,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
       }
     }
     __syncwarp();  // this warp's P rows may be rewritten by the next tile
-    if (!TP::kQ8 && lane == 0) ptx::mbar_arrive(empty + stage);
+    if (!TP::kExpand && lane == 0) ptx::mbar_arrive(empty + stage);
   }
   if (!ok_waits || *abort_sm) {
     atomicCAS(a.status, 0, 3);
