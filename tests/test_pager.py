@@ -72,3 +72,20 @@ def test_capacity_errors(mbl):
 def test_rejects_bad_page_size(mbl):
     with pytest.raises(mbl.MolotError):
         mbl.Pager(0, 2, 64, 10, 4, 2, 3)
+
+
+def test_storage_types(mbl):
+    """Pools of each storage type are accepted (tables-only here: no device
+    memory); an unknown type and Q8 rows that do not split into 32-value
+    blocks of both halves are refused."""
+    for dtype in ("f32", "bf16", "q8"):
+        p = mbl.Pager(0, 2, 128, 16, 4, 2, 3, dtype=dtype)
+        assert p.dtype == dtype and p.free_pages() == 4
+        p.close()
+    with pytest.raises(ValueError):
+        mbl.Pager(0, 2, 128, 16, 4, 2, 3, dtype="fp8")
+    with pytest.raises(mbl.MolotError) as e:
+        mbl.Pager(0, 2, 96, 16, 4, 2, 3, dtype="q8")
+    assert e.value.status == mbl.ERR_INVALID
+    h = mbl.ctypes.c_void_p()
+    assert mbl._lib.molot_pager_create_ex(0, 2, 128, 16, 4, 2, 3, 7, mbl.ctypes.byref(h)) == mbl.ERR_INVALID
