@@ -152,4 +152,85 @@ class KVCache {
   int nkv_, hd_, cap_;
 };
 
+// Continuous-batching page manager (molot_pager_*): sequences, their pages
+// and lengths, block tables for a batch, and optionally the per-layer K/V
+// page pools in HBM ([num_pages][nkv][page_size][d] of the storage type).
+class Pager {
+ public:
+  Pager(int n_layers, int nkv, int d, int page_size, int num_pages, int max_seqs,
+        int max_pages_per_seq, int kv_dtype = MOLOT_KV_F32)
+      : max_pages_(max_pages_per_seq) {
+    check(molot_pager_create_ex(n_layers, nkv, d, page_size, num_pages, max_seqs,
+                                max_pages_per_seq, kv_dtype, &h_));
+  }
+  ~Pager() { molot_pager_destroy(h_); }
+  Pager(const Pager&) = delete;
+  Pager& operator=(const Pager&) = delete;
+
+  int add(int slots) {
+    int s = -1;
+    check(molot_pager_add(h_, slots, &s));
+    return s;
+  }
+  void grow(int seq, int n_new = 1) { check(molot_pager_grow(h_, seq, n_new)); }
+  void free(int seq) { check(molot_pager_free(h_, seq)); }
+  int length(int seq) const {
+    int r = molot_pager_length(h_, seq);
+    if (r < 0) check(r);
+    return r;
+  }
+  int free_pages() const { return molot_pager_free_pages(h_); }
+  int max_pages() const { return max_pages_; }
+  // Host block table [B][max_pages()] and lengths of the batch `seqs`.
+  void tables(const int* seqs, int B, int* block_table, int* seq_lens) {
+    check(molot_pager_tables(h_, seqs, B, block_table, seq_lens));
+  }
+  // Device K/V pools of one layer (raw bases for BF16 / Q8 pools).
+  void layer_pools(int layer, float** k_pool, float** v_pool) {
+    check(molot_pager_layer_pools(h_, layer, k_pool, v_pool));
+  }
+
+ private:
+  molot_pager* h_ = nullptr;
+  int max_pages_;
+};
+
+// Batch shape of one paged decode step (molot_paged_*): build once per step,
+// then append + decode per layer over that layer's pools.
+class PagedPlan {
+ public:
+  explicit PagedPlan(int kv_dtype = MOLOT_KV_F32) {
+    check(molot_paged_plan_create(&h_));
+    check(molot_paged_plan_set_kv_dtype(h_, kv_dtype));
+  }
+  ~PagedPlan() { molot_paged_plan_destroy(h_); }
+  PagedPlan(const PagedPlan&) = delete;
+  PagedPlan& operator=(const PagedPlan&) = delete;
+
+  // seq_lens (host): slots per sequence, the new token's included.
+  void build(int B, int nq, int nkv, int d, const int* seq_lens, const int* positions = nullptr,
+             int window = 0, void* stream = nullptr) {
+    check(molot_paged_plan_build(h_, B, nq, nkv, d, seq_lens, positions, window, stream));
+  }
+  // forward.h:554-575 for the batch: the new rows go to slot seq_lens[b]-1.
+  void append(const float* q, const float* k, const float* v, float* q_out, const float* q_norm,
+              const float* k_norm, bool v_norm, float eps, const float* freq, float* k_pool,
+              float* v_pool, const int* block_table, int max_pages, int page_size,
+              void* stream = nullptr) {
+    check(molot_paged_append(h_, q, k, v, q_out, q_norm, k_norm, v_norm ? 1 : 0, eps, freq, k_pool,
+                             v_pool, block_table, max_pages, page_size, stream));
+  }
+  void decode(const float* Q, float* O, const float* k_pool, const float* v_pool,
+              const int* block_table, int max_pages, int page_size, float scale,
+              void* stream = nullptr) {
+    check(molot_paged_decode(h_, Q, O, k_pool, v_pool, block_table, max_pages, page_size, scale,
+                             stream));
+  }
+  // Synchronise and surface device-side wait timeouts.
+  void sync(void* stream = nullptr) { check(molot_paged_check(h_, stream)); }
+
+ private:
+  molot_paged_plan* h_ = nullptr;
+};
+
 }  // namespace molot_b200

@@ -4,6 +4,7 @@
 // failed CHECK, like the reference's bench.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <random>
@@ -207,6 +208,79 @@ int main() {
     const double e = rel_err(y, r);
     CHECK(e <= 1e-6, "gemv_q4 rel err %g", e);
     std::printf("[ok] gemv_q4 %dx%d rel_err=%.2e\n", rows, cols, e);
+  }
+  // ---- continuous batching through Pager + PagedPlan (FP32 pools)
+  {
+    const int nq = 8, nkv = 2, d = 128, ps = 16, B = 2;
+    molot_b200::Pager pager(1, nkv, d, ps, 16, 4, 8);
+    const int s0 = pager.add(30), s1 = pager.add(9);
+    const int seqs[B] = {s0, s1};
+    float *kp, *vp;
+    pager.layer_pools(0, &kp, &vp);
+    std::vector<int> bt((size_t)B * pager.max_pages()), lens(B);
+    pager.tables(seqs, B, bt.data(), lens.data());
+    // host mirrors of each sequence's cache ([n][nkv*d]), prompt rows scattered into pages
+    std::vector<std::vector<float>> hk(B), hv(B);
+    for (int b = 0; b < B; ++b) {
+      hk[b].resize((size_t)lens[b] * nkv * d);
+      hv[b].resize(hk[b].size());
+      for (auto& x : hk[b]) x = frand();
+      for (auto& x : hv[b]) x = frand();
+      for (int t = 0; t < lens[b]; ++t)
+        for (int g = 0; g < nkv; ++g) {
+          const size_t dst = (((size_t)bt[b * pager.max_pages() + t / ps] * nkv + g) * ps +
+                              t % ps) * d;
+          cudaMemcpy(kp + dst, hk[b].data() + ((size_t)t * nkv + g) * d, d * 4,
+                     cudaMemcpyHostToDevice);
+          cudaMemcpy(vp + dst, hv[b].data() + ((size_t)t * nkv + g) * d, d * 4,
+                     cudaMemcpyHostToDevice);
+        }
+    }
+    for (int b = 0; b < B; ++b) pager.grow(seqs[b]);
+    pager.tables(seqs, B, bt.data(), lens.data());
+    std::vector<float> q((size_t)B * nq * d), k((size_t)B * nkv * d), v(k.size()),
+        o(q.size()), ref((size_t)nq * d);
+    for (auto& x : q) x = frand();
+    for (auto& x : k) x = frand();
+    for (auto& x : v) x = frand();
+    float *dq, *dk, *dv, *dqr, *dout;
+    int* dbt;
+    cudaMalloc(&dq, q.size() * 4);
+    cudaMalloc(&dk, k.size() * 4);
+    cudaMalloc(&dv, v.size() * 4);
+    cudaMalloc(&dqr, q.size() * 4);
+    cudaMalloc(&dout, q.size() * 4);
+    cudaMalloc(&dbt, bt.size() * 4);
+    cudaMemcpy(dq, q.data(), q.size() * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(dk, k.data(), k.size() * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(dv, v.data(), v.size() * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(dbt, bt.data(), bt.size() * 4, cudaMemcpyHostToDevice);
+    molot_b200::PagedPlan plan;
+    plan.build(B, nq, nkv, d, lens.data());
+    const float scale = 1.f / std::sqrt((float)d);
+    plan.append(dq, dk, dv, dqr, nullptr, nullptr, false, 1e-6f, nullptr, kp, vp, dbt,
+                pager.max_pages(), ps);
+    plan.decode(dqr, dout, kp, vp, dbt, pager.max_pages(), ps, scale);
+    plan.sync();
+    cudaMemcpy(o.data(), dout, o.size() * 4, cudaMemcpyDeviceToHost);
+    double worst = 0;
+    for (int b = 0; b < B; ++b) {
+      hk[b].insert(hk[b].end(), k.begin() + (size_t)b * nkv * d, k.begin() + (size_t)(b + 1) * nkv * d);
+      hv[b].insert(hv[b].end(), v.begin() + (size_t)b * nkv * d, v.begin() + (size_t)(b + 1) * nkv * d);
+      oracle_attn_decode_gqa_cache(q.data() + (size_t)b * nq * d, hk[b].data(), hv[b].data(),
+                                   ref.data(), nq, nkv, lens[b], d, scale, lens[b] - 1, 0);
+      std::vector<float> got(o.begin() + (size_t)b * nq * d, o.begin() + (size_t)(b + 1) * nq * d);
+      worst = std::max(worst, rel_err(got, ref));
+    }
+    CHECK(worst <= 1e-5, "paged decode rel err %g", worst);
+    CHECK(pager.length(s0) == 31 && pager.length(s1) == 10, "pager lengths");
+    cudaFree(dq);
+    cudaFree(dk);
+    cudaFree(dv);
+    cudaFree(dqr);
+    cudaFree(dout);
+    cudaFree(dbt);
+    std::printf("[ok] Pager + PagedPlan append/decode B=%d rel_err=%.2e\n", B, worst);
   }
   if (failures) {
     std::printf("CORRECTNESS: %d FAILURES\n", failures);
