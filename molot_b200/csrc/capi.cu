@@ -159,9 +159,9 @@ struct KernelRef {
   int smem = 0;
 };
 
-template <int D, int GS, int HS, class KT = float>
+template <int D, int GS, int HS, class KT = float, bool SPLIT = false>
 KernelRef decode_ref() {
-  return {reinterpret_cast<const void*>(&gqa_decode_kernel<D, GS, HS, KT>),
+  return {reinterpret_cast<const void*>(&gqa_decode_kernel<D, GS, HS, KT, SPLIT>),
           DecodeSmem<D, GS, KT>::kTotal};
 }
 
@@ -204,6 +204,33 @@ bool pick_decode_t(int D, int G, KernelRef* k) {
 }
 
 bool pick_decode(int D, int G, KernelRef* k) { return pick_decode_t<float>(D, G, k); }
+
+// FP32 kernels with split K/V stage barriers (hd <= 128; see gqa_decode_kernel).
+bool pick_decode_split(int D, int G, KernelRef* k) {
+  switch (D) {
+    case 64:
+      switch (G) {
+        case 1: *k = decode_ref<64, 1, 1, float, true>(); return true;
+        case 2: *k = decode_ref<64, 2, 1, float, true>(); return true;
+        case 4: *k = decode_ref<64, 4, 1, float, true>(); return true;
+        case 8: *k = decode_ref<64, 8, 1, float, true>(); return true;
+        case 16: *k = decode_ref<64, 8, 2, float, true>(); return true;
+        case 32: *k = decode_ref<64, 8, 4, float, true>(); return true;
+      }
+      return false;
+    case 128:
+      switch (G) {
+        case 1: *k = decode_ref<128, 1, 1, float, true>(); return true;
+        case 2: *k = decode_ref<128, 2, 1, float, true>(); return true;
+        case 4: *k = decode_ref<128, 4, 1, float, true>(); return true;
+        case 8: *k = decode_ref<128, 4, 2, float, true>(); return true;
+        case 16: *k = decode_ref<128, 4, 4, float, true>(); return true;
+        case 32: *k = decode_ref<128, 4, 8, float, true>(); return true;
+      }
+      return false;
+  }
+  return false;
+}
 
 // kvt: the cache's molot_kv_dtype.
 bool pick_decode_kv(int D, int G, int kvt, KernelRef* k) {
@@ -322,6 +349,17 @@ int decode_uniform(Workspace& ws, const float* Q, float* O, const void* K, const
   // of slots for it measured best (cfg2 fused step, FP32 and BF16 caches);
   // the two forms keep one partition, so their results stay bit-identical.
   a.tail_w = (fused || prefetch_old_rows) ? kShareW / 2 : 0;
+  {
+    // Split K/V stage barriers where they measured faster (see the kernel).
+    const int tile_rows = d <= 64 ? TileShape<64, float>::T : TileShape<128, float>::T;
+    const long long rows_per_cta = (long long)nblk * kBlk * nkv / grid;
+    KernelRef ks;
+    if (kvt == MOLOT_KV_F32 && d <= 128 && a.aligned && rows_per_cta >= 8LL * tile_rows &&
+        pick_decode_split(d, G, &ks)) {
+      k = ks;
+      if ((rc = prepare_kernel(k, dev))) return rc;
+    }
+  }
   a.prefetch_old_rows = prefetch_old_rows ? 1 : 0;
   if (fused) {  // per-token prologue fused into this launch (slot n-1 is new)
     a.fused = 1;

@@ -293,7 +293,7 @@ struct DecodeSmem {
   // fused mode: the new k and v rows, then the launch's constants (cos and
   // sin of the RoPE angles [D/2] each, q_norm [D], k_norm [D])
   static constexpr int kNewRow = 2 * D * 4 + 3 * D * 4;
-  static constexpr int kBars = 2 * TS::STAGES * 8;
+  static constexpr int kBars = 4 * TS::STAGES * 8;  // full and empty, K and V halves
   static constexpr int kTotal = kStageBytes + kMergeO + kMergeML + kNewRow + kBars + 16;
   static_assert(kTotal <= 227 * 1024, "decode CTA exceeds the shared-memory limit");
 };
@@ -397,12 +397,13 @@ __device__ __forceinline__ float ex2(float x) {
 // kr / vr point at the chunk's first K / V row in shared memory; rows are D
 // elements apart; each lane reads its dims (KvElem<KT>).  FULL: every row is
 // valid.
-template <int D, int GS, int RC, bool FULL, class KT>
+template <int D, int GS, int RC, bool FULL, class KT, class AfterQK, class BeforePV>
 __device__ __forceinline__ void process_rows(const KT* kr, const KT* vr, int tok, int pt0,
                                              int pt1, float scale, float (&q)[GS][D / 8],
                                              float (&o)[GS][D / 8], float (&m2)[GS],
                                              float (&l)[GS], int new_tok, const KT* nk,
-                                             const KT* nv, int l8) {
+                                             const KT* nv, int l8, AfterQK after_qk,
+                                             BeforePV before_pv) {
   constexpr int DV = D / 16;
   constexpr int RS = TileShape<D, KT>::RS;
   using E = KvElem<KT>;
@@ -442,6 +443,7 @@ __device__ __forceinline__ void process_rows(const KT* kr, const KT* vr, int tok
       sc[r][h] = ok[r] ? s : -CUDART_INF_F;
     }
   }
+  after_qk();  // the chunk's K rows are read
   bool need_any = false;
   float mc2[GS];
 #pragma unroll
@@ -473,6 +475,7 @@ __device__ __forceinline__ void process_rows(const KT* kr, const KT* vr, int tok
       l[h] += p[r][h];
     }
   }
+  before_pv();  // the chunk's V rows may be read from here on
 #pragma unroll
   for (int r = 0; r < RC; ++r) {
     const KT* v = (!FULL && tok + r == new_tok) ? nv : vr + r * RS;
@@ -772,7 +775,13 @@ __device__ __forceinline__ void combine_segment(const DecodeArgs& a, int s, cons
   }
 }
 
-template <int D, int GS, int HS, class KT = float>
+// SPLIT: the K and V halves of each ring stage fill and free on their own
+// barriers, so a stage's K half is refilled as soon as every warp has its
+// scores.  The host launches it where it measured faster: single-sequence
+// FP32 launches at hd <= 128 with at least 8 tiles per CTA (cfg2 -3 %); it
+// was slower with fewer tiles, for the consumer-bound BF16 / Q8 launches and
+// for paged batches, which therefore run the one-barrier-pair form.
+template <int D, int GS, int HS, class KT = float, bool SPLIT = false>
 __global__ void __launch_bounds__(kDecodeThreads, 1)
     gqa_decode_kernel(const __grid_constant__ DecodeArgs a) {
   using TS = TileShape<D, KT>;
@@ -806,8 +815,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
                                         2 * D * 4);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + SM::kStageBytes + SM::kMergeO +
                                                    SM::kMergeML + SM::kNewRow);
-  uint64_t* empty_bar = full_bar + STAGES;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty_bar + STAGES);
+  // [stage][K, V]: in split mode the halves of a stage fill and free
+  // separately; otherwise a stage uses its K half's barriers for both
+  uint64_t* empty_bar = full_bar + 2 * STAGES;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty_bar + 2 * STAGES);
   volatile int* ticket_sm = abort_flag + 1;
   volatile int* seg_cta_sm = abort_flag + 2;  // [2]
 
@@ -815,7 +826,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; ++i) {
+    for (int i = 0; i < 2 * STAGES; ++i) {
       ptx::mbar_init(full_bar + i, 1);
       ptx::mbar_init(empty_bar + i, kConsumerWarps);
     }
@@ -829,6 +840,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   // on the SMs that the preceding launch's last CTAs free; they take the
   // lightest ranges (the first CTAs of a segment, never the new row's).
   const int cta = a.grid - 1 - (int)blockIdx.x;
+  constexpr bool split = SPLIT;
   const long long cbeg = range_begin(a, cta);
   const long long cend = range_begin(a, cta + 1);
   const int s_first = first_seg_of_cta(a, cta);
@@ -855,73 +867,80 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         const int pt1c = a.fused ? min(pt1, sv.n - 1) : pt1;
         for (int blk = lb; blk < le; blk += TS::TB, ++it) {
           const int stage = it % STAGES;
-          if (it >= STAGES && !*abort_flag) {
-            if (!ptx::mbar_wait_bounded(empty_bar + stage, ((it / STAGES) - 1) & 1,
-                                        a.timeout_ns)) {
-              if (lane == 0) raise_status(a, abort_flag, kDevErrProducerTimeout);
-            }
-          }
-          __syncwarp();
           const int tok0 = blk * kBlk;
-          // Slots written by the immediately preceding launch (the new
-          // token's row) may only be read after that launch has completed.
-          if (!waited && (!a.prefetch_old_rows || min(tok0 + TS::T, pt1c) >= sv.n)) {
-            ptx::pdl_wait();
-            waited = true;
-          }
           int qa[4], qn[4];
-          uint32_t bytes = 0;
+          uint32_t bytes = 0;  // of one half (K or V)
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int lo = max(tok0 + q * QR, pt0);
             const int hi = min(tok0 + (q + 1) * QR, pt1c);
             qa[q] = lo;
             qn[q] = hi > lo ? hi - lo : 0;
-            bytes += (uint32_t)qn[q] * TS::RB * 2u;
+            bytes += (uint32_t)qn[q] * TS::RB;
           }
-          if (*abort_flag) {
-            // Consumers skip waits once aborted; complete the phase without data.
-            if (lane == 0) ptx::mbar_arrive(full_bar + stage);
-            continue;
-          }
-          if (lane == 0) ptx::mbar_arrive_expect_tx(full_bar + stage, bytes);
-          __syncwarp();
           unsigned char* st_base = stages + (size_t)stage * TS::STAGE;
-          if (rows_contig) {
-            if (lane < 8) {
-              const int q = lane & 3;
-              const int kv = lane >> 2;
-              if (qn[q] > 0) {
-                const unsigned char* base = static_cast<const unsigned char*>(kv ? a.V : a.K);
-                long long off;  // stride units
-                if (a.block_table) {
-                  const int p =
-                      __ldg(a.block_table + (long long)sv.b * a.bt_stride + qa[q] / a.page_size);
-                  off = (long long)p * a.page_stride + (long long)sv.g * a.page_hstride +
-                        (long long)(qa[q] % a.page_size) * TS::RS;
-                } else {
-                  off = (long long)sv.b * a.kv_bstride + (long long)qa[q] * a.stride_t +
-                        (long long)sv.g * a.stride_h;
-                }
-                unsigned char* dst = st_base + kv * TS::KQ + q * TS::QSTRIDE +
-                                     (qa[q] - (tok0 + q * QR)) * TS::RB;
-                ptx::bulk_g2s(dst, base + off * EB, (uint32_t)qn[q] * TS::RB, full_bar + stage,
-                              pol);
+          // Split mode: the K and V halves are awaited and filled one after
+          // the other, each on its own barriers (lanes 0-3 issue a half's
+          // quarters).  Otherwise one round fills both halves through the K
+          // half's barriers (lanes 0-7: quarter = lane & 3, half = lane >> 2).
+          for (int kv = 0; kv < (split ? 2 : 1); ++kv) {
+            uint64_t* fb = full_bar + 2 * stage + kv;
+            if (it >= STAGES && !*abort_flag) {
+              if (!ptx::mbar_wait_bounded(empty_bar + 2 * stage + kv, ((it / STAGES) - 1) & 1,
+                                          a.timeout_ns)) {
+                if (lane == 0) raise_status(a, abort_flag, kDevErrProducerTimeout);
               }
             }
-          } else {
-            for (int idx = lane; idx < 2 * 4 * QR; idx += 32) {
-              const int kv = idx / (4 * QR);
-              const int rem = idx - kv * 4 * QR;
-              const int q = rem / QR;
-              const int r = rem - q * QR;
-              const int t = tok0 + q * QR + r;
-              if (t >= qa[q] && t < qa[q] + qn[q]) {
-                const unsigned char* base = static_cast<const unsigned char*>(kv ? a.V : a.K);
-                const long long off = (long long)sv.b * a.kv_bstride + (long long)t * a.stride_t +
-                                      (long long)sv.g * a.stride_h;
-                unsigned char* dst = st_base + kv * TS::KQ + q * TS::QSTRIDE + r * TS::RB;
-                ptx::bulk_g2s(dst, base + off * EB, (uint32_t)TS::RB, full_bar + stage, pol);
+            __syncwarp();
+            // Slots written by the immediately preceding launch (the new
+            // token's row) may only be read after that launch has completed.
+            if (!waited && (!a.prefetch_old_rows || min(tok0 + TS::T, pt1c) >= sv.n)) {
+              ptx::pdl_wait();
+              waited = true;
+            }
+            if (*abort_flag) {
+              // Consumers skip waits once aborted; complete the phase without data.
+              if (lane == 0) ptx::mbar_arrive(fb);
+              continue;
+            }
+            if (lane == 0) ptx::mbar_arrive_expect_tx(fb, split ? bytes : 2 * bytes);
+            __syncwarp();
+            if (rows_contig) {
+              if (lane < (split ? 4 : 8)) {
+                const int q = lane & 3;
+                const int h = split ? kv : lane >> 2;  // K or V half
+                if (qn[q] > 0) {
+                  const unsigned char* base = static_cast<const unsigned char*>(h ? a.V : a.K);
+                  long long off;  // stride units
+                  if (a.block_table) {
+                    const int p =
+                        __ldg(a.block_table + (long long)sv.b * a.bt_stride + qa[q] / a.page_size);
+                    off = (long long)p * a.page_stride + (long long)sv.g * a.page_hstride +
+                          (long long)(qa[q] % a.page_size) * TS::RS;
+                  } else {
+                    off = (long long)sv.b * a.kv_bstride + (long long)qa[q] * a.stride_t +
+                          (long long)sv.g * a.stride_h;
+                  }
+                  unsigned char* dst = st_base + h * TS::KQ + q * TS::QSTRIDE +
+                                       (qa[q] - (tok0 + q * QR)) * TS::RB;
+                  ptx::bulk_g2s(dst, base + off * EB, (uint32_t)qn[q] * TS::RB, fb, pol);
+                }
+              }
+            } else {
+              const int n_idx = (split ? 1 : 2) * 4 * QR;
+              for (int idx = lane; idx < n_idx; idx += 32) {
+                const int h = split ? kv : idx / (4 * QR);
+                const int rem = split ? idx : idx - h * 4 * QR;
+                const int q = rem / QR;
+                const int r = rem - q * QR;
+                const int t = tok0 + q * QR + r;
+                if (t >= qa[q] && t < qa[q] + qn[q]) {
+                  const unsigned char* base = static_cast<const unsigned char*>(h ? a.V : a.K);
+                  const long long off = (long long)sv.b * a.kv_bstride +
+                                        (long long)t * a.stride_t + (long long)sv.g * a.stride_h;
+                  unsigned char* dst = st_base + h * TS::KQ + q * TS::QSTRIDE + r * TS::RB;
+                  ptx::bulk_g2s(dst, base + off * EB, (uint32_t)TS::RB, fb, pol);
+                }
               }
             }
           }
@@ -933,10 +952,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     // Drain: every issued stage must have landed before the CTA may exit.
     if (lane == 0) {
       const int first = it > STAGES ? it - STAGES : 0;
-      for (int j = first; j < it; ++j) {
-        if (!ptx::mbar_wait_bounded(full_bar + (j % STAGES), (j / STAGES) & 1, a.timeout_ns)) {
-          raise_status(a, abort_flag, kDevErrProducerTimeout);
-          break;
+      bool ok = true;
+      for (int j = first; j < it && ok; ++j) {
+        for (int kv = 0; kv < (split ? 2 : 1) && ok; ++kv) {
+          if (!ptx::mbar_wait_bounded(full_bar + 2 * (j % STAGES) + kv, (j / STAGES) & 1,
+                                      a.timeout_ns)) {
+            raise_status(a, abort_flag, kDevErrProducerTimeout);
+            ok = false;
+          }
         }
       }
     }
@@ -1026,12 +1049,16 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
 
       for (int blk = lb; blk < le; blk += TS::TB, ++it) {
         const int stage = it % STAGES;
+        const uint32_t par = (it / STAGES) & 1;
+        uint64_t* fk = full_bar + 2 * stage;  // K half; fk + 1: V half
+        uint64_t* ek = empty_bar + 2 * stage;
         if (!*abort_flag) {
-          if (!ptx::mbar_wait_bounded(full_bar + stage, (it / STAGES) & 1, a.timeout_ns)) {
+          if (!ptx::mbar_wait_bounded(fk, par, a.timeout_ns)) {
             if (lane == 0) raise_status(a, abort_flag, kDevErrConsumerTimeout);
           }
         }
         __syncwarp();
+        bool k_freed = false;  // this warp has released the K half
         if (!*abort_flag) {
           const KT* kq = reinterpret_cast<const KT*>(stages + (size_t)stage * TS::STAGE +
                                                      grp * TS::QSTRIDE);
@@ -1042,24 +1069,45 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
           // [pt0, pt1); the rest take the predicate-free path.
           const bool full = blk * kBlk >= pt0 && blk * kBlk + TS::T <= pt1 &&
                             !(new_tok >= blk * kBlk && new_tok < blk * kBlk + TS::T);
+          // The K half is released once the warp's last chunk has its
+          // scores; the V half is waited for before its first chunk's P*V.
+          int r0 = 0;
+          auto after_qk = [&]() {
+            if (split && r0 + RC >= R) {
+              __syncwarp();
+              if (lane == 0) ptx::mbar_arrive(ek);
+              k_freed = true;
+            }
+          };
+          auto before_pv = [&]() {
+            if (split && r0 == 0) {
+              if (!*abort_flag && !ptx::mbar_wait_bounded(fk + 1, par, a.timeout_ns)) {
+                if (lane == 0) raise_status(a, abort_flag, kDevErrConsumerTimeout);
+              }
+              __syncwarp();
+            }
+          };
           // One copy of each chunk body: the chunk loops stay rolled so the
           // instruction working set fits the SM's instruction cache.
           if (full) {
 #pragma unroll 1
-            for (int r0 = 0; r0 < R; r0 += RC)
+            for (r0 = 0; r0 < R; r0 += RC)
               process_rows<D, GS, RC, true>(kq + (wi * R + r0) * TS::RS, vq + (wi * R + r0) * TS::RS,
                                             tok_base + r0, pt0, pt1, a.scale, q, o, m, l,
-                                            new_tok, new_k, new_v, l8);
+                                            new_tok, new_k, new_v, l8, after_qk, before_pv);
           } else {
 #pragma unroll 1
-            for (int r0 = 0; r0 < R; r0 += RC)
+            for (r0 = 0; r0 < R; r0 += RC)
               process_rows<D, GS, RC, false>(kq + (wi * R + r0) * TS::RS, vq + (wi * R + r0) * TS::RS,
                                              tok_base + r0, pt0, pt1, a.scale, q, o, m, l,
-                                             new_tok, new_k, new_v, l8);
+                                             new_tok, new_k, new_v, l8, after_qk, before_pv);
           }
         }
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(empty_bar + stage);
+        if (lane == 0) {
+          if (!k_freed) ptx::mbar_arrive(ek);
+          if (split) ptx::mbar_arrive(ek + 1);
+        }
       }
 
       // ---- finalize the piece: merge 4 row groups, then warps, then CTAs.
