@@ -21,6 +21,7 @@
 #ifndef MOLOT_B200_H
 #define MOLOT_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -45,10 +46,22 @@ enum molot_status {
 const char* molot_status_string(int status);
 /* Detail of the last error on the calling thread (CUDA error text etc.). */
 const char* molot_last_error(void);
-/* Reads (and clears when `clear` != 0) the device-side status word of the
- * current device's default workspace; synchronises the device.  Returns
+/* Reads (and clears when `clear` != 0) the device-side status words of the
+ * current device's default workspace and of its no-alloc scratch (see
+ * molot_attn_decode_strided_noalloc); synchronises the device.  Returns
  * MOLOT_OK or MOLOT_ERR_TIMEOUT. */
 int molot_device_status(int clear);
+
+/* Failure-detection test hook (no counterpart in the reference).  The next
+ * decode-kernel launch made by the calling host thread, through any entry
+ * point, runs with its producer withholding every copy and with its stage
+ * waits bounded by wait_limit_ns: the consumers' first wait runs out with no
+ * copy in flight, the launch records MOLOT_ERR_TIMEOUT in the status word of
+ * the workspace it used and its outputs are garbage.  Nothing faults, traps
+ * or hangs.  wait_limit_ns = 0 cancels a pending request.  For tests of the
+ * status path (molot_kv_check, molot_paged_check, molot_device_status,
+ * molot_noalloc_status); never set in production. */
+int molot_debug_withhold_next(unsigned long long wait_limit_ns);
 
 /* ------------------------------------------------------------------------
  * attn.h drop-ins: host buffers, synchronous ("ready on return").
@@ -114,6 +127,14 @@ int molot_attn_decode_strided_noalloc(const float* Q, const float* K, const floa
                                       int nq, int nkv, int n, int d, long long stride_t,
                                       long long stride_h, float scale, int pos_cur, int window,
                                       void* stream);
+
+/* Status word of the no-alloc scratch on the current device: synchronises
+ * `stream`, returns MOLOT_OK, or MOLOT_ERR_TIMEOUT when a no-alloc decode
+ * gave up on a bounded wait since the word was last cleared (its outputs are
+ * then garbage); clears the word when `clear` != 0.  The word stays set
+ * until read with clear (no-alloc calls do not reset it).  Allocates
+ * nothing. */
+int molot_noalloc_status(void* stream, int clear);
 
 /* Replaces molot::attn_prefill_gqa (gemm.h:409-446) on host buffers: Qm, Om
  * [M][nq][d], K/V [N][nkv*d] (attn.h:122-124 layout); query m sits at
@@ -299,6 +320,60 @@ int molot_paged_append(molot_paged_plan* plan, const float* q, const float* k, c
 
 /* Synchronises and reports device-side timeouts of the plan's launches. */
 int molot_paged_check(molot_paged_plan* plan, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Peer gather for kv-head sharding over several GPUs (no counterpart in the
+ * reference, which runs on one CPU; it serves forward.h:589-600, where the
+ * attention of every head feeds the output projection).  One process per
+ * GPU of one node.  Rank r owns kv heads [r*nkv/N, (r+1)*nkv/N) and their
+ * grouped q heads, for every sequence.  Its paged decode writes each final
+ * output value straight into the gathered buffer of every rank over NVLink
+ * / NVSwitch (plain stores to peer memory mapped by CUDA IPC; no
+ * multicast), so the gather costs no separate collective and overlaps the
+ * attention itself.  Set-up:
+ *   molot_comm_create(N, r, bytes, &c);            every rank, its own GPU
+ *   molot_comm_handle(c, h[r]);                    64 bytes per rank
+ *   (exchange the N handles: MPI_Allgather, sockets, a torch store ...)
+ *   molot_comm_open(c, h);                         maps the peers' buffers
+ * Per layer: molot_paged_decode_gather(plan, c, ...) then, on the stream of
+ * whatever reads the gathered outputs, molot_comm_wait(c, stream).  Every
+ * rank makes the same sequence of decode_gather / wait calls on one comm
+ * (each wait matches the decode_gather of the same index).  An offset of the
+ * buffer may be rewritten once every rank has consumed it: alternating two
+ * offsets by layer parity is safe when each rank consumes layer l's outputs
+ * in stream order before its decode of layer l+1.
+ * ---------------------------------------------------------------------- */
+typedef struct molot_comm molot_comm;
+
+#define MOLOT_COMM_HANDLE_BYTES 64
+#define MOLOT_COMM_MAX_RANKS 8
+
+/* This rank's end of an nranks-way group on the current device, with a
+ * gathered-output buffer of buf_bytes (a multiple of 16) plus a small
+ * control block.  nranks 1..8; with nranks == 1 no open is needed. */
+int molot_comm_create(int nranks, int rank, size_t buf_bytes, molot_comm** out);
+/* The IPC handle of this rank's buffer (MOLOT_COMM_HANDLE_BYTES bytes). */
+int molot_comm_handle(const molot_comm* c, void* handle);
+/* Maps every peer's buffer: `handles` holds nranks handles in rank order
+ * (this rank's own entry is ignored). */
+int molot_comm_open(molot_comm* c, const void* handles);
+/* Device address of this rank's gathered buffer (floats). */
+int molot_comm_buffer(const molot_comm* c, float** buf);
+/* molot_paged_decode whose outputs land in every rank's gathered buffer at
+ * float offset out_offset, laid out [B][nranks*nq][d] with this rank's nq
+ * heads (the plan's) at [rank*nq, (rank+1)*nq).  Every sequence of the plan
+ * must attend at least one slot.  Q [B][nq][d] as for molot_paged_decode. */
+int molot_paged_decode_gather(molot_paged_plan* plan, molot_comm* c, const float* Q,
+                              size_t out_offset, const float* k_pool, const float* v_pool,
+                              const int* block_table, int max_pages, int page_size, float scale,
+                              void* stream);
+/* Stream-ordered: work after it on `stream` sees every rank's outputs of
+ * the matching molot_paged_decode_gather.  The wait is bounded (5 s); one
+ * that gives up records MOLOT_ERR_TIMEOUT for molot_comm_check. */
+int molot_comm_wait(molot_comm* c, void* stream);
+/* Synchronises `stream` and reports (then clears) a wait that gave up. */
+int molot_comm_check(molot_comm* c, void* stream);
+void molot_comm_destroy(molot_comm* c);
 
 /* ------------------------------------------------------------------------
  * Continuous-batching page manager: page ids, per-sequence page lists and

@@ -229,8 +229,51 @@ class PagedPlan {
   // Synchronise and surface device-side wait timeouts.
   void sync(void* stream = nullptr) { check(molot_paged_check(h_, stream)); }
 
+  molot_paged_plan* handle() const { return h_; }
+
  private:
   molot_paged_plan* h_ = nullptr;
+};
+
+// Peer-gather group for kv-head sharding over the GPUs of one node
+// (molot_comm_*): construct on every rank, exchange handle() bytes with the
+// job's own transport (MPI_Allgather, a socket, ...), then open().  Each
+// rank's decode_gather writes its heads' outputs into every rank's
+// gathered buffer; wait() orders later work on a stream after all of them.
+class PeerGather {
+ public:
+  PeerGather(int nranks, int rank, size_t buf_bytes) {
+    check(molot_comm_create(nranks, rank, buf_bytes, &h_));
+  }
+  ~PeerGather() { molot_comm_destroy(h_); }
+  PeerGather(const PeerGather&) = delete;
+  PeerGather& operator=(const PeerGather&) = delete;
+
+  // MOLOT_COMM_HANDLE_BYTES bytes for the other ranks.
+  void handle(void* out) const { check(molot_comm_handle(h_, out)); }
+  // nranks handles in rank order.
+  void open(const void* handles) { check(molot_comm_open(h_, handles)); }
+  // This rank's gathered buffer (device floats).
+  float* buffer() const {
+    float* p = nullptr;
+    check(molot_comm_buffer(h_, &p));
+    return p;
+  }
+  // Paged decode of this rank's kv heads, outputs into every rank's buffer
+  // at float offset out_offset ([B][nranks*nq][d], this rank's heads at
+  // [rank*nq, (rank+1)*nq)).
+  void decode_gather(PagedPlan& plan, const float* Q, size_t out_offset, const float* k_pool,
+                     const float* v_pool, const int* block_table, int max_pages, int page_size,
+                     float scale, void* stream = nullptr) {
+    check(molot_paged_decode_gather(plan.handle(), h_, Q, out_offset, k_pool, v_pool, block_table,
+                                    max_pages, page_size, scale, stream));
+  }
+  void wait(void* stream = nullptr) { check(molot_comm_wait(h_, stream)); }
+  // Synchronise and surface a wait for a peer that gave up.
+  void sync(void* stream = nullptr) { check(molot_comm_check(h_, stream)); }
+
+ private:
+  molot_comm* h_ = nullptr;
 };
 
 }  // namespace molot_b200

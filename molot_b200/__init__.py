@@ -13,7 +13,9 @@ and error behaviour mirror the reference's functions
   ``decode_strided``, ``norm_rope_append``;
 * ``KVCache`` (forward.h's per-layer KVC, HBM-resident) with
   ``append_rope`` / ``decode``;
-* ``PagedPlan`` for batched decode over 16-token pages.
+* ``PagedPlan`` for batched decode over 16-token pages;
+* ``Comm``, the peer-gather group of kv-head-sharded decode over several
+  GPUs (``PagedPlan.decode_gather``).
 
 torch is used only to hold device memory and streams.  There is no CPU
 fallback: importing this package fails loudly when the library is missing.
@@ -142,6 +144,20 @@ _decl("molot_paged_plan_build", [_p, _i, _i, _i, _i, _p, _p, _i, _p])
 _decl("molot_paged_decode", [_p, _p, _p, _p, _p, _p, _i, _i, _f, _p])
 _decl("molot_paged_append", [_p, _p, _p, _p, _p, _p, _p, _i, _f, _p, _p, _p, _p, _i, _i, _p])
 _decl("molot_paged_check", [_p, _p])
+_decl("molot_debug_withhold_next", [ctypes.c_ulonglong])
+_decl("molot_noalloc_status", [_p, _i])
+_decl("molot_comm_create", [_i, _i, ctypes.c_size_t, _pp])
+_decl("molot_comm_handle", [_p, _p])
+_decl("molot_comm_open", [_p, _p])
+_decl("molot_comm_buffer", [_p, _pp])
+_decl("molot_comm_wait", [_p, _p])
+_decl("molot_comm_check", [_p, _p])
+_decl("molot_comm_destroy", [_p], None)
+_decl("molot_paged_decode_gather",
+      [_p, _p, _p, ctypes.c_size_t, _p, _p, _p, _i, _i, _f, _p])
+
+COMM_HANDLE_BYTES = 64
+COMM_MAX_RANKS = 8
 
 
 def library():
@@ -318,8 +334,22 @@ def rope_inv_freq(base, d) -> np.ndarray:
 
 
 def device_status(clear: bool = True) -> int:
-    """Device-side status of the default workspace (0 or ERR_TIMEOUT)."""
+    """Device-side status of the current device's default workspace and of
+    its no-alloc scratch (0 or ERR_TIMEOUT)."""
     return _lib.molot_device_status(1 if clear else 0)
+
+
+def noalloc_status(stream=None, clear: bool = True) -> int:
+    """Status word of the no-alloc scratch (molot_noalloc_status): 0, or
+    ERR_TIMEOUT when a no-alloc decode gave up on a bounded wait."""
+    return _lib.molot_noalloc_status(_stream_ptr(stream), 1 if clear else 0)
+
+
+def debug_withhold_next(wait_limit_ns: int) -> None:
+    """Failure-detection test hook (molot_debug_withhold_next): the calling
+    thread's next decode launch withholds its copies so its first bounded
+    wait runs out after wait_limit_ns; 0 cancels."""
+    check(_lib.molot_debug_withhold_next(int(wait_limit_ns)))
 
 
 # ------------------------------------------------------------------ device forms
@@ -571,5 +601,75 @@ class PagedPlan:
                                       _ptr(k_pool), _ptr(v_pool), _ptr(block_table),
                                       block_table.shape[1], page_size, _stream_ptr(stream)))
 
+    def decode_gather(self, comm, Q, out_offset, k_pool, v_pool, block_table, page_size, scale,
+                      stream=None) -> None:
+        """molot_paged_decode_gather: outputs into every rank's gathered
+        buffer of `comm` at float offset out_offset ([B][nranks*nq][d])."""
+        check(_lib.molot_paged_decode_gather(self._h, comm.handle, _ptr(Q), int(out_offset),
+                                             _ptr(k_pool), _ptr(v_pool), _ptr(block_table),
+                                             block_table.shape[1], page_size, scale,
+                                             _stream_ptr(stream)))
+
     def check(self, stream=None) -> None:
         check(_lib.molot_paged_check(self._h, _stream_ptr(stream)))
+
+
+class Comm:
+    """Peer-gather group for kv-head sharding (molot_comm_*): one process per
+    GPU; every rank's gathering decode writes its heads' outputs straight
+    into every rank's buffer over NVLink.  The caller exchanges the 64-byte
+    handles (`handle()`) between ranks and passes all of them to `open()`."""
+
+    def __init__(self, nranks: int, rank: int, buf_bytes: int):
+        h = ctypes.c_void_p()
+        check(_lib.molot_comm_create(nranks, rank, buf_bytes, ctypes.byref(h)))
+        self._h = h
+        self.nranks, self.rank, self.buf_bytes = nranks, rank, buf_bytes
+
+    @property
+    def handle(self):
+        return self._h
+
+    def ipc_handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(COMM_HANDLE_BYTES)
+        check(_lib.molot_comm_handle(self._h, buf))
+        return buf.raw
+
+    def open(self, handles) -> None:
+        """handles: the nranks byte strings of ipc_handle(), in rank order."""
+        if len(handles) != self.nranks:
+            raise ValueError("one handle per rank")
+        blob = b"".join(bytes(x) for x in handles)
+        if len(blob) != COMM_HANDLE_BYTES * self.nranks:
+            raise ValueError("bad handle size")
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        check(_lib.molot_comm_open(self._h, buf))
+
+    def buffer(self, shape, offset: int = 0):
+        """torch float32 view of the gathered buffer from float `offset`."""
+        import torch
+        p = ctypes.c_void_p()
+        check(_lib.molot_comm_buffer(self._h, ctypes.byref(p)))
+        n = 1
+        for x in shape:
+            n *= int(x)
+        if (offset + n) * 4 > self.buf_bytes:
+            raise ValueError("view outside the comm buffer")
+        return torch.as_tensor(_CudaArray(p.value + 4 * offset, tuple(shape)), device="cuda")
+
+    def wait(self, stream=None) -> None:
+        check(_lib.molot_comm_wait(self._h, _stream_ptr(stream)))
+
+    def check(self, stream=None) -> None:
+        check(_lib.molot_comm_check(self._h, _stream_ptr(stream)))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.molot_comm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -8,6 +8,7 @@ the CUDA runtime statically, so it needs only the driver at run time.
 from __future__ import annotations
 
 import argparse
+import concurrent.futures
 import glob
 import os
 import shutil
@@ -55,7 +56,7 @@ def build(force: bool = False, ptxas_verbose: bool = False, quiet: bool = False)
         return LIB
     objdir = os.path.join(PKG, "_build")
     os.makedirs(objdir, exist_ok=True)
-    objs = []
+    objs, cmds = [], []
     for src in sources():
         obj = os.path.join(objdir, os.path.basename(src) + ".o")
         cmd = [nvcc(), *ARCH_FLAGS, *NVCC_FLAGS, "-I", INCLUDE, "-c", src, "-o", obj]
@@ -63,8 +64,12 @@ def build(force: bool = False, ptxas_verbose: bool = False, quiet: bool = False)
             cmd += ["-Xptxas", "-v"]
         if not quiet:
             print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
+        cmds.append(cmd)
         objs.append(obj)
+    # translation units compile independently: run them side by side
+    with concurrent.futures.ThreadPoolExecutor(max_workers=os.cpu_count() or 1) as ex:
+        for f in [ex.submit(subprocess.run, c, check=True) for c in cmds]:
+            f.result()
     tmp = LIB + ".tmp"
     cmd = [nvcc(), *ARCH_FLAGS, "-shared", "-o", tmp, *objs, "-lpthread"]
     if not quiet:

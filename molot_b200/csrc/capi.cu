@@ -12,12 +12,20 @@
 #include <vector>
 
 #include "append.cuh"
+#include "comm.cuh"
 #include "decode.cuh"
+#include "dispatch.cuh"
 #include "gemv.cuh"
 #include "molot_b200.h"
 #include "prefill.cuh"
 
 namespace molot {
+
+void take_withhold(DecodeArgs& a);
+// No-alloc scratch status of device `dev` (noalloc.cu): MOLOT_OK when it was
+// never set up there.
+int noalloc_status_check(int dev, cudaStream_t st, bool clear);
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -154,91 +162,16 @@ struct Workspace {
 
 // ------------------------------------------------------------- dispatch
 
-struct KernelRef {
-  const void* fn = nullptr;
-  int smem = 0;
-};
-
-template <int D, int GS, int HS, class KT = float, bool SPLIT = false>
-KernelRef decode_ref() {
-  return {reinterpret_cast<const void*>(&gqa_decode_kernel<D, GS, HS, KT, SPLIT>),
-          DecodeSmem<D, GS, KT>::kTotal};
-}
-
-// Kernel of a head_dim / group size, for every cache storage type (the
-// same group splits throughout).
-template <class KT>
-bool pick_decode_t(int D, int G, KernelRef* k) {
-  switch (D) {
-    case 64:
-      switch (G) {
-        case 1: *k = decode_ref<64, 1, 1, KT>(); return true;
-        case 2: *k = decode_ref<64, 2, 1, KT>(); return true;
-        case 4: *k = decode_ref<64, 4, 1, KT>(); return true;
-        case 8: *k = decode_ref<64, 8, 1, KT>(); return true;
-        case 16: *k = decode_ref<64, 8, 2, KT>(); return true;
-        case 32: *k = decode_ref<64, 8, 4, KT>(); return true;
-      }
-      return false;
-    case 128:
-      switch (G) {
-        case 1: *k = decode_ref<128, 1, 1, KT>(); return true;
-        case 2: *k = decode_ref<128, 2, 1, KT>(); return true;
-        case 4: *k = decode_ref<128, 4, 1, KT>(); return true;
-        case 8: *k = decode_ref<128, 4, 2, KT>(); return true;
-        case 16: *k = decode_ref<128, 4, 4, KT>(); return true;
-        case 32: *k = decode_ref<128, 4, 8, KT>(); return true;
-      }
-      return false;
-    case 256:
-      switch (G) {
-        case 1: *k = decode_ref<256, 1, 1, KT>(); return true;
-        case 2: *k = decode_ref<256, 2, 1, KT>(); return true;
-        case 4: *k = decode_ref<256, 2, 2, KT>(); return true;
-        case 8: *k = decode_ref<256, 2, 4, KT>(); return true;
-        case 16: *k = decode_ref<256, 2, 8, KT>(); return true;
-      }
-      return false;
-  }
-  return false;
-}
-
-bool pick_decode(int D, int G, KernelRef* k) { return pick_decode_t<float>(D, G, k); }
-
 // FP32 kernels with split K/V stage barriers (hd <= 128; see gqa_decode_kernel).
-bool pick_decode_split(int D, int G, KernelRef* k) {
-  switch (D) {
-    case 64:
-      switch (G) {
-        case 1: *k = decode_ref<64, 1, 1, float, true>(); return true;
-        case 2: *k = decode_ref<64, 2, 1, float, true>(); return true;
-        case 4: *k = decode_ref<64, 4, 1, float, true>(); return true;
-        case 8: *k = decode_ref<64, 8, 1, float, true>(); return true;
-        case 16: *k = decode_ref<64, 8, 2, float, true>(); return true;
-        case 32: *k = decode_ref<64, 8, 4, float, true>(); return true;
-      }
-      return false;
-    case 128:
-      switch (G) {
-        case 1: *k = decode_ref<128, 1, 1, float, true>(); return true;
-        case 2: *k = decode_ref<128, 2, 1, float, true>(); return true;
-        case 4: *k = decode_ref<128, 4, 1, float, true>(); return true;
-        case 8: *k = decode_ref<128, 4, 2, float, true>(); return true;
-        case 16: *k = decode_ref<128, 4, 4, float, true>(); return true;
-        case 32: *k = decode_ref<128, 4, 8, float, true>(); return true;
-      }
-      return false;
-  }
-  return false;
-}
+bool pick_decode_split(int D, int G, KernelRef* k) { return pick_decode_f32(D, G, true, k); }
 
 // kvt: the cache's molot_kv_dtype.
 bool pick_decode_kv(int D, int G, int kvt, KernelRef* k) {
   switch (kvt) {
-    case MOLOT_KV_BF16: return pick_decode_t<__nv_bfloat16>(D, G, k);
-    case MOLOT_KV_Q8: return pick_decode_t<Q8Row>(D, G, k);
+    case MOLOT_KV_BF16: return pick_decode_bf16(D, G, k);
+    case MOLOT_KV_Q8: return pick_decode_q8(D, G, k);
   }
-  return pick_decode_t<float>(D, G, k);
+  return pick_decode_f32(D, G, false, k);
 }
 
 template <class CT>
@@ -308,6 +241,7 @@ int check_shape(int nq, int nkv, int d, KernelRef* k, int kvt = MOLOT_KV_F32) {
 
 // One decode grid; split segments are merged inside it by their last CTA.
 int launch_decode(const KernelRef& k, DecodeArgs& a, cudaStream_t st) {
+  take_withhold(a);
   return launch(k.fn, dim3(a.grid), dim3(kDecodeThreads), k.smem, st, &a);
 }
 
@@ -484,29 +418,8 @@ int host_decode(const float* Q, const float* K, const float* V, float* O, int nq
 
 // ------------------------------------------------------------- prefill
 
-template <int D, class KT>
-KernelRef prefill_ref() {
-  return {reinterpret_cast<const void*>(&gqa_prefill_kernel<D, KT>), PrefillTile<D, KT>::kTotal};
-}
-
-template <class KT>
-bool pick_prefill_t(int D, KernelRef* k) {
-  switch (D) {
-    case 64: *k = prefill_ref<64, KT>(); return true;
-    case 128: *k = prefill_ref<128, KT>(); return true;
-    case 256: *k = prefill_ref<256, KT>(); return true;
-  }
-  return false;
-}
-
 // kvt: the cache's molot_kv_dtype.
-bool pick_prefill(int D, KernelRef* k, int kvt = MOLOT_KV_F32) {
-  switch (kvt) {
-    case MOLOT_KV_BF16: return pick_prefill_t<__nv_bfloat16>(D, k);
-    case MOLOT_KV_Q8: return pick_prefill_t<Q8Row>(D, k);
-  }
-  return pick_prefill_t<float>(D, k);
-}
+bool pick_prefill(int D, KernelRef* k, int kvt = MOLOT_KV_F32) { return pick_prefill_kv(D, kvt, k); }
 
 // gemm.h:409-446 on device buffers: Q/O [M][nq][d] (token stride q_tstride /
 // o_tstride floats), slot t of kv head g at K + t*stride_t + g*stride_h.
@@ -621,6 +534,16 @@ int gemv_q4_launch(const float* scales, const int8_t* zeros, const uint8_t* data
 // molot_last_error().
 int set_last_error(int code, const char* msg) { return fail(code, msg); }
 
+// molot_debug_withhold_next: pending request of the calling host thread.
+thread_local unsigned long long g_withhold_ns = 0;
+
+void take_withhold(DecodeArgs& a) {
+  if (!g_withhold_ns) return;
+  a.withhold = 1;
+  a.timeout_ns = g_withhold_ns;
+  g_withhold_ns = 0;
+}
+
 }  // namespace molot
 
 using namespace molot;
@@ -718,7 +641,14 @@ int molot_device_status(int clear) {
   std::lock_guard<std::mutex> lk(c.mu);
   if ((rc = c.init(dev))) return rc;
   MOLOT_CUDA(cudaDeviceSynchronize());
-  return c.ws.check(c.stream, clear != 0);
+  const int a = c.ws.check(c.stream, clear != 0);
+  const int b = noalloc_status_check(dev, c.stream, clear != 0);
+  return a ? a : b;
+}
+
+int molot_debug_withhold_next(unsigned long long wait_limit_ns) {
+  g_withhold_ns = wait_limit_ns;
+  return MOLOT_OK;
 }
 
 // ---------------------------------------------------------------- drop-ins
@@ -1300,11 +1230,18 @@ int molot_paged_plan_build(molot_paged_plan* p, int B, int nq, int nkv, int d,
   return MOLOT_OK;
 }
 
-int molot_paged_decode(molot_paged_plan* p, const float* Q, float* O, const float* k_pool,
-                       const float* v_pool, const int* block_table, int max_pages,
-                       int page_size, float scale, void* stream) {
+}  // extern "C"
+
+namespace molot {
+namespace {
+// molot_paged_decode, or with a comm its gathering form: outputs into every
+// rank's gathered buffer at float offset out_offset ([B][nranks*nq][d]).
+int paged_decode_impl(molot_paged_plan* p, const float* Q, float* O, const float* k_pool,
+                      const float* v_pool, const int* block_table, int max_pages, int page_size,
+                      float scale, cudaStream_t st, molot_comm* c, size_t out_offset) {
   if (!p || !p->built) return fail(MOLOT_ERR_INVALID, "plan not built");
-  if (!Q || !O || !k_pool || !v_pool || !block_table) return fail(MOLOT_ERR_INVALID, "null pointer");
+  if (!Q || (!O && !c) || !k_pool || !v_pool || !block_table)
+    return fail(MOLOT_ERR_INVALID, "null pointer");
   if (page_size <= 0 || page_size % kBlk) return fail(MOLOT_ERR_INVALID, "page_size must be a multiple of 16");
   if (!aligned16(k_pool) || !aligned16(v_pool)) return fail(MOLOT_ERR_INVALID, "pools must be 16-byte aligned");
   int dev, rc;
@@ -1312,22 +1249,39 @@ int molot_paged_decode(molot_paged_plan* p, const float* Q, float* O, const floa
   if (dev != p->device) return fail(MOLOT_ERR_INVALID, "plan used on another device");
   KernelRef k;
   if ((rc = check_shape(p->nq, p->nkv, p->d, &k, p->kvt))) return rc;
-  cudaStream_t st = (cudaStream_t)stream;
-  // Sequences with an empty attended range produce zeros (attn.h:163).
-  bool any_empty = false;
-  for (int b = 0; b < p->B; ++b) any_empty |= p->h_n[b] <= p->h_t0[b];
-  if (any_empty) {
+  DecodeArgs a = {};
+  a.o_bstride = (long long)p->nq * p->d;
+  if (c) {
+    if (!c->opened) return fail(MOLOT_ERR_INVALID, "comm not opened");
+    if (c->device != dev) return fail(MOLOT_ERR_INVALID, "comm used on another device");
+    const size_t row = (size_t)c->nranks * p->nq * p->d;  // floats per sequence
+    if (out_offset % 4 || (out_offset + (size_t)p->B * row) * sizeof(float) > c->data_bytes)
+      return fail(MOLOT_ERR_INVALID, "gathered outputs outside the comm buffer (or offset not a "
+                                     "multiple of 4 floats)");
+    for (int b = 0; b < p->B; ++b)
+      if (p->h_n[b] <= p->h_t0[b])
+        return fail(MOLOT_ERR_INVALID, "peer gather needs every sequence to attend >= 1 slot");
+    a.npeer = c->nranks;
+    for (int r = 0; r < c->nranks; ++r) {
+      a.peer_O[r] = reinterpret_cast<float*>(c->peer_base[r]) + out_offset +
+                    (size_t)c->rank * p->nq * p->d;
+      a.peer_flag[r] = &c->ctl(r)->flags[c->rank];
+    }
+    a.done_ctr = &c->own_ctl()->done;
+    a.epoch = &c->own_ctl()->epoch;
+    O = a.peer_O[c->rank];
+    a.o_bstride = (long long)row;
+  } else {
+    // Sequences with an empty attended range produce zeros (attn.h:163).
     for (int b = 0; b < p->B; ++b)
       if (p->h_n[b] <= p->h_t0[b])
         MOLOT_CUDA(cudaMemsetAsync(O + (size_t)b * p->nq * p->d, 0, sizeof(float) * p->nq * p->d, st));
+    if (p->all_empty) return MOLOT_OK;
   }
-  if (p->all_empty) return MOLOT_OK;
   if ((rc = prepare_kernel(k, dev))) return rc;
-  DecodeArgs a = {};
   a.Q = Q;
   a.q_bstride = (long long)p->nq * p->d;
   a.O = O;
-  a.o_bstride = (long long)p->nq * p->d;
   a.K = k_pool;
   a.V = v_pool;
   a.block_table = block_table;
@@ -1356,6 +1310,26 @@ int molot_paged_decode(molot_paged_plan* p, const float* Q, float* O, const floa
   a.prefetch_old_rows = (p->appended_pool == k_pool) ? 1 : 0;
   p->appended_pool = nullptr;
   return launch_decode(k, a, st);
+}
+}  // namespace
+}  // namespace molot
+
+extern "C" {
+
+int molot_paged_decode(molot_paged_plan* p, const float* Q, float* O, const float* k_pool,
+                       const float* v_pool, const int* block_table, int max_pages,
+                       int page_size, float scale, void* stream) {
+  return paged_decode_impl(p, Q, O, k_pool, v_pool, block_table, max_pages, page_size, scale,
+                           (cudaStream_t)stream, nullptr, 0);
+}
+
+int molot_paged_decode_gather(molot_paged_plan* p, molot_comm* c, const float* Q,
+                              size_t out_offset, const float* k_pool, const float* v_pool,
+                              const int* block_table, int max_pages, int page_size, float scale,
+                              void* stream) {
+  if (!c) return fail(MOLOT_ERR_INVALID, "null comm");
+  return paged_decode_impl(p, Q, nullptr, k_pool, v_pool, block_table, max_pages, page_size,
+                           scale, (cudaStream_t)stream, c, out_offset);
 }
 
 int molot_paged_append(molot_paged_plan* p, const float* q, const float* k, const float* v,

@@ -188,6 +188,15 @@ __device__ __forceinline__ float q_sumsq(const float (&x)[D / 8], int l8) {
 // Status codes written into the device status word.
 constexpr int kDevErrConsumerTimeout = 1;
 constexpr int kDevErrProducerTimeout = 2;
+constexpr int kDevErrPeerTimeout = 3;
+
+// Ranks of a peer-gather group (one GPU each, NVLink / NVSwitch).
+constexpr int kMaxPeers = 8;
+// Bound of the producer's final wait for its own copies in flight.  It is
+// fixed, whatever the stage-wait bound of the launch: a CTA must never exit
+// while a bulk copy into its shared memory is still landing, and copies
+// from valid addresses always complete.
+constexpr unsigned long long kDrainLimitNs = 2000000000ull;
 
 struct DecodeArgs {
   // Query / output: head h of sequence b at Q + b*q_bstride + h*D.
@@ -256,8 +265,33 @@ struct DecodeArgs {
   float* partials;  // [2*grid][partial_record_floats(G, D)]
   int* counters;    // [S] per-segment tickets, zero between launches
   int* status;
+  // Bound of every wait for a stage (producer and consumers).
   unsigned long long timeout_ns;
+  // Failure-detection test hook (molot_debug_withhold_next): the producer
+  // issues no copy and exits, so the consumers' first wait runs out after
+  // timeout_ns with nothing in flight.  0 in every normal launch.
+  int withhold;
+  // Peer gather (molot_paged_decode_gather): when npeer > 0 every final
+  // output value goes to all npeer ranks' gathered buffers, peer_O[p] being
+  // rank p's copy of what O addresses here (O == peer_O[own rank]).  After
+  // its last store the grid's last CTA raises this rank's epoch flag in
+  // every rank's buffer (peer_flag[p]); molot_comm_wait waits for them.
+  int npeer;
+  float* peer_O[kMaxPeers];
+  unsigned long long* peer_flag[kMaxPeers];
+  unsigned int* done_ctr;      // CTAs finished, zero between launches
+  unsigned long long* epoch;   // this rank's launches so far
 };
+
+// Final output value: into O, or into every rank's gathered buffer.
+__device__ __forceinline__ void put_out(const DecodeArgs& a, float* dst, float v) {
+  if (a.npeer == 0) {
+    *dst = v;
+    return;
+  }
+  const long long off = dst - a.O;
+  for (int p = 0; p < a.npeer; ++p) a.peer_O[p][off] = v;
+}
 
 template <int D, class KT = float>
 struct TileShape {
@@ -735,10 +769,10 @@ __device__ __forceinline__ void combine_segment(const DecodeArgs& a, int s, cons
     }
     if (csplit == 1) {
       float* dst = out_seg + chunk * 4;
-      dst[0] = acc.x / L;
-      dst[1] = acc.y / L;
-      dst[2] = acc.z / L;
-      dst[3] = acc.w / L;
+      put_out(a, dst + 0, acc.x / L);
+      put_out(a, dst + 1, acc.y / L);
+      put_out(a, dst + 2, acc.z / L);
+      put_out(a, dst + 3, acc.w / L);
     } else {
       // csplit > 1 implies nchunk * csplit <= 256: the task fits `red`.
       float* r = red + (size_t)task * 6;
@@ -766,10 +800,10 @@ __device__ __forceinline__ void combine_segment(const DecodeArgs& a, int s, cons
       acc.w += r[5] * f;
     }
     float* dst = out_seg + chunk * 4;
-    dst[0] = acc.x / L;
-    dst[1] = acc.y / L;
-    dst[2] = acc.z / L;
-    dst[3] = acc.w / L;
+    put_out(a, dst + 0, acc.x / L);
+    put_out(a, dst + 1, acc.y / L);
+    put_out(a, dst + 2, acc.z / L);
+    put_out(a, dst + 3, acc.w / L);
   }
 }
 
@@ -846,7 +880,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   if (warp >= kConsumerWarps) {
     // ------------------------------------------------------------ producer
     ptx::setmaxnreg_dec<kProducerRegs>();
-    if (warp != kConsumerWarps) return;
+    if (warp != kConsumerWarps || a.withhold) return;
     const uint64_t pol = ptx::policy_evict_first();
     const bool rows_contig = (a.block_table != nullptr) || (a.stride_t * EB == TS::RB);
     bool waited = false;  // griddepcontrol.wait done by this warp
@@ -954,7 +988,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       for (int j = first; j < it && ok; ++j) {
         for (int kv = 0; kv < (split ? 2 : 1) && ok; ++kv) {
           if (!ptx::mbar_wait_bounded(full_bar + 2 * (j % STAGES) + kv, (j / STAGES) & 1,
-                                      a.timeout_ns)) {
+                                      kDrainLimitNs)) {
             raise_status(a, abort_flag, kDevErrProducerTimeout);
             ok = false;
           }
@@ -1185,7 +1219,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
           acc += merge_o[((size_t)ww * GS + hh) * D + j] * f;
         }
         if (whole) {
-          out_seg[idx] = acc / L;
+          put_out(a, out_seg + idx, acc / L);
         } else {
           part[idx] = acc;
           if (j == 0) {
@@ -1213,6 +1247,24 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     }
     pos = pend > pos ? pend : pos;
     ++s;
+  }
+  if (a.npeer > 0) {
+    // Peer gather: once every CTA's output stores are issued, the last CTA
+    // to finish publishes this launch's epoch in every rank's buffer.  The
+    // system-scope fences order the CTAs' stores to peer memory before the
+    // count and the count before the flags.
+    ptx::named_bar_sync(1, kConsumerWarps * 32);
+    if (ctid == 0) {
+      __threadfence_system();
+      const unsigned int t = atomicAdd(a.done_ctr, 1u);
+      if (t == (unsigned int)a.grid - 1) {
+        __threadfence_system();
+        *a.done_ctr = 0;
+        const unsigned long long e = *a.epoch + 1;
+        *a.epoch = e;
+        for (int p = 0; p < a.npeer; ++p) ptx::st_release_sys(a.peer_flag[p], e);
+      }
+    }
   }
 }
 

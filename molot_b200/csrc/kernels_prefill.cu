@@ -1,0 +1,32 @@
+// Prefill attention kernels for every storage type.
+#include "dispatch.cuh"
+#include "molot_b200.h"
+#include "prefill.cuh"
+
+namespace molot {
+namespace {
+template <int D, class KT>
+KernelRef ref() {
+  return {reinterpret_cast<const void*>(&gqa_prefill_kernel<D, KT>), PrefillTile<D, KT>::kTotal};
+}
+
+template <class KT>
+bool pick(int D, KernelRef* k) {
+  switch (D) {
+    case 64: *k = ref<64, KT>(); return true;
+    case 128: *k = ref<128, KT>(); return true;
+    case 256: *k = ref<256, KT>(); return true;
+  }
+  return false;
+}
+}  // namespace
+
+bool pick_prefill_kv(int D, int kvt, KernelRef* k) {
+  switch (kvt) {
+    case MOLOT_KV_BF16: return pick<__nv_bfloat16>(D, k);
+    case MOLOT_KV_Q8: return pick<Q8Row>(D, k);
+  }
+  return pick<float>(D, k);
+}
+
+}  // namespace molot

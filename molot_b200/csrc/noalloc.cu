@@ -16,11 +16,16 @@
 // Larger requests are rejected with MOLOT_ERR_UNSUPPORTED.
 //
 // All calls share the one array, and it keeps what the last call left in it:
-// each call clears the tickets and the status word (cudaMemsetAsync on the
-// array, which allocates nothing) before its launch; the partial records are
-// always written before they are read.  Calls whose work
-// overlaps on the GPU -- different streams, or different host threads
-// without ordering -- race on the array; order them on one stream.
+// each call clears the tickets (cudaMemsetAsync on the array, which
+// allocates nothing) before its launch; the partial records are always
+// written before they are read.  The status word is not cleared by a call:
+// a call that gave up on a bounded wait leaves MOLOT_ERR_TIMEOUT there until
+// molot_noalloc_status (or molot_device_status) reads and clears it.  Calls
+// whose work overlaps on the GPU -- different streams, or different host
+// threads without ordering -- race on the array; order them on one stream.
+//
+// The partition of the work and the kernel variant are those of
+// molot_attn_decode_strided_dev, so both give bit-identical outputs.
 //
 // Set-up: on the first call on a device, with that device current, the
 // array's device address is fetched once with cudaGetSymbolAddress (the
@@ -32,11 +37,13 @@
 #include <string>
 
 #include "decode.cuh"
+#include "dispatch.cuh"
 #include "molot_b200.h"
 
 namespace molot {
 
 int set_last_error(int code, const char* msg);
+void take_withhold(DecodeArgs& a);
 
 namespace {
 
@@ -73,51 +80,50 @@ int scratch_for(int dev, unsigned char** out) {
   return MOLOT_OK;
 }
 
-struct Kernel {
-  const void* fn;
-  int smem;
-};
-
-template <int D, int GS, int HS>
-Kernel kernel_of() {
-  return {reinterpret_cast<const void*>(&gqa_decode_kernel<D, GS, HS>), DecodeSmem<D, GS>::kTotal};
+// The FP32 decode kernels of molot_attn_decode_strided_dev, within the
+// no-alloc limits (group <= 8).  split: the split K/V stage-barrier form.
+bool pick(int d, int g, bool split, KernelRef* k) {
+  return g <= 8 && pick_decode_f32(d, g, split, k);
 }
-
-bool pick(int d, int g, Kernel* k) {
-  switch (d) {
-    case 64:
-      switch (g) {
-        case 1: *k = kernel_of<64, 1, 1>(); return true;
-        case 2: *k = kernel_of<64, 2, 1>(); return true;
-        case 4: *k = kernel_of<64, 4, 1>(); return true;
-        case 8: *k = kernel_of<64, 8, 1>(); return true;
-      }
-      return false;
-    case 128:
-      switch (g) {
-        case 1: *k = kernel_of<128, 1, 1>(); return true;
-        case 2: *k = kernel_of<128, 2, 1>(); return true;
-        case 4: *k = kernel_of<128, 4, 1>(); return true;
-        case 8: *k = kernel_of<128, 4, 2>(); return true;
-      }
-      return false;
-    case 256:
-      switch (g) {
-        case 1: *k = kernel_of<256, 1, 1>(); return true;
-        case 2: *k = kernel_of<256, 2, 1>(); return true;
-        case 4: *k = kernel_of<256, 2, 2>(); return true;
-      }
-      return false;
-  }
-  return false;
-}
-
 
 int cuda_err(cudaError_t e, const char* what) {
   return set_last_error(MOLOT_ERR_CUDA, (std::string(what) + ": " + cudaGetErrorString(e)).c_str());
 }
 
+int* status_word(unsigned char* scratch) {
+  return reinterpret_cast<int*>(scratch + kNoAllocPartialBytes + kNoAllocCounterBytes);
+}
+
+// Reads the status word on `st` into the host (no allocation: a pageable
+// destination goes through the driver's own staging), clears it on request.
+int read_status(unsigned char* scratch, cudaStream_t st, bool clear) {
+  int h = 0;
+  cudaError_t e = cudaMemcpyAsync(&h, status_word(scratch), sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_err(e, "reading the no-alloc status word");
+  if (h == 0) return MOLOT_OK;
+  if (clear) {
+    e = cudaMemsetAsync(status_word(scratch), 0, sizeof(int), st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_err(e, "clearing the no-alloc status word");
+  }
+  return set_last_error(MOLOT_ERR_TIMEOUT, h == kDevErrConsumerTimeout
+                                               ? "no-alloc decode: wait for a KV tile timed out"
+                                               : "no-alloc decode: wait for a free stage timed out");
+}
+
 }  // namespace
+
+int noalloc_status_check(int dev, cudaStream_t st, bool clear) {
+  unsigned char* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (dev < 0 || dev >= kMaxDevices || !g_scratch_addr[dev]) return MOLOT_OK;
+    scratch = static_cast<unsigned char*>(g_scratch_addr[dev]);
+  }
+  return read_status(scratch, st, clear);
+}
+
 }  // namespace molot
 
 using namespace molot;
@@ -131,8 +137,8 @@ extern "C" int molot_attn_decode_strided_noalloc(const float* Q, const float* K,
   if (nq <= 0 || nkv <= 0 || d <= 0 || n < 0 || nq % nkv)
     return set_last_error(MOLOT_ERR_INVALID, "bad sizes (nq must be a positive multiple of nkv)");
   const int G = nq / nkv;
-  Kernel k;
-  if (nkv > kNoAllocMaxSegments || G * d > kNoAllocMaxGroupDim || !pick(d, G, &k))
+  KernelRef k;
+  if (nkv > kNoAllocMaxSegments || G * d > kNoAllocMaxGroupDim || !pick(d, G, false, &k))
     return set_last_error(MOLOT_ERR_UNSUPPORTED,
                           "no-alloc decode supports head_dim 64/128/256, group 1/2/4/8 with "
                           "group*head_dim <= 1024 and nkv <= 256");
@@ -165,11 +171,22 @@ extern "C" int molot_attn_decode_strided_noalloc(const float* Q, const float* K,
 
   float* partials = reinterpret_cast<float*>(scratch);
   int* counters = reinterpret_cast<int*>(scratch + kNoAllocPartialBytes);
-  int* status = reinterpret_cast<int*>(scratch + kNoAllocPartialBytes + kNoAllocCounterBytes);
-  // Tickets and status must start at zero; a previous call may have left
-  // them otherwise if it gave up on a wait.
-  e = cudaMemsetAsync(counters, 0, kNoAllocCounterBytes + kNoAllocStatusBytes, st);
+  int* status = status_word(scratch);
+  // Tickets must start at zero; a previous call may have left them
+  // otherwise if it gave up on a wait.  The status word is left for
+  // molot_noalloc_status to report.
+  e = cudaMemsetAsync(counters, 0, kNoAllocCounterBytes, st);
   if (e != cudaSuccess) return cuda_err(e, "cudaMemsetAsync(no-alloc tickets)");
+  // The partition and kernel variant of molot_attn_decode_strided_dev: one
+  // segment per CTA when there are at least as many CTAs as kv heads, and
+  // the split K/V stage barriers for long FP32 launches at head_dim <= 128.
+  const int aligned = grid >= nkv ? 1 : 0;
+  {
+    const int tile_rows = d <= 64 ? TileShape<64, float>::T : TileShape<128, float>::T;
+    const long long rows_per_cta = (long long)nblk * kBlk * nkv / grid;
+    KernelRef ks;
+    if (d <= 128 && aligned && rows_per_cta >= 8LL * tile_rows && pick(d, G, true, &ks)) k = ks;
+  }
   e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
   if (e != cudaSuccess) return cuda_err(e, "cudaFuncSetAttribute");
 
@@ -197,7 +214,9 @@ extern "C" int molot_attn_decode_strided_noalloc(const float* Q, const float* K,
   a.status = status;
   a.timeout_ns = 2000000000ull;
   a.grid = grid;
+  a.aligned = aligned;
   a.prefetch_old_rows = 0;  // the caller's K/V may come from the preceding launch
+  take_withhold(a);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -211,4 +230,11 @@ extern "C" int molot_attn_decode_strided_noalloc(const float* Q, const float* K,
   void* args[] = {&a};
   e = cudaLaunchKernelExC(&cfg, k.fn, args);
   return e == cudaSuccess ? MOLOT_OK : cuda_err(e, "launch (no-alloc decode)");
+}
+
+extern "C" int molot_noalloc_status(void* stream, int clear) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_err(e, "cudaGetDevice");
+  return noalloc_status_check(dev, static_cast<cudaStream_t>(stream), clear != 0);
 }

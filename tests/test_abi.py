@@ -78,3 +78,29 @@ def test_product_does_not_reference_oracle():
     out = subprocess.run(["nm", "-D", os.path.join(ROOT, "molot_b200", "libmolot_b200.so")],
                          capture_output=True, text=True, check=True).stdout
     assert "oracle_" not in out and "ref_attn" not in out
+
+
+def test_comm_and_hooks_validate_without_device(lib):
+    """The peer-gather group and the test hook reject bad arguments before
+    any CUDA call."""
+    L = lib.library()
+    h = ctypes.c_void_p()
+    assert L.molot_comm_create(0, 0, 1024, ctypes.byref(h)) == lib.ERR_INVALID
+    assert L.molot_comm_create(9, 0, 1024, ctypes.byref(h)) == lib.ERR_INVALID
+    assert L.molot_comm_create(2, 2, 1024, ctypes.byref(h)) == lib.ERR_INVALID
+    assert L.molot_comm_create(2, -1, 1024, ctypes.byref(h)) == lib.ERR_INVALID
+    assert L.molot_comm_create(2, 0, 1000, ctypes.byref(h)) == lib.ERR_INVALID  # not 16-aligned
+    assert L.molot_comm_create(2, 0, 0, ctypes.byref(h)) == lib.ERR_INVALID
+    assert L.molot_comm_create(2, 0, 1024, None) == lib.ERR_INVALID
+    assert L.molot_comm_handle(None, None) == lib.ERR_INVALID
+    assert L.molot_comm_open(None, None) == lib.ERR_INVALID
+    assert L.molot_comm_buffer(None, None) == lib.ERR_INVALID
+    assert L.molot_comm_wait(None, None) == lib.ERR_INVALID
+    assert L.molot_comm_check(None, None) == lib.ERR_INVALID
+    L.molot_comm_destroy(None)
+    assert L.molot_paged_decode_gather(None, None, None, 0, None, None, None, 1, 16, 1.0,
+                                       None) == lib.ERR_INVALID
+    # the hook only records a request; 0 cancels it
+    assert L.molot_debug_withhold_next(1000) == lib.OK
+    assert L.molot_debug_withhold_next(0) == lib.OK
+    assert lib.COMM_HANDLE_BYTES == 64 and lib.COMM_MAX_RANKS == 8

@@ -1,6 +1,7 @@
 """GPU parity of the paged, batched decode (continuous batching) and of the
 batched append, against per-sequence calls of the oracle on gathered pages."""
 import math
+import os
 
 import numpy as np
 import pytest
@@ -85,6 +86,52 @@ def test_paged_batch64_llama8b(mb, torch_cuda, orc):
     Q = rng.standard_normal((64, nq, d)).astype(np.float32)
     got = run_paged(mb, torch_cuda, Q, Kp, Vp, bt, lens, None, nq, nkv, d, ps, d ** -0.5, 0)
     check_against_oracle(orc, got, Q, Kp, Vp, bt, lens, None, nq, nkv, d, ps, d ** -0.5, 0)
+
+
+def oracle_parallel(orc, Q, Kp, Vp, bt, lens, nq, nkv, d, ps, scale, window):
+    """The oracle per sequence, sequences on threads (the C checker releases
+    the GIL), for the long-context cases."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    def one(b):
+        return orc.attn_decode_paged(Q[b:b + 1], Kp, Vp, bt[b:b + 1], [lens[b]], None, 1, nq,
+                                     nkv, d, ps, scale, window)[0]
+
+    with ThreadPoolExecutor(max_workers=min(len(lens), os.cpu_count() or 1)) as ex:
+        return np.stack(list(ex.map(one, range(len(lens)))))
+
+
+def test_paged_cfg4_full_lengths(mb, torch_cuda, orc):
+    """cfg4 as configured: lengths from its own seeded U[512, 32768] draw
+    (the bench's draw, always including its longest sequence), Llama-3-8B
+    heads, 16-slot pages, a shuffled block table; 8 of its 64 sequences."""
+    rng = np.random.default_rng(4)
+    draw = [int(x) for x in rng.integers(512, 32769, size=64)]
+    longest = int(np.argmax(draw))
+    pick = [longest] + [i for i in range(64) if i != longest][:7]
+    lens = [draw[i] + 1 for i in pick]  # cached slots + the new token's
+    nq, nkv, d, ps = 32, 8, 128, 16
+    Kp, Vp, bt = make_pool(lens, nkv, d, ps, seed=404)
+    Q = np.random.default_rng(405).standard_normal((len(lens), nq, d)).astype(np.float32)
+    got = run_paged(mb, torch_cuda, Q, Kp, Vp, bt, lens, None, nq, nkv, d, ps, d ** -0.5, 0)
+    want = oracle_parallel(orc, Q, Kp, Vp, bt, lens, nq, nkv, d, ps, d ** -0.5, 0)
+    for b in range(len(lens)):
+        assert orc.rel_err(got[b], want[b]) <= PARITY_TOL, (b, lens[b])
+
+
+def test_paged_cfg5_one_rank(mb, torch_cuda, orc):
+    """cfg5 as one of 8 ranks sees it: one kv head and its 8 query heads
+    (G = 8), 16-slot pages, sequences of ~131k, ~40k and 8k slots plus a
+    short one.  The stream-K partition spreads the 131k-slot segment over
+    ~100 CTAs, so its combine merges many partials in several batches."""
+    lens = [131073, 40001, 8193, 37]
+    nq, nkv, d, ps = 8, 1, 128, 16
+    Kp, Vp, bt = make_pool(lens, nkv, d, ps, seed=505)
+    Q = np.random.default_rng(506).standard_normal((len(lens), nq, d)).astype(np.float32)
+    got = run_paged(mb, torch_cuda, Q, Kp, Vp, bt, lens, None, nq, nkv, d, ps, d ** -0.5, 0)
+    want = oracle_parallel(orc, Q, Kp, Vp, bt, lens, nq, nkv, d, ps, d ** -0.5, 0)
+    for b in range(len(lens)):
+        assert orc.rel_err(got[b], want[b]) <= PARITY_TOL, (b, lens[b])
 
 
 def test_paged_explicit_positions(mb, torch_cuda, orc):

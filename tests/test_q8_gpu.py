@@ -202,3 +202,54 @@ def test_prefill_on_q8_cache(mb, torch_cuda, orc, nq, nkv, hd, M, window):
         assert orc.rel_err(o.cpu().numpy().reshape(nq, hd), want1) <= PARITY_TOL
     finally:
         kv.close()
+
+
+def test_fused_q8_new_rows_code_count(mb, torch_cuda, orc):
+    """The new rows of 48 consecutive fused steps on a Q8 cache: every code
+    of K (QK-norm + RoPE) and V (V-norm) against the oracle's quantization
+    of the reference prologue's rows.  The kernel's RMSNorm / RoPE values
+    may differ from the oracle's correctly rounded libm by an ulp, which
+    moves a code only when x/scale lands within an ulp of a rounding
+    boundary: the count of such codes is bounded and none moves by more
+    than one step."""
+    torch = torch_cuda
+    nq, nkv, hd, n0, steps = 32, 8, 128, 300, 48
+    rng = np.random.default_rng(4848)
+    kc = rng.standard_normal((n0, nkv * hd)).astype(np.float32)
+    vc = rng.standard_normal((n0, nkv * hd)).astype(np.float32)
+    qn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    freq = orc.rope_inv_freq(5e5, hd)
+    ks = rng.standard_normal((steps, nkv * hd)).astype(np.float32)
+    vs = rng.standard_normal((steps, nkv * hd)).astype(np.float32)
+    qs = rng.standard_normal((steps, nq * hd)).astype(np.float32)
+    kv = mb.KVCache(1, nkv, hd, n0 + steps, dtype="q8")
+    try:
+        kv.write(0, 0, cu(torch, kc), cu(torch, vc))
+        kv.set_length(0, n0)
+        o = torch.empty(nq * hd, device="cuda")
+        dqn, dkn, dfreq = cu(torch, qn), cu(torch, kn), cu(torch, freq)
+        for t in range(steps):
+            kv.step(0, cu(torch, qs[t]), cu(torch, ks[t]), cu(torch, vs[t]), o, hd ** -0.5,
+                    n0 + t, 0, dqn, dkn, True, 1e-6, dfreq)
+        kv.check()
+        assert kv.length(0) == n0 + steps
+        kt, vt = kv.layer_tensors(0)
+        got_k = cache_rows(mb, kt[:, n0:], steps, hd)
+        got_v = cache_rows(mb, vt[:, n0:], steps, hd)
+    finally:
+        kv.close()
+    want_k = np.stack([np.concatenate([
+        orc.rope_apply(orc.rmsnorm(ks[t, h * hd:(h + 1) * hd], kn, 1e-6), hd, n0 + t, freq)
+        for h in range(nkv)]) for t in range(steps)])
+    want_v = np.stack([orc.rmsnorm_plain(vs[t], 1e-6) for t in range(steps)])
+    total = moved = 0
+    for (gq, gs), rows in ((got_k, want_k), (got_v, want_v)):
+        wq, ws, _ = oracle_q8(orc, rows, nkv, hd)
+        assert np.max(np.abs(gs - ws) / ws) <= 5e-7
+        dq = np.abs(gq.astype(np.int32) - wq.astype(np.int32))
+        assert dq.max() <= 1
+        total += dq.size
+        moved += int(np.count_nonzero(dq))
+    assert total == 2 * steps * nkv * hd
+    assert moved <= total // 1000, f"{moved} of {total} codes differ by one step"
