@@ -81,6 +81,8 @@ CONFIGS = {
                  len_hi=131072, page=16, theta=5e5, seed=5,
                  desc="Llama-3-70B shape, B=32, n~U[8192,131072], kv-head sharded"),
 }
+for _name, _cfg in CONFIGS.items():
+    _cfg["name"] = _name
 METRIC = "GQA decode attn KV GB/s (% of HBM peak) and tok/s at ctx 16k, 1/2/4/8 GPU"
 
 
@@ -288,10 +290,10 @@ class RefWorkload:
         self.bytes = 0
         self.seconds = 0.0
 
-    def call(self, i, record=True):
+    def call(self, i, record=True, item=None):
         cfg = self.cfg
         nq, nkv, d = cfg["nq"], cfg["nkv"], cfg["d"]
-        j = i % len(self.items)
+        j = i % len(self.items) if item is None else item
         n, pos, w = self.items[j]
         scale = 1.0 / math.sqrt(d)
         if cfg["kind"] == "gemv":  # one layer's GEMVs per call
@@ -363,37 +365,74 @@ def ref_kind_and_cores():
 # ------------------------------------------------------------------ reference arm
 
 def run_reference(args, cfg):
+    """The reference's own attn_decode_gqa_cache on the host cores.  For the
+    single-sequence configs (cfg1 / cfg2) and cfg3 every step is timed in
+    full: one call per layer, each on its own layer-sized cache (two cycled
+    buffers, far larger than the CPU caches), exactly --steps steps after
+    --warmup untimed ones.  The reference times attention only: its per-token
+    norm / RoPE / append (about 1 % of its step) are outside the timed calls,
+    while the GPU arm's step includes them.  The paged, prefill and GEMV
+    configs would take minutes per step on the host: there the line times a
+    bounded sample of calls and extrapolates the step, and says so."""
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
     kind, cores = ref_kind_and_cores()
     wl = RefWorkload(cfg, kind, cores)
-    per_step = len(wl.items) if cfg["kind"] == "gemma" else 2
-    for i in range(args.warmup):
-        wl.call(i, record=False)
-    for i in range(args.steps * per_step):
-        wl.call(i)
-    sec = wl.step_seconds()
     metric, unit, amount, div = step_work(cfg)
-    value = amount / sec / div
     batch = cfg.get("batch", cfg.get("prompt", 1) if cfg["kind"] == "prefill" else 1)
-    what = {"single": f"one layer, n={cfg.get('ctx', 0) + 1}",
-            "gemma": "a global and a 1024-slot SWA layer, alternating",
-            "prefill": f"one layer's attn_prefill_gqa over a {cfg.get('prompt')}-token prompt",
-            "gemv": "one layer's fused-QKV and O gemv_q4",
-            }.get(cfg["kind"], "one sequence per call, lengths from the config's seeded draw")
+    full = cfg["kind"] in ("single", "gemma")
+    if full:
+        items = ([0] * cfg["layers"] if cfg["kind"] == "single" else
+                 [0 if w == 0 else 1 for w, _ in gemma_layers(cfg)])
+        i = 0
+        for _ in range(args.warmup):
+            for j in items:
+                wl.call(i, record=False, item=j)
+                i += 1
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            for j in items:
+                wl.call(i, item=j)
+                i += 1
+        sec = (time.perf_counter() - t0) / args.steps
+        config = (single_config(args, cfg, world) if cfg["kind"] == "single"
+                  else gemma_config(args, cfg, world))
+        sample = (f"{args.steps} full steps timed ({len(items)} attn_decode_gqa_cache calls "
+                  f"each, one per layer) after {args.warmup} untimed; attention only (the "
+                  "reference's norm / RoPE / append are not in the timed calls)")
+        timed_s = sec * args.steps
+    else:
+        per_step = 2
+        for i in range(args.warmup):
+            wl.call(i, record=False)
+        for i in range(args.steps * per_step):
+            wl.call(i)
+        sec = wl.step_seconds()
+        what = {"prefill": f"one layer's attn_prefill_gqa over a {cfg.get('prompt')}-token "
+                           "prompt",
+                "gemv": "one layer's fused-QKV and O gemv_q4",
+                }.get(cfg["kind"], "one sequence per call, lengths from the config's seeded "
+                                   "draw")
+        config = {"workload": f"{args.config}: {cfg['desc']}", "layers": cfg["layers"],
+                  "nq": cfg["nq"], "nkv": cfg["nkv"], "head_dim": cfg["d"],
+                  "kv_dtype": args.kv}
+        sample = wl.describe(what) + (f"; {args.steps * per_step} calls timed in all, not "
+                                      f"{args.steps} full steps")
+        timed_s = wl.seconds
+    value = amount / sec / div
     line = {
         "impl": "reference", "metric": metric, "value": round(value, 3), "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
         "scaling": "weak" if cfg["kind"] in ("single", "gemma", "prefill", "gemv") else "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
-        "config": {"workload": f"{args.config}: {cfg['desc']} (reference CPU sample)",
-                   "layers": cfg["layers"], "nq": cfg["nq"], "nkv": cfg["nkv"],
-                   "head_dim": cfg["d"]},
+        "config": config,
         "tok_per_s": round(batch / sec, 3),
+        "timed_region_s": round(timed_s, 3),
+        "steps_timed_in_full": bool(full),
         "cpu_baseline": {"value": round(value, 3), "unit": unit, "cores": cores, "kind": kind,
-                         "sample": wl.describe(what)},
+                         "sample": sample},
         "e2e": {"value": round(value, 3), "unit": unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -419,116 +458,156 @@ def cpu_baseline_sample(cfg):
 
 # ------------------------------------------------------------------ molot arm
 
-def run_single(args, cfg):
-    import torch
-    import torch.distributed as dist
+def single_config(args, cfg, world):
+    """`config` of a single-sequence line; the reference arm emits the same."""
+    n = cfg["ctx"] + 1
+    per_gpu = step_bytes(cfg, args.kv)
+    return {"workload": f"{args.config}: {cfg['desc']}", "layers": cfg["layers"],
+            "nq": cfg["nq"], "nkv": cfg["nkv"], "head_dim": cfg["d"], "n": n,
+            "rope_theta": cfg["theta"], "kv_dtype": args.kv,
+            "parallelism": f"replicas x{world} (one sequence per GPU)",
+            "l2": f"inputs larger than L2 ({per_gpu / 1e9:.1f} GB KV per GPU)"}
 
-    world, rank, local = dist_env()
-    if world > 1:
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
-    torch.cuda.set_device(local)
-    import molot_b200 as mb
 
-    L, nq, nkv, d = cfg["layers"], cfg["nq"], cfg["nkv"], cfg["d"]
-    ctx = cfg["ctx"]
-    n = ctx + 1
-    scale = 1.0 / math.sqrt(d)
-    dev = torch.device("cuda", local)
-    stream = torch.cuda.current_stream()
+def timed_repeats(rt, fn, steps, repeats):
+    """ms per step over `repeats` windows of exactly `steps` calls of fn, each
+    window timed with CUDA events (barrier + synchronize on both sides) and
+    taken as the max over ranks; returns (median, windows)."""
+    vals = [rt.max(rt.timed(fn, steps)) for _ in range(max(1, repeats))]
+    return statistics.median(vals), vals
 
-    bf16 = args.kv == "bf16"
-    q8 = args.kv == "q8"
-    cache = mb.KVCache(L, nkv, d, n, dtype=args.kv)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(1234 + rank)
-    for layer in range(L):
-        if q8:  # rows enter through the library's quantizing write
-            rows_k = torch.randn((ctx, nkv * d), device=dev, generator=gen)
-            rows_v = torch.randn((ctx, nkv * d), device=dev, generator=gen)
-            cache.write(layer, 0, rows_k, rows_v)
-            del rows_k, rows_v
-            continue
-        kt, vt = cache.layer_tensors(layer)  # head-major [nkv][cap][hd]
-        kt[:, :ctx].normal_(generator=gen)
-        vt[:, :ctx].normal_(generator=gen)
-    q_raw = torch.randn((L, nq * d), device=dev, generator=gen)
-    k_raw = torch.randn((L, nkv * d), device=dev, generator=gen)
-    v_raw = torch.randn((L, nkv * d), device=dev, generator=gen)
-    q_norm = (1 + 0.1 * torch.randn(d, device=dev, generator=gen)).contiguous()
-    k_norm = (1 + 0.1 * torch.randn(d, device=dev, generator=gen)).contiguous()
-    freq = torch.tensor([1.0 / cfg["theta"] ** (2.0 * i / d) for i in range(d // 2)],
-                        dtype=torch.float32, device=dev)
-    q_rot = torch.randn((L, nq * d), device=dev, generator=gen)
-    out = torch.empty((L, nq * d), device=dev)
-    torch.cuda.synchronize()
 
-    fused = args.path == "fused"
-
-    def step(qr, kr, vr, o, decode_only=False):
-        st = torch.cuda.current_stream()
-        for layer in range(L):
-            if decode_only:
-                cache.decode(layer, q_rot[layer], o[layer], scale, ctx, cfg["window"], nq, st)
-                continue
-            cache.set_length(layer, ctx)
-            if fused:
-                cache.step(layer, qr[layer], kr[layer], vr[layer], o[layer], scale, ctx,
-                           cfg["window"], q_norm, k_norm, False, 1e-6, freq, nq, st)
-            else:
-                cache.append_rope(layer, qr[layer], kr[layer], vr[layer], q_rot[layer], q_norm,
-                                  k_norm, False, 1e-6, freq, ctx, nq, st)
-                cache.decode(layer, q_rot[layer], o[layer], scale, ctx, cfg["window"], nq, st)
-
-    def barrier():
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    def timed(fn, iters):
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        barrier()
-        e0.record()
-        for _ in range(iters):
-            fn()
-        e1.record()
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / iters
-
-    # ---- warm-up through the eager API (also sizes the scratch workspace)
-    for _ in range(args.warmup):
-        step(q_raw, k_raw, v_raw, out)
-    cache.check(stream)
-
-    # ---- device-resident step: the 2*L launches captured once, replayed
-    graph = torch.cuda.CUDAGraph()
+def capture(torch, fn):
+    """fn() captured into a CUDA graph after one run on a side stream."""
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
-        step(q_raw, k_raw, v_raw, out)  # warm the side stream
+        fn()
     torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
-    with torch.cuda.graph(graph):
-        step(q_raw, k_raw, v_raw, out)
-    dgraph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(dgraph):
-        step(q_raw, k_raw, v_raw, out, decode_only=True)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return g
+
+
+class SingleSeq:
+    """KV cache, per-layer inputs and the step of a single-sequence config
+    (cfg1 / cfg2): per layer molot_attn_step (fused) or
+    molot_attn_append_rope + molot_attn_decode (split)."""
+
+    def __init__(self, rt, args, cfg):
+        import molot_b200 as mb
+        torch = rt.torch
+        self.rt, self.cfg, self.torch = rt, cfg, torch
+        L, nq, nkv, d = cfg["layers"], cfg["nq"], cfg["nkv"], cfg["d"]
+        self.L, self.nq, self.nkv, self.d = L, nq, nkv, d
+        ctx = self.ctx = cfg["ctx"]
+        self.n = ctx + 1
+        self.scale = 1.0 / math.sqrt(d)
+        self.fused = args.path == "fused"
+        dev = rt.dev
+        self.cache = mb.KVCache(L, nkv, d, self.n, dtype=args.kv)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(1234 + rt.rank)
+        for layer in range(L):
+            if args.kv == "q8":  # rows enter through the library's quantizing write
+                rows_k = torch.randn((ctx, nkv * d), device=dev, generator=gen)
+                rows_v = torch.randn((ctx, nkv * d), device=dev, generator=gen)
+                self.cache.write(layer, 0, rows_k, rows_v)
+                del rows_k, rows_v
+                continue
+            kt, vt = self.cache.layer_tensors(layer)  # head-major [nkv][cap][hd]
+            kt[:, :ctx].normal_(generator=gen)
+            vt[:, :ctx].normal_(generator=gen)
+        self.q_raw = torch.randn((L, nq * d), device=dev, generator=gen)
+        self.k_raw = torch.randn((L, nkv * d), device=dev, generator=gen)
+        self.v_raw = torch.randn((L, nkv * d), device=dev, generator=gen)
+        self.q_norm = (1 + 0.1 * torch.randn(d, device=dev, generator=gen)).contiguous()
+        self.k_norm = (1 + 0.1 * torch.randn(d, device=dev, generator=gen)).contiguous()
+        self.freq = rope_freq(torch, cfg["theta"], d, dev)
+        self.q_rot = torch.randn((L, nq * d), device=dev, generator=gen)
+        self.out = torch.empty((L, nq * d), device=dev)
+        torch.cuda.synchronize()
+
+    def step(self, qr=None, kr=None, vr=None, o=None, decode_only=False):
+        qr = self.q_raw if qr is None else qr
+        kr = self.k_raw if kr is None else kr
+        vr = self.v_raw if vr is None else vr
+        o = self.out if o is None else o
+        st = self.torch.cuda.current_stream()
+        c, cfg = self.cache, self.cfg
+        for layer in range(self.L):
+            if decode_only:
+                c.decode(layer, self.q_rot[layer], o[layer], self.scale, self.ctx, cfg["window"],
+                         self.nq, st)
+                continue
+            c.set_length(layer, self.ctx)
+            if self.fused:
+                c.step(layer, qr[layer], kr[layer], vr[layer], o[layer], self.scale, self.ctx,
+                       cfg["window"], self.q_norm, self.k_norm, False, 1e-6, self.freq, self.nq,
+                       st)
+            else:
+                c.append_rope(layer, qr[layer], kr[layer], vr[layer], self.q_rot[layer],
+                              self.q_norm, self.k_norm, False, 1e-6, self.freq, self.ctx,
+                              self.nq, st)
+                c.decode(layer, self.q_rot[layer], o[layer], self.scale, self.ctx,
+                         cfg["window"], self.nq, st)
+
+    def close(self):
+        self.cache.close()
+
+
+def single_sub(rt, args, name):
+    """A BASELINE single-sequence config measured beside the headline one
+    (N = 1 line): device time per token of the fused step (CUDA graph)."""
+    cfg = dict(CONFIGS[name])
+    s = SingleSeq(rt, args, cfg)
+    for _ in range(args.warmup):
+        s.step()
+    s.cache.check()
+    g = capture(rt.torch, s.step)
+    for _ in range(args.warmup):
+        g.replay()
+    ms, reps = timed_repeats(rt, g.replay, args.steps, args.repeats)
+    s.cache.check()
+    del g
+    s.close()
+    peak, _ = hbm_peak()
+    layer_bytes = 2 * cfg["nkv"] * (cfg["ctx"] + 1) * kv_row_bytes(args.kv, cfg["d"])
+    achieved = layer_bytes / (ms / cfg["layers"] * 1e-3) / 1e9
+    return {"workload": f"{name}: {cfg['desc']}", "ms_per_token": round(ms, 4),
+            "tok_per_s": round(1000.0 / ms, 1), "value": round(achieved, 1), "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "avg_launch_ms": round(ms / cfg["layers"], 5),
+            "bytes_per_launch": layer_bytes, "repeats_ms": [round(x, 4) for x in reps],
+            "path": "molot_attn_step per layer (CUDA graph)"}
+
+
+def run_single(args, cfg):
+    rt = Rt()
+    torch = rt.torch
+    world, rank = rt.world, rt.rank
+    L, nq, nkv, d = cfg["layers"], cfg["nq"], cfg["nkv"], cfg["d"]
+    n = cfg["ctx"] + 1
+    s = SingleSeq(rt, args, cfg)
+    fused = s.fused
+
+    # ---- warm-up through the eager API (also sizes the scratch workspace)
+    for _ in range(args.warmup):
+        s.step()
+    s.cache.check()
+
+    # ---- device-resident step: the step's launches captured once, replayed
+    graph = capture(torch, s.step)
+    dgraph = capture(torch, lambda: s.step(decode_only=True))
     for _ in range(args.warmup):
         graph.replay()
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(rt.local)
     clocks.start()
     time.sleep(0.3)
-    ms = max_over_ranks(timed(graph.replay, args.steps))
+    ms, reps = timed_repeats(rt, graph.replay, args.steps, args.repeats)
     clk = clocks.stop()
-    cache.check(stream)
+    s.cache.check()
     # dominant kernel: with the fused path every launch of the step is one
     # (prologue + append + decode) kernel, so the step graph times it; the
     # split path replays L back-to-back decode launches alone.
@@ -537,31 +616,45 @@ def run_single(args, cfg):
     else:
         for _ in range(args.warmup):
             dgraph.replay()
-        dec_avg_ms = timed(dgraph.replay, args.steps) / L
-        cache.check(stream)
+        dec_avg_ms = rt.timed(dgraph.replay, args.steps) / L
+        s.cache.check()
 
     # ---- end-to-end through the public API with host copies (eager calls)
-    h_q = torch.randn((L, nq * d), generator=torch.Generator().manual_seed(5)).pin_memory()
-    h_k = torch.randn((L, nkv * d), generator=torch.Generator().manual_seed(6)).pin_memory()
-    h_v = torch.randn((L, nkv * d), generator=torch.Generator().manual_seed(7)).pin_memory()
-    h_o = torch.empty((L, nq * d)).pin_memory()
-    d_q, d_k, d_v = torch.empty_like(q_raw), torch.empty_like(k_raw), torch.empty_like(v_raw)
-    d_o = torch.empty_like(out)
+    h_q = pinned_like(torch, s.q_raw, 5)
+    h_k = pinned_like(torch, s.k_raw, 6)
+    h_v = pinned_like(torch, s.v_raw, 7)
+    h_o = torch.empty(s.out.shape).pin_memory()
+    d_q, d_k, d_v = (torch.empty_like(t) for t in (s.q_raw, s.k_raw, s.v_raw))
+    d_o = torch.empty_like(s.out)
 
     def e2e_step():
         d_q.copy_(h_q, non_blocking=True)
         d_k.copy_(h_k, non_blocking=True)
         d_v.copy_(h_v, non_blocking=True)
-        step(d_q, d_k, d_v, d_o)
+        s.step(d_q, d_k, d_v, d_o)
         h_o.copy_(d_o, non_blocking=True)
 
     for _ in range(args.warmup):
         e2e_step()
-    e2e_ms = max_over_ranks(timed(e2e_step, args.steps))
-    cache.check(stream)
+    e2e_ms = rt.max(rt.timed(e2e_step, args.steps))
+    s.cache.check()
     del graph, dgraph
+    s.close()
+    torch.cuda.empty_cache()
 
-    row_bytes = mb.q8_row_bytes(d) if q8 else d * (2 if bf16 else 4)
+    # ---- the other BASELINE configs, measured in the same run
+    extras = {}
+    if args.extras and args.config == "cfg2" and args.kv == "f32" and fused:
+        if world == 1:
+            extras["configs"] = {"cfg1": single_sub(rt, args, "cfg1"),
+                                 "cfg3": gemma_sub(rt, args)}
+            torch.cuda.empty_cache()
+        extras["batched"] = {}
+        for name in ("cfg4", "cfg5"):
+            extras["batched"][name] = paged_measure(rt, args, dict(CONFIGS[name]), brief=True)
+            torch.cuda.empty_cache()
+
+    row_bytes = kv_row_bytes(args.kv, d)
     kv_bytes_layer = 2 * nkv * n * row_bytes
     total_bytes = kv_bytes_layer * L * world
     value = total_bytes / (ms * 1e-3) / 1e9
@@ -570,20 +663,17 @@ def run_single(args, cfg):
     achieved = kv_bytes_layer / (dec_avg_ms * 1e-3) / 1e9
     traffic = read_traffic("gqa_decode_kernel",
                            args.config + ("-" + args.kv if args.kv != "f32" else ""))
-
-    result = None
     if rank == 0:
         result = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,1) K/V and q/k/v generated on device)",
-            "config": {"workload": f"{args.config}: {cfg['desc']}", "layers": L, "nq": nq,
-                       "nkv": nkv, "head_dim": d, "n": n, "rope_theta": cfg["theta"],
-                       "kv_dtype": args.kv,
-                       "parallelism": f"replicas x{world} (one sequence per GPU)",
-                       "l2": f"inputs larger than L2 ({total_bytes / world / 1e9:.1f} GB KV "
-                             "per GPU)"},
+            "config": single_config(args, cfg, world),
+            "repeats": {"windows": len(reps), "steps_each": args.steps,
+                        "ms_per_step": [round(x, 4) for x in reps],
+                        "spread_pct": round(100.0 * (max(reps) - min(reps)) / ms, 2),
+                        "reported": "median window (each window: max over ranks)"},
             "tok_per_s": round(world * 1000.0 / ms, 2),
             "pct_hbm_peak": round(100.0 * value / world / peak, 2),
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
@@ -606,13 +696,11 @@ def run_single(args, cfg):
                          "avg_launch_ms": round(dec_avg_ms, 5)},
             "clocks": clk,
         }
+        result.update(extras)
         if world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline_sample(cfg)
         print(json.dumps(result), flush=True)
-    cache.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    rt.close()
     return 0
 
 
@@ -710,88 +798,149 @@ def emit(rt, args, cfg, ms, e2e_ms, clk, h2d, d2h, launches, roof, config, scali
     print(json.dumps(line), flush=True)
 
 
+def gemma_config(args, cfg, world):
+    """`config` of a cfg3 line; the reference arm emits the same."""
+    layers = gemma_layers(cfg)
+    return {"workload": f"{args.config}: {cfg['desc']}", "layers": cfg["layers"],
+            "nq": cfg["nq"], "nkv": cfg["nkv"], "head_dim": cfg["d"], "n": cfg["ctx"] + 1,
+            "global_layers": [l for l, (w, _) in enumerate(layers) if w == 0],
+            "swa_window": cfg["swa_window"], "scale": cfg["scale"], "kv_dtype": args.kv,
+            "parallelism": f"replicas x{world} (one sequence per GPU)",
+            "l2": "inputs larger than L2 (1.585 GB KV read per step)"}
+
+
+class GemmaSeq:
+    """cfg3 (Gemma-3-4B shape): KV cache, inputs and the step, one
+    molot_attn_step launch per layer; SWA layers attend 1024 slots."""
+
+    def __init__(self, rt, args, cfg):
+        import molot_b200 as mb
+        torch = rt.torch
+        self.torch, self.cfg = torch, cfg
+        L, nq, nkv, d = cfg["layers"], cfg["nq"], cfg["nkv"], cfg["d"]
+        self.L, self.nq, self.nkv, self.d = L, nq, nkv, d
+        ctx = self.ctx = cfg["ctx"]
+        self.n = ctx + 1
+        self.layers = gemma_layers(cfg)
+        dev = rt.dev
+        self.cache = mb.KVCache(L, nkv, d, self.n, dtype=args.kv)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(1234 + rt.rank)
+        for l, (w, _) in enumerate(self.layers):
+            lo = max(0, ctx - w + 1) if w else 0
+            if args.kv == "q8":  # rows enter through the library's quantizing write
+                rows = torch.randn((2, ctx - lo, nkv * d), device=dev, generator=gen)
+                self.cache.write(l, lo, rows[0], rows[1])
+                del rows
+                continue
+            kt, vt = self.cache.layer_tensors(l)  # head-major [nkv][cap][hd]
+            kt[:, lo:ctx].normal_(generator=gen)
+            vt[:, lo:ctx].normal_(generator=gen)
+        self.q_raw = torch.randn((L, nq * d), device=dev, generator=gen)
+        self.k_raw = torch.randn((L, nkv * d), device=dev, generator=gen)
+        self.v_raw = torch.randn((L, nkv * d), device=dev, generator=gen)
+        self.q_norm = (1 + 0.1 * torch.randn(d, device=dev, generator=gen)).contiguous()
+        self.k_norm = (1 + 0.1 * torch.randn(d, device=dev, generator=gen)).contiguous()
+        self.freq = {th: rope_freq(torch, th, d, dev) for _, th in self.layers}
+        self.out = torch.empty((L, nq * d), device=dev)
+        self.glob = [l for l, (w, _) in enumerate(self.layers) if w == 0]
+        self.swa = [l for l, (w, _) in enumerate(self.layers) if w != 0]
+        torch.cuda.synchronize()
+
+    def step(self, qr=None, kr=None, vr=None, o=None, only=None):
+        qr = self.q_raw if qr is None else qr
+        kr = self.k_raw if kr is None else kr
+        vr = self.v_raw if vr is None else vr
+        o = self.out if o is None else o
+        st = self.torch.cuda.current_stream()
+        for l in (range(self.L) if only is None else only):
+            w, th = self.layers[l]
+            self.cache.set_length(l, self.ctx)
+            self.cache.step(l, qr[l], kr[l], vr[l], o[l], self.cfg["scale"], self.ctx, w,
+                            self.q_norm, self.k_norm, True, 1e-6, self.freq[th], self.nq, st)
+
+    def close(self):
+        self.cache.close()
+
+
+def gemma_sub(rt, args):
+    """cfg3 beside the headline config (N = 1 line): time per token of the
+    34-launch step, and per launch of its global and SWA layers."""
+    cfg = dict(CONFIGS["cfg3"])
+    g3 = GemmaSeq(rt, args, cfg)
+    for _ in range(args.warmup):
+        g3.step()
+    g3.cache.check()
+    g = capture(rt.torch, g3.step)
+    gg = capture(rt.torch, lambda: g3.step(only=g3.glob))
+    gs = capture(rt.torch, lambda: g3.step(only=g3.swa))
+    for _ in range(args.warmup):
+        g.replay()
+    ms, reps = timed_repeats(rt, g.replay, args.steps, args.repeats)
+    for _ in range(args.warmup):
+        gg.replay()
+    glob_ms = rt.timed(gg.replay, args.steps) / len(g3.glob)
+    for _ in range(args.warmup):
+        gs.replay()
+    swa_ms = rt.timed(gs.replay, args.steps) / len(g3.swa)
+    g3.cache.check()
+    del g, gg, gs
+    g3.close()
+    peak, _ = hbm_peak()
+    total = step_bytes(cfg, args.kv)
+    gbytes = 2 * cfg["nkv"] * (cfg["ctx"] + 1) * kv_row_bytes(args.kv, cfg["d"])
+    sbytes = 2 * cfg["nkv"] * cfg["swa_window"] * kv_row_bytes(args.kv, cfg["d"])
+    value = total / (ms * 1e-3) / 1e9
+    return {"workload": f"cfg3: {cfg['desc']}", "ms_per_token": round(ms, 4),
+            "tok_per_s": round(1000.0 / ms, 1), "value": round(value, 1), "unit": "GB/s",
+            "frac": round(value / peak, 4), "bytes_per_token": total,
+            "global_launch_ms": round(glob_ms, 5),
+            "global_frac": round(gbytes / (glob_ms * 1e-3) / 1e9 / peak, 4),
+            "swa_launch_ms": round(swa_ms, 5),
+            "swa_frac": round(sbytes / (swa_ms * 1e-3) / 1e9 / peak, 4),
+            "repeats_ms": [round(x, 4) for x in reps],
+            "path": "molot_attn_step per layer (CUDA graph)"}
+
+
 def run_gemma(args, cfg):
     """cfg3: one molot_attn_step launch per layer; SWA layers read 1024 slots."""
     rt = Rt()
     torch = rt.torch
-    import molot_b200 as mb
-
-    L, nq, nkv, d = cfg["layers"], cfg["nq"], cfg["nkv"], cfg["d"]
-    ctx, scale = cfg["ctx"], cfg["scale"]
-    n = ctx + 1
-    layers = gemma_layers(cfg)
-    cache = mb.KVCache(L, nkv, d, n, dtype=args.kv)
-    gen = torch.Generator(device=rt.dev)
-    gen.manual_seed(1234 + rt.rank)
-    for l, (w, _) in enumerate(layers):
-        lo = max(0, ctx - w + 1) if w else 0
-        if args.kv == "q8":  # rows enter through the library's quantizing write
-            rows = torch.randn((2, ctx - lo, nkv * d), device=rt.dev, generator=gen)
-            cache.write(l, lo, rows[0], rows[1])
-            del rows
-            continue
-        kt, vt = cache.layer_tensors(l)  # head-major [nkv][cap][hd]
-        kt[:, lo:ctx].normal_(generator=gen)
-        vt[:, lo:ctx].normal_(generator=gen)
-    q_raw = torch.randn((L, nq * d), device=rt.dev, generator=gen)
-    k_raw = torch.randn((L, nkv * d), device=rt.dev, generator=gen)
-    v_raw = torch.randn((L, nkv * d), device=rt.dev, generator=gen)
-    q_norm = (1 + 0.1 * torch.randn(d, device=rt.dev, generator=gen)).contiguous()
-    k_norm = (1 + 0.1 * torch.randn(d, device=rt.dev, generator=gen)).contiguous()
-    freq = {th: rope_freq(torch, th, d, rt.dev) for _, th in layers}
-    out = torch.empty((L, nq * d), device=rt.dev)
-    glob = [l for l, (w, _) in enumerate(layers) if w == 0]
-
-    def step(qr, kr, vr, o, only=None):
-        st = torch.cuda.current_stream()
-        for l in (range(L) if only is None else only):
-            w, th = layers[l]
-            cache.set_length(l, ctx)
-            cache.step(l, qr[l], kr[l], vr[l], o[l], scale, ctx, w, q_norm, k_norm, True, 1e-6,
-                       freq[th], nq, st)
-
+    g3 = GemmaSeq(rt, args, cfg)
+    L, nq, nkv, d, n = g3.L, g3.nq, g3.nkv, g3.d, g3.n
     for _ in range(args.warmup):
-        step(q_raw, k_raw, v_raw, out)
-    cache.check()
-    side = torch.cuda.Stream()
-    side.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(side):
-        step(q_raw, k_raw, v_raw, out)
-    torch.cuda.current_stream().wait_stream(side)
-    torch.cuda.synchronize()
-    graph, ggraph = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        step(q_raw, k_raw, v_raw, out)
-    with torch.cuda.graph(ggraph):
-        step(q_raw, k_raw, v_raw, out, only=glob)
+        g3.step()
+    g3.cache.check()
+    graph = capture(torch, g3.step)
+    ggraph = capture(torch, lambda: g3.step(only=g3.glob))
     for _ in range(args.warmup):
         graph.replay()
     clocks = ClockSampler(rt.local)
     clocks.start()
     time.sleep(0.3)
-    ms = rt.max(rt.timed(graph.replay, args.steps))
+    ms, reps = timed_repeats(rt, graph.replay, args.steps, args.repeats)
     clk = clocks.stop()
     for _ in range(args.warmup):
         ggraph.replay()
-    glob_ms = rt.timed(ggraph.replay, args.steps) / len(glob)
-    cache.check()
+    glob_ms = rt.timed(ggraph.replay, args.steps) / len(g3.glob)
+    g3.cache.check()
 
-    h = [pinned_like(torch, t, 5 + i) for i, t in enumerate((q_raw, k_raw, v_raw))]
+    h = [pinned_like(torch, t, 5 + i) for i, t in enumerate((g3.q_raw, g3.k_raw, g3.v_raw))]
     h_o = torch.empty((L, nq * d)).pin_memory()
-    dq, dk, dv = (torch.empty_like(t) for t in (q_raw, k_raw, v_raw))
-    d_o = torch.empty_like(out)
+    dq, dk, dv = (torch.empty_like(t) for t in (g3.q_raw, g3.k_raw, g3.v_raw))
+    d_o = torch.empty_like(g3.out)
 
     def e2e_step():
         dq.copy_(h[0], non_blocking=True)
         dk.copy_(h[1], non_blocking=True)
         dv.copy_(h[2], non_blocking=True)
-        step(dq, dk, dv, d_o)
+        g3.step(dq, dk, dv, d_o)
         h_o.copy_(d_o, non_blocking=True)
 
     for _ in range(args.warmup):
         e2e_step()
     e2e_ms = rt.max(rt.timed(e2e_step, args.steps))
-    cache.check()
+    g3.cache.check()
     del graph, ggraph
     gbytes = 2 * nkv * n * kv_row_bytes(args.kv, d)
     if rt.rank == 0:
@@ -802,15 +951,14 @@ def run_gemma(args, cfg):
                    "kernel": "gqa_decode_kernel<256,2,1> (fused step, global layer)",
                    "timed": "the 5 global-layer launches alone",
                    "bytes_per_launch": gbytes, "avg_launch_ms": round(glob_ms, 5)},
-             config={"workload": f"{args.config}: {cfg['desc']}", "layers": L, "nq": nq,
-                     "nkv": nkv, "head_dim": d, "n": n, "global_layers": glob,
-                     "swa_window": cfg["swa_window"], "scale": scale,
-                     "parallelism": f"replicas x{rt.world} (one sequence per GPU)",
-                     "l2": "inputs larger than L2 (1.585 GB KV read per step)"},
+             config=gemma_config(args, cfg, rt.world),
              scaling="weak",
              extra={"path": "molot_attn_step per layer (QK-norm, V-norm, RoPE, append, "
-                            "decode in one launch)"})
-    cache.close()
+                            "decode in one launch)",
+                    "repeats": {"windows": len(reps), "steps_each": args.steps,
+                                "ms_per_step": [round(x, 4) for x in reps],
+                                "reported": "median window (each window: max over ranks)"}})
+    g3.close()
     rt.close()
     return 0
 
@@ -1045,165 +1193,358 @@ def fill_normal(torch, dst, template):
         flat[off:off + k].copy_(template[:k])
 
 
-def run_paged(args, cfg):
-    """cfg4 (sequences split over ranks) / cfg5 (kv heads split over ranks,
-    outputs all-gathered): batched append + paged decode per layer."""
-    rt = Rt()
-    torch = rt.torch
-    import molot_b200 as mb
-    from molot_b200 import shard
+class PagedBatch:
+    """cfg4 (sequences split over the ranks by LPT, no collective) / cfg5 (kv
+    heads split over the ranks, each layer's outputs gathered into every
+    rank's [B][nq][d] by the decode itself over NVLink, molot_comm): the
+    pools, block table, plan and per-layer inputs of this rank, and the step
+    (batched append + paged decode per layer)."""
 
-    L, nq, nkv, d, ps = cfg["layers"], cfg["nq"], cfg["nkv"], cfg["d"], cfg["page"]
-    lens = paged_lengths(cfg)
-    B, G = len(lens), nq // nkv
-    if cfg["kind"] == "paged_seq":
-        mine = shard.lpt_partition(lens, rt.world)[rt.rank]
-        g0, g1 = 0, nkv
-        parallelism = f"sequence-sharded (LPT on lengths) over {rt.world} rank(s), no collective"
-    else:
-        mine = list(range(B))
-        g0, g1 = shard.head_shard(nkv, rt.world, rt.rank)
-        parallelism = (f"kv-head sharded over {rt.world} rank(s) ({nkv // rt.world} kv heads "
-                       "each); per-layer NCCL all-gather of O on a second stream")
-    gather = cfg["kind"] == "paged_head" and rt.world > 1
-    nkv_l, Bl = g1 - g0, len(mine)
-    nq_l = nkv_l * G
-    seq = [lens[i] + 1 for i in mine]  # slots including the new token's
-    pages = [math.ceil(x / ps) for x in seq]
-    P = sum(pages)
-    rng = np.random.default_rng(cfg["seed"] + 1000 + rt.rank)
-    perm = rng.permutation(P).astype(np.int32)
-    bt = np.zeros((Bl, max(pages)), np.int32)
-    k = 0
-    for b, m in enumerate(pages):
-        bt[b, :m] = perm[k:k + m]
-        k += m
-    bt_dev = torch.from_numpy(bt).to(rt.dev)
-    # bytes of one row of one kv head in the pools' storage type
-    rb = mb.q8_row_bytes(d) if args.kv == "q8" else d * (2 if args.kv == "bf16" else 4)
-    pool_bytes = 2 * P * nkv_l * ps * rb
-    L_res = max(1, min(L, int(args.resident_gb * 1e9 // pool_bytes)))
-    gen = torch.Generator(device=rt.dev)
-    gen.manual_seed(1234 + rt.rank)
-    template = torch.randn(1 << 26, device=rt.dev, generator=gen)
-    pools = []
-    for _ in range(L_res):
-        if args.kv == "q8":  # random codes, block scales 0.02
-            K = torch.randint(0, 256, (P, nkv_l, ps, rb), dtype=torch.uint8, device=rt.dev,
-                              generator=gen)
-            V = torch.randint(0, 256, (P, nkv_l, ps, rb), dtype=torch.uint8, device=rt.dev,
-                              generator=gen)
-            for t in (K, V):
-                t[..., d:d + d // 8].view(torch.float32).fill_(0.02)
+    def __init__(self, rt, args, cfg):
+        import molot_b200 as mb
+        from molot_b200 import shard
+        torch = rt.torch
+        self.rt, self.args, self.cfg, self.torch, self.mb = rt, args, cfg, torch, mb
+        L, nq, nkv, d, ps = cfg["layers"], cfg["nq"], cfg["nkv"], cfg["d"], cfg["page"]
+        self.L, self.nq, self.nkv, self.d, self.ps = L, nq, nkv, d, ps
+        lens = self.lens = paged_lengths(cfg)
+        B, G = len(lens), nq // nkv
+        self.B = B
+        self.head_sharded = cfg["kind"] == "paged_head"
+        if not self.head_sharded:
+            parts = shard.lpt_partition(lens, rt.world)
+            mine = parts[rt.rank]
+            g0, g1 = 0, nkv
+            loads = [sum(lens[i] + 1 for i in p) for p in parts]
+            self.imbalance = max(loads) / (sum(loads) / len(loads))
         else:
-            dt = torch.bfloat16 if args.kv == "bf16" else torch.float32
-            K = torch.empty((P, nkv_l, ps, d), device=rt.dev, dtype=dt)
-            V = torch.empty((P, nkv_l, ps, d), device=rt.dev, dtype=dt)
-            fill_normal(torch, K, template)
-            fill_normal(torch, V, template[7:])
-        pools.append((K, V))
-    del template
-    q_raw = torch.randn((L, Bl, nq_l, d), device=rt.dev, generator=gen)
-    k_raw = torch.randn((L, Bl, nkv_l, d), device=rt.dev, generator=gen)
-    v_raw = torch.randn((L, Bl, nkv_l, d), device=rt.dev, generator=gen)
-    q_rot = torch.empty_like(q_raw)
-    out = torch.empty_like(q_raw)
-    o_full = torch.empty((L, B, nq, d), device=rt.dev) if gather else None
-    freq = rope_freq(torch, cfg["theta"], d, rt.dev)
-    scale = 1.0 / math.sqrt(d)
-    plan = mb.PagedPlan(args.kv)
-    plan.build(nq_l, nkv_l, d, seq, None, 0)
-    comm = torch.cuda.Stream() if gather else None
+            mine = list(range(B))
+            g0, g1 = shard.head_shard(nkv, rt.world, rt.rank)
+            self.imbalance = 1.0
+        self.mine, self.g0 = mine, g0
+        nkv_l, Bl = g1 - g0, len(mine)
+        nq_l = nkv_l * G
+        self.nkv_l, self.nq_l, self.Bl = nkv_l, nq_l, Bl
+        seq = self.seq = [lens[i] + 1 for i in mine]  # slots including the new token's
+        pages = self.pages = [math.ceil(x / ps) for x in seq]
+        P = sum(pages)
+        rng = np.random.default_rng(cfg["seed"] + 1000 + rt.rank)
+        perm = rng.permutation(P).astype(np.int32)
+        bt = np.zeros((Bl, max(pages)), np.int32)
+        k = 0
+        for b, m in enumerate(pages):
+            bt[b, :m] = perm[k:k + m]
+            k += m
+        self.bt_host = bt
+        self.bt = torch.from_numpy(bt).to(rt.dev)
+        rb = self.rb = kv_row_bytes(args.kv, d)
+        self.pool_bytes = 2 * P * nkv_l * ps * rb
+        self.L_res = max(1, min(L, int(args.resident_gb * 1e9 // self.pool_bytes)))
+        gen = torch.Generator(device=rt.dev)
+        gen.manual_seed(1234 + rt.rank)
+        template = torch.randn(1 << 26, device=rt.dev, generator=gen)
+        self.pools = []
+        for _ in range(self.L_res):
+            if args.kv == "q8":  # random codes, block scales 0.02
+                K = torch.randint(0, 256, (P, nkv_l, ps, rb), dtype=torch.uint8, device=rt.dev,
+                                  generator=gen)
+                V = torch.randint(0, 256, (P, nkv_l, ps, rb), dtype=torch.uint8, device=rt.dev,
+                                  generator=gen)
+                for t in (K, V):
+                    t[..., d:d + d // 8].view(torch.float32).fill_(0.02)
+            else:
+                dt = torch.bfloat16 if args.kv == "bf16" else torch.float32
+                K = torch.empty((P, nkv_l, ps, d), device=rt.dev, dtype=dt)
+                V = torch.empty((P, nkv_l, ps, d), device=rt.dev, dtype=dt)
+                fill_normal(torch, K, template)
+                fill_normal(torch, V, template[7:])
+            self.pools.append((K, V))
+        del template
+        self.q_raw = torch.randn((L, Bl, nq_l, d), device=rt.dev, generator=gen)
+        self.k_raw = torch.randn((L, Bl, nkv_l, d), device=rt.dev, generator=gen)
+        self.v_raw = torch.randn((L, Bl, nkv_l, d), device=rt.dev, generator=gen)
+        self.q_rot = torch.empty_like(self.q_raw)
+        self.out = torch.empty_like(self.q_raw)
+        self.freq = rope_freq(torch, cfg["theta"], d, rt.dev)
+        self.scale = 1.0 / math.sqrt(d)
+        self.plan = mb.PagedPlan(args.kv)
+        self.plan.build(nq_l, nkv_l, d, seq, None, 0)
+        self.local_layer_bytes = sum(2 * nkv_l * x * rb for x in seq)
+        # cfg5: the peer gather (every rank's decode writes into every rank's
+        # buffer); NCCL all-gather only if peer mappings cannot be made here
+        self.mode, self.comm, self.note = None, None, None
+        self.per_layer = B * nq * d
+        if self.head_sharded:
+            self.side = torch.cuda.Stream()
+            self.events = [torch.cuda.Event() for _ in range(L)]
+            try:
+                self.comm = mb.Comm(rt.world, rt.rank, 4 * L * self.per_layer)
+                if rt.world > 1:
+                    hs = [None] * rt.world
+                    rt.dist.all_gather_object(hs, self.comm.ipc_handle())
+                    self.comm.open(hs)
+                self.mode = "peer"
+            except Exception as e:  # report, then gather with NCCL instead
+                self.note = f"peer gather unavailable ({e}); NCCL all-gather used"
+                if self.comm is not None:
+                    self.comm.close()
+                    self.comm = None
+                self.mode = "nccl" if rt.world > 1 else None
+                self.o_full = torch.empty((L, B, nq, d), device=rt.dev)
+        torch.cuda.synchronize()
 
-    def step(qr, kr, vr, o, decode_only=False):
+    def gathered(self):
+        """[L][B][nq][d] view of this rank's gathered outputs (cfg5)."""
+        if self.mode == "peer":
+            return self.comm.buffer((self.L, self.B, self.nq, self.d))
+        return self.o_full if self.mode == "nccl" else self.out
+
+    def step(self, qr=None, kr=None, vr=None, decode_only=False, gather=True):
+        from molot_b200 import shard
+        torch = self.torch
+        qr = self.q_raw if qr is None else qr
+        kr = self.k_raw if kr is None else kr
+        vr = self.v_raw if vr is None else vr
         st = torch.cuda.current_stream()
-        for l in range(L):
-            K, V = pools[l % L_res]
+        peer = gather and not decode_only and self.mode == "peer"
+        nccl = gather and not decode_only and self.mode == "nccl"
+        plan, bt, ps = self.plan, self.bt, self.ps
+        for l in range(self.L):
+            K, V = self.pools[l % self.L_res]
             if not decode_only:
-                plan.append(qr[l], kr[l], vr[l], q_rot[l], K, V, bt_dev, ps, None, None, False,
-                            1e-6, freq, st)
-            plan.decode(q_rot[l], o[l], K, V, bt_dev, ps, scale, st)
-            if gather and not decode_only:
-                ev = torch.cuda.Event()
+                plan.append(qr[l], kr[l], vr[l], self.q_rot[l], K, V, bt, ps, None, None, False,
+                            1e-6, self.freq, st)
+            if peer:
+                plan.decode_gather(self.comm, self.q_rot[l], l * self.per_layer, K, V, bt, ps,
+                                   self.scale, st)
+                ev = self.events[l]
                 ev.record(st)
-                with torch.cuda.stream(comm):
-                    comm.wait_event(ev)
-                    shard.gather_heads(o[l], out=o_full[l])
-        if gather and not decode_only:
-            st.wait_stream(comm)
+                self.side.wait_event(ev)
+                self.comm.wait(self.side)
+            else:
+                plan.decode(self.q_rot[l], self.out[l], K, V, bt, ps, self.scale, st)
+                if nccl:
+                    ev = self.events[l]
+                    ev.record(st)
+                    with torch.cuda.stream(self.side):
+                        self.side.wait_event(ev)
+                        shard.gather_heads(self.out[l], out=self.o_full[l])
+        if peer or nccl:
+            st.wait_stream(self.side)
 
+    def check(self):
+        self.plan.check()
+        if self.comm is not None:
+            self.comm.check()
+
+    def parity(self):
+        """Layer 0 after the timed steps (its pools hold the appended rows,
+        q_rot[0] the rotated queries): this rank's decode against the oracle
+        for the sequences `picked`, and for cfg5 the gathered [B][nq][d]
+        against every rank's own decode output, bit for bit."""
+        import oracle  # the checker, outside every timed region
+        from concurrent.futures import ThreadPoolExecutor
+        torch, rt = self.torch, self.rt
+        K, V = self.pools[0]
+        chk = torch.empty_like(self.out[0])
+        self.plan.decode(self.q_rot[0], chk, K, V, self.bt, self.ps, self.scale)
+        self.plan.check()
+        order = sorted(range(self.Bl), key=lambda b: self.seq[b])
+        if self.head_sharded:  # shortest, longest and two between
+            picked = sorted({order[0], order[len(order) // 3], order[2 * len(order) // 3],
+                             order[-1]})
+        else:  # the longest sequence this rank holds
+            picked = [order[-1]]
+        q = self.q_rot[0].cpu().numpy()
+        o = chk.cpu().numpy()
+        res = {"kind": "oracle (attn.h:125-177 restated) on layer 0, after the timed steps",
+               "seqs_checked_per_rank": len(picked), "tol": 1e-5}
+        if self.args.kv != "f32":
+            res.update(ok=None, skipped="oracle check only on FP32 pools")
+            return res
+        nkv_l, d, ps = self.nkv_l, self.d, self.ps
+
+        def rows(pool, b):
+            n = self.seq[b]
+            idx = torch.from_numpy(self.bt_host[b, :self.pages[b]].astype(np.int64)).to(rt.dev)
+            x = pool.index_select(0, idx).permute(0, 2, 1, 3).reshape(-1, nkv_l * d)[:n]
+            return x.cpu().numpy()
+
+        data = [(b, rows(K, b), rows(V, b)) for b in picked]
+
+        def one(item):
+            # the parity bar: within 1e-5 of the reference's algorithm, or --
+            # at long contexts, where the reference's own FP32 sums drift
+            # that far from the exact value -- no farther from a float64
+            # evaluation than the reference itself (+1e-6)
+            b, kb, vb = item
+            n = self.seq[b]
+            args_ = (q[b].reshape(-1), kb, vb, self.nq_l, nkv_l, n, d, self.scale, n - 1, 0)
+            want = oracle.attn_decode_gqa_cache(*args_)
+            e_ref = oracle.rel_err(o[b], want)
+            if e_ref <= 1e-5:
+                return e_ref, None, None, True
+            f64 = oracle.attn_decode_gqa_cache_f64(*args_)
+            e_gpu64, e_ref64 = oracle.rel_err(o[b], f64), oracle.rel_err(want, f64)
+            return e_ref, e_gpu64, e_ref64, e_gpu64 <= e_ref64 + 1e-6
+
+        with ThreadPoolExecutor(max_workers=min(len(data), os.cpu_count() or 1)) as ex:
+            out = list(ex.map(one, data))
+        del data
+        err = rt.max(max(x[0] for x in out))
+        ok = all(x[3] for x in out)
+        res.update(max_rel_err=err,
+                   bar="rel err <= 1e-5 vs the reference's algorithm, or vs float64 no more "
+                       "than the reference's own + 1e-6")
+        f64 = [x for x in out if x[1] is not None]
+        if f64:
+            res.update(vs_f64={"gpu": max(x[1] for x in f64), "reference": max(x[2] for x in f64),
+                               "seqs": len(f64)})
+        if self.head_sharded and self.mode == "peer":
+            full = self.comm.buffer((self.B, self.nq, self.d))
+            full.fill_(float("nan"))
+            rt.barrier()
+            self.plan.decode_gather(self.comm, self.q_rot[0], 0, K, V, self.bt, self.ps,
+                                    self.scale)
+            self.comm.wait()
+            self.check()
+            rt.barrier()
+            if rt.world > 1:
+                parts = torch.empty((rt.world,) + tuple(chk.shape), device=rt.dev)
+                rt.dist.all_gather_into_tensor(parts, chk.contiguous())
+                want = parts.permute(1, 0, 2, 3).reshape(self.B, self.nq, self.d)
+            else:
+                want = chk
+            same = bool(torch.equal(full, want))
+            bad = rt.max(0.0 if same else 1.0)
+            res["gather_bit_exact"] = bad == 0.0
+            ok = ok and bad == 0.0
+            rt.barrier()
+        res["ok"] = bool(rt.max(0.0 if ok else 1.0) == 0.0)
+        return res
+
+    def close(self):
+        self.plan.close()
+        if self.comm is not None:
+            self.comm.close()
+        self.pools = []
+
+
+def paged_config(args, cfg, pb, world):
+    lens = pb.lens
+    par = (f"sequence-sharded (LPT on lengths) over {world} rank(s), no collective"
+           if not pb.head_sharded else
+           f"kv-head sharded over {world} rank(s) ({pb.nkv_l} kv heads each); outputs written "
+           "into every rank's [B][nq][d] by the decode itself over NVLink (molot_comm)"
+           if pb.mode == "peer" else
+           f"kv-head sharded over {world} rank(s); per-layer NCCL all-gather on a second stream")
+    return {"workload": f"{cfg['name']}: {cfg['desc']}",
+            "layers": pb.L, "nq": pb.nq, "nkv": pb.nkv, "head_dim": pb.d, "batch": pb.B,
+            "batch_rank0": pb.Bl, "len_min": min(lens), "len_mean": round(sum(lens) / pb.B, 1),
+            "len_max": max(lens), "page_size": pb.ps, "resident_layer_pools": pb.L_res,
+            "parallelism": par, "kv_dtype": args.kv,
+            "l2": f"each layer pool ({pb.pool_bytes / 1e9:.2f} GB on rank 0) > L2"}
+
+
+def paged_measure(rt, args, cfg, brief=False):
+    """Device-time measurements of a paged config at this world size: the
+    step (CUDA graph, max over ranks), rank 0's decode launches alone (the
+    roofline), the limiter, and the in-run parity check."""
+    torch = rt.torch
+    pb = PagedBatch(rt, args, cfg)
     for _ in range(args.warmup):
-        step(q_raw, k_raw, v_raw, out)
-    plan.check()
-    side = torch.cuda.Stream()
-    side.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(side):
-        step(q_raw, k_raw, v_raw, out, decode_only=True)
-    torch.cuda.current_stream().wait_stream(side)
-    torch.cuda.synchronize()
-    dgraph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(dgraph):
-        step(q_raw, k_raw, v_raw, out, decode_only=True)
-    graph = None
-    if not gather:  # NCCL stays out of graphs; the gathered step runs eagerly
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step(q_raw, k_raw, v_raw, out)
-        run = graph.replay
-    else:
-        def run():
-            step(q_raw, k_raw, v_raw, out)
+        pb.step()
+    pb.check()
+    graph = capture(torch, pb.step)
+    dgraph = capture(torch, lambda: pb.step(decode_only=True))
     for _ in range(args.warmup):
-        run()
-    clocks = ClockSampler(rt.local)
-    clocks.start()
-    time.sleep(0.3)
-    ms = rt.max(rt.timed(run, args.steps))
-    clk = clocks.stop()
+        graph.replay()
+    ms, reps = timed_repeats(rt, graph.replay, args.steps, 3 if brief else args.repeats)
+    mine_ms = rt.timed(graph.replay, args.steps)  # this rank alone, for the imbalance
+    mean_ms = rt.sum(mine_ms) / rt.world
     for _ in range(args.warmup):
         dgraph.replay()
-    dec_ms = rt.timed(dgraph.replay, args.steps) / L
-    plan.check()
+    dec_ms = rt.timed(dgraph.replay, args.steps) / pb.L
+    pb.check()
+    limiter = {"lpt_bytes_max_over_mean": round(pb.imbalance, 4),
+               "rank_step_ms_max_over_mean": round(rt.max(mine_ms) / mean_ms, 4)}
+    if pb.head_sharded and pb.mode is not None:
+        ngraph = capture(torch, lambda: pb.step(gather=False))
+        for _ in range(args.warmup):
+            ngraph.replay()
+        plain_ms = rt.max(rt.timed(ngraph.replay, args.steps))
+        del ngraph
+        limiter.update(gather=pb.mode, step_without_gather_ms=round(plain_ms, 4),
+                       gather_cost_ms_per_step=round(ms - plain_ms, 4),
+                       gather_cost_pct=round(100.0 * (ms - plain_ms) / ms, 2))
+        if pb.note:
+            limiter["note"] = pb.note
+    pb.check()
+    del graph, dgraph
+    parity = pb.parity()
+    peak, peak_kind = hbm_peak()
+    total = step_bytes(cfg, args.kv)
+    achieved = pb.local_layer_bytes / (dec_ms * 1e-3) / 1e9
+    res = {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+           "ms_per_step": round(ms, 4), "tok_per_s": round(pb.B * 1000.0 / ms, 2),
+           "scaling": "strong", "n_gpus": rt.world,
+           "pct_hbm_peak": round(100.0 * total / (ms * 1e-3) / 1e9 / rt.world / peak, 2),
+           "repeats_ms": [round(x, 4) for x in reps],
+           "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                        "unit": "GB/s", "frac": round(achieved / peak, 4),
+                        "kernel": "gqa_decode_kernel<128,%s> (paged plan)" %
+                                  ("4,2" if pb.nq // pb.nkv == 8 else "4,1"),
+                        "timed": "rank 0's paged decode launches alone",
+                        "bytes_per_launch": pb.local_layer_bytes,
+                        "avg_launch_ms": round(dec_ms, 5),
+                        "peak_source": f"{peak_kind} hbm_gbs"},
+           "limiter": limiter, "parity": parity,
+           "config": paged_config(args, cfg, pb, rt.world),
+           "path": "molot_paged_append + " + ("molot_paged_decode_gather + molot_comm_wait"
+                                              if pb.mode == "peer" else "molot_paged_decode")
+                   + " per layer (CUDA graph)"}
+    if brief:
+        pb.close()
+        return res
+    return res, pb
 
-    h = [pinned_like(torch, t, 5 + i) for i, t in enumerate((q_raw, k_raw, v_raw))]
-    res = o_full if gather else out
-    h_o = torch.empty(res.shape).pin_memory()
-    dq, dk, dv = (torch.empty_like(t) for t in (q_raw, k_raw, v_raw))
-    d_o = torch.empty_like(out)
+
+def run_paged(args, cfg):
+    """cfg4 / cfg5 as the line's own workload (with e2e)."""
+    rt = Rt()
+    torch = rt.torch
+    clocks = ClockSampler(rt.local)
+    clocks.start()
+    res, pb = paged_measure(rt, args, cfg)
+    clk = clocks.stop()
+    h = [pinned_like(torch, t, 5 + i) for i, t in enumerate((pb.q_raw, pb.k_raw, pb.v_raw))]
+    res_dev = pb.gathered() if pb.head_sharded else pb.out
+    h_o = torch.empty(tuple(res_dev.shape)).pin_memory()
+    dq, dk, dv = (torch.empty_like(t) for t in (pb.q_raw, pb.k_raw, pb.v_raw))
 
     def e2e_step():
         dq.copy_(h[0], non_blocking=True)
         dk.copy_(h[1], non_blocking=True)
         dv.copy_(h[2], non_blocking=True)
-        step(dq, dk, dv, d_o)
-        h_o.copy_(o_full if gather else d_o, non_blocking=True)
+        pb.step(dq, dk, dv)
+        h_o.copy_(res_dev, non_blocking=True)
 
     for _ in range(args.warmup):
         e2e_step()
     e2e_ms = rt.max(rt.timed(e2e_step, args.steps))
-    plan.check()
-    del graph, dgraph
-    local_layer_bytes = sum(2 * nkv_l * x * rb for x in seq)
-    h2d = rt.sum(4 * L * Bl * (nq_l + 2 * nkv_l) * d)
+    pb.check()
+    h2d = rt.sum(4 * pb.L * pb.Bl * (pb.nq_l + 2 * pb.nkv_l) * pb.d)
     d2h = rt.sum(h_o.numel() * 4)
     if rt.rank == 0:
-        emit(rt, args, cfg, ms, e2e_ms, clk, h2d=h2d, d2h=d2h,
-             launches=2 * L * args.steps,
-             roof={"bound": "hbm", "achieved": round(local_layer_bytes / (dec_ms * 1e-3) / 1e9, 1),
-                   "traffic": read_traffic("gqa_decode_kernel", args.config),
-                   "kernel": "gqa_decode_kernel<128,4,1> (paged plan)",
-                   "timed": "rank 0's paged decode launches alone",
-                   "bytes_per_launch": local_layer_bytes, "avg_launch_ms": round(dec_ms, 5)},
-             config={"workload": f"{args.config}: {cfg['desc']}", "layers": L, "nq": nq,
-                     "nkv": nkv, "head_dim": d, "batch": B, "batch_rank0": Bl,
-                     "len_min": min(lens), "len_mean": round(sum(lens) / B, 1),
-                     "len_max": max(lens), "page_size": ps,
-                     "resident_layer_pools": L_res, "parallelism": parallelism,
-                     "l2": f"each layer pool ({pool_bytes / 1e9:.2f} GB on rank 0) > L2"},
-             scaling="strong",
-             extra={"path": "molot_paged_append + molot_paged_decode per layer"
-                            + (" + NCCL all-gather" if gather else "")})
-    plan.close()
+        emit(rt, args, cfg, res["ms_per_step"], e2e_ms, clk, h2d=h2d, d2h=d2h,
+             launches=(2 if pb.mode != "peer" else 3) * pb.L * args.steps,
+             roof={k: v for k, v in res["roofline"].items()
+                   if k not in ("peak", "unit", "frac", "peak_source")} |
+             {"traffic": read_traffic("gqa_decode_kernel", args.config)},
+             config=res["config"], scaling="strong",
+             extra={"path": res["path"], "limiter": res["limiter"], "parity": res["parity"],
+                    "repeats_ms": res["repeats_ms"]})
+    pb.close()
     rt.close()
     return 0
 
@@ -1226,6 +1567,12 @@ def main(argv=None):
                     help="cfg4/cfg5: device memory for distinct layer pools per rank")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (small cases for profiler captures)")
+    ap.add_argument("--repeats", type=int, default=5,
+                    help="timed windows of exactly --steps steps each; the line reports the "
+                         "median window")
+    ap.add_argument("--no-extras", dest="extras", action="store_false",
+                    help="default run only: skip the cfg1/cfg3 objects (N=1) and the batched "
+                         "cfg4/cfg5 objects (every N)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
