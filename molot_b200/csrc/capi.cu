@@ -239,10 +239,28 @@ int check_shape(int nq, int nkv, int d, KernelRef* k, int kvt = MOLOT_KV_F32) {
   return MOLOT_OK;
 }
 
-// One decode grid; split segments are merged inside it by their last CTA.
+// One decode grid; split segments are merged inside it (by their last CTA,
+// or by thread-block clusters, DecodeArgs::cluster).
 int launch_decode(const KernelRef& k, DecodeArgs& a, cudaStream_t st) {
   take_withhold(a);
-  return launch(k.fn, dim3(a.grid), dim3(kDecodeThreads), k.smem, st, &a);
+  if (a.cluster < 2) return launch(k.fn, dim3(a.grid), dim3(kDecodeThreads), k.smem, st, &a);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = a.cluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.grid);
+  cfg.blockDim = dim3(kDecodeThreads);
+  cfg.dynamicSmemBytes = k.smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  void* args[] = {&a};
+  MOLOT_CUDA(cudaLaunchKernelExC(&cfg, k.fn, args));
+  return MOLOT_OK;
 }
 
 // Single-sequence decode over a strided contiguous cache.  prefetch_old_rows:
@@ -270,13 +288,17 @@ int decode_uniform(Workspace& ws, const float* Q, float* O, const void* K, const
   const int blo = t0 / kBlk;
   const int nblk = (n + kBlk - 1) / kBlk - blo;
   const long long NB = (long long)nkv * nblk;
-  const int grid = (int)std::min<long long>(NB, sm_count(dev));
+  if ((rc = prepare_kernel(k, dev))) return rc;
+  const UniformPlan up =
+      plan_uniform(NB, nkv, nblk, sm_count(dev), max_active_clusters(k, kClusterCtas, dev));
+  const int grid = up.grid;
   const int G = nq / nkv;
   if ((rc = ws.ensure(dev, (size_t)2 * grid * partial_record_floats(G, d), nkv, 0))) return rc;
-  if ((rc = prepare_kernel(k, dev))) return rc;
   DecodeArgs a = {};
   a.grid = grid;
-  a.aligned = grid >= nkv ? 1 : 0;  // one segment per CTA (see DecodeArgs)
+  a.aligned = up.aligned;  // one segment per CTA (see DecodeArgs)
+  a.cluster = up.cluster;
+  a.cl_per_seg = up.cl_per_seg;
   // The last CTA of a segment holds slot n-1: in a fused step it also
   // builds that row, in a decode right after the append that wrote it, it
   // can only stream that row once the append has completed.  Half a share
@@ -533,6 +555,36 @@ int gemv_q4_launch(const float* scales, const int8_t* zeros, const uint8_t* data
 // Lets other translation units of the library report through
 // molot_last_error().
 int set_last_error(int code, const char* msg) { return fail(code, msg); }
+
+int max_active_clusters(const KernelRef& k, int cluster, int dev) {
+  static std::mutex mu;
+  struct Entry {
+    const void* fn;
+    int cluster, dev, n;
+  };
+  static std::vector<Entry> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  for (auto& e : cache)
+    if (e.fn == k.fn && e.cluster == cluster && e.dev == dev) return e.n;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cluster * 64);
+  cfg.blockDim = dim3(kDecodeThreads);
+  cfg.dynamicSmemBytes = k.smem;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, k.fn, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache.push_back({k.fn, cluster, dev, n});
+  return n;
+}
 
 // molot_debug_withhold_next: pending request of the calling host thread.
 thread_local unsigned long long g_withhold_ns = 0;

@@ -137,10 +137,22 @@ struct KvElem<Q8Row> {
     const int sh = (m & 1) * 16;
     const float c0 = __int2float_rn((int)(signed char)(w >> sh));
     const float c1 = __int2float_rn((int)(signed char)(w >> (sh + 8)));
-    x0 = __fmul_rn(c0, s);
-    x1 = __fmul_rn(c1, s);
+    const float2 x = __fmul2_rn(make_float2(c0, c1), make_float2(s, s));
+    x0 = x.x;
+    x1 = x.y;
   }
 };
+
+// Two independent round-to-nearest FMAs in one packed-FP32 instruction
+// (sm_100): (d0, d1) += (a0 * b0, a1 * b1).  Each half rounds exactly as
+// __fmaf_rn does, so the reference's accumulation order and its bits are
+// kept while the consumers issue half the FMA instructions.
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0,
+                                     float b1) {
+  const float2 r = __ffma2_rn(make_float2(a0, a1), make_float2(b0, b1), make_float2(d0, d1));
+  d0 = r.x;
+  d1 = r.y;
+}
 
 // Sum of squares of one q head held in a row group's lane layout, equal bit
 // for bit to the reference's (norm.h:10-18: 16 FMA accumulators, accumulator
@@ -239,6 +251,15 @@ struct DecodeArgs {
   // (kShareW - tail_w) / kShareW of the others' (it also builds the fused
   // step's new row, which holds slot n-1).  0: equal shares.
   int tail_w;
+  // Cluster merge (uniform launches, aligned partition): each segment's CTAs
+  // form cl_per_seg thread-block clusters of `cluster` CTAs (grid = S *
+  // cl_per_seg * cluster).  A cluster merges its CTAs' partials through
+  // distributed shared memory; with one cluster per segment that merge
+  // writes the output, otherwise each cluster leaves one partial record and
+  // the last cluster to finish (ticket) merges the cl_per_seg records.
+  // cluster < 2: off (per-CTA partials, ticket and last-CTA combine).
+  int cluster;
+  int cl_per_seg;
   // Programmatic dependent launch.  When set, the producer may stream each
   // segment's slots below its newest one (n-1) before the preceding launch
   // has completed: they were written two or more launches earlier (the
@@ -458,10 +479,7 @@ __device__ __forceinline__ void process_rows(const KT* kr, const KT* vr, int tok
       float k0, k1;
       E::template load2<D>(k, mm, l8, k0, k1);
 #pragma unroll
-      for (int h = 0; h < GS; ++h) {
-        a0[h] = __fmaf_rn(q[h][2 * mm], k0, a0[h]);
-        a1[h] = __fmaf_rn(q[h][2 * mm + 1], k1, a1[h]);
-      }
+      for (int h = 0; h < GS; ++h) fma2(a0[h], a1[h], q[h][2 * mm], q[h][2 * mm + 1], k0, k1);
     }
     // The reference's _mm512_reduce_add_ps tree: lanes l and l+8 (held by
     // this lane), then l^4, l^2, l^1 within the row group.
@@ -493,7 +511,11 @@ __device__ __forceinline__ void process_rows(const KT* kr, const KT* vr, int tok
       const float alpha = need ? ex2(m2[h] - mc2[h]) : 1.f;
       l[h] *= alpha;
 #pragma unroll
-      for (int i = 0; i < 2 * DV; ++i) o[h][i] *= alpha;
+      for (int i = 0; i < 2 * DV; i += 2) {
+        const float2 x = __fmul2_rn(make_float2(o[h][i], o[h][i + 1]), make_float2(alpha, alpha));
+        o[h][i] = x.x;
+        o[h][i + 1] = x.y;
+      }
       m2[h] = need ? mc2[h] : m2[h];
     }
   }
@@ -520,10 +542,8 @@ __device__ __forceinline__ void process_rows(const KT* kr, const KT* vr, int tok
         v1 = 0.f;
       }
 #pragma unroll
-      for (int h = 0; h < GS; ++h) {
-        o[h][2 * mm] = __fmaf_rn(p[r][h], v0, o[h][2 * mm]);
-        o[h][2 * mm + 1] = __fmaf_rn(p[r][h], v1, o[h][2 * mm + 1]);
-      }
+      for (int h = 0; h < GS; ++h)
+        fma2(o[h][2 * mm], o[h][2 * mm + 1], p[r][h], p[r][h], v0, v1);
     }
   }
 }
@@ -807,6 +827,102 @@ __device__ __forceinline__ void combine_segment(const DecodeArgs& a, int s, cons
   }
 }
 
+// Cluster merge of a segment (see DecodeArgs::cluster), run by the 256
+// consumer threads of every CTA of the cluster after its piece: `cbuf` (this
+// CTA's shared memory) holds the CTA's partial -- o[G][D], then m[G], l[G]
+// in the log2 domain -- or, when the CTA had no slots, nothing yet.  The
+// cluster's CTAs each merge a slice of the float4 chunks of o across the
+// cluster, reading the peers' partials through distributed shared memory.
+template <int D>
+__device__ __forceinline__ void cluster_finish(const DecodeArgs& a, int cta, float* cbuf,
+                                               bool have_part, int ctid,
+                                               volatile int* ticket_sm) {
+  constexpr int NT = kConsumerWarps * 32;
+  const int G = a.G;
+  const int GD = G * D;
+  const int C = a.cluster;
+  if (!have_part) {  // no slots in this CTA's range: a neutral partial
+    for (int i = ctid; i < GD + 2 * G; i += NT)
+      cbuf[i] = (i >= GD && i < GD + G) ? -CUDART_INF_F : 0.f;
+  }
+  ptx::cluster_sync();  // every CTA's partial is in its shared memory
+  const int cs = C * a.cl_per_seg;  // CTAs per segment
+  const int s = cta / cs;
+  const int ci = (cta - s * cs) / C;  // cluster index within the segment
+  const SegView sv = seg_view(a, s);
+  float* out_seg = a.O + (long long)sv.b * a.o_bstride + (long long)sv.g * G * D;
+  const int psz = partial_record_floats(G, D);
+  float* rec = a.partials + (size_t)(s * a.cl_per_seg + ci) * psz;
+  const uint32_t rank = ptx::cluster_ctarank();
+  const int nchunk = GD / 4;
+  for (int chunk = (int)rank * NT + ctid; chunk < nchunk; chunk += C * NT) {
+    const int hl = (chunk * 4) / D;
+    float M = -CUDART_INF_F;
+    for (int r = 0; r < C; ++r) M = fmaxf(M, ptx::ld_dsmem(ptx::dsmem_addr(cbuf + GD + hl, r)));
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < C; ++r) {
+      const float mr = ptx::ld_dsmem(ptx::dsmem_addr(cbuf + GD + hl, r));
+      const float lr = ptx::ld_dsmem(ptx::dsmem_addr(cbuf + GD + G + hl, r));
+      const float4 o4 = ptx::ld_dsmem4(ptx::dsmem_addr(cbuf + chunk * 4, r));
+      const float f = (mr == -CUDART_INF_F) ? 0.f : ex2(mr - M);
+      L = __fmaf_rn(lr, f, L);
+      acc.x = __fmaf_rn(o4.x, f, acc.x);
+      acc.y = __fmaf_rn(o4.y, f, acc.y);
+      acc.z = __fmaf_rn(o4.z, f, acc.z);
+      acc.w = __fmaf_rn(o4.w, f, acc.w);
+    }
+    if (a.cl_per_seg == 1) {
+      float* dst = out_seg + chunk * 4;
+      put_out(a, dst + 0, acc.x / L);
+      put_out(a, dst + 1, acc.y / L);
+      put_out(a, dst + 2, acc.z / L);
+      put_out(a, dst + 3, acc.w / L);
+    } else {
+      reinterpret_cast<float4*>(rec)[chunk] = acc;
+      if ((chunk * 4) % D == 0) {
+        rec[GD + hl] = M;
+        rec[GD + G + hl] = L;
+      }
+    }
+  }
+  if (a.cl_per_seg > 1) __threadfence();  // the record slices, before the leader's ticket
+  ptx::cluster_sync();  // no CTA reads a peer's shared memory after this
+  if (a.cl_per_seg > 1 && rank == 0) {
+    // The cluster's record is complete; the last cluster of the segment to
+    // draw a ticket merges the segment's records.
+    if (ctid == 0) *ticket_sm = ptx::atom_add_acq_rel_gpu(a.counters + s, 1);
+    ptx::named_bar_sync(1, NT);
+    if (*ticket_sm == a.cl_per_seg - 1) {
+      const float* recs = a.partials + (size_t)s * a.cl_per_seg * psz;
+      for (int chunk = ctid; chunk < nchunk; chunk += NT) {
+        const int hl = (chunk * 4) / D;
+        float M = -CUDART_INF_F;
+        for (int k = 0; k < a.cl_per_seg; ++k) M = fmaxf(M, __ldcg(recs + k * psz + GD + hl));
+        float L = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < a.cl_per_seg; ++k) {
+          const float* rk = recs + (size_t)k * psz;
+          const float mr = __ldcg(rk + GD + hl);
+          const float f = (mr == -CUDART_INF_F) ? 0.f : ex2(mr - M);
+          const float4 o4 = __ldcg(reinterpret_cast<const float4*>(rk) + chunk);
+          L = __fmaf_rn(__ldcg(rk + GD + G + hl), f, L);
+          acc.x = __fmaf_rn(o4.x, f, acc.x);
+          acc.y = __fmaf_rn(o4.y, f, acc.y);
+          acc.z = __fmaf_rn(o4.z, f, acc.z);
+          acc.w = __fmaf_rn(o4.w, f, acc.w);
+        }
+        float* dst = out_seg + chunk * 4;
+        put_out(a, dst + 0, acc.x / L);
+        put_out(a, dst + 1, acc.y / L);
+        put_out(a, dst + 2, acc.z / L);
+        put_out(a, dst + 3, acc.w / L);
+      }
+      if (ctid == 0) a.counters[s] = 0;
+    }
+  }
+}
+
 // SPLIT: the K and V halves of each ring stage fill and free on their own
 // barriers, so a stage's K half is refilled as soon as every warp has its
 // scores.  The host launches it where it measured faster: single-sequence
@@ -1019,6 +1135,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
 
   int it = 0;
   bool tables_ready = false;
+  const bool clustered = a.cluster > 1;
+  // cluster merge: this CTA's partial, in the ring (idle once the CTA's
+  // last tile is consumed; a cluster-merged CTA has one piece)
+  float* cbuf = reinterpret_cast<float*>(stages);
+  bool have_part = false;
   long long pos = cbeg;
   int s = s_first;
   while (pos < cend) {
@@ -1029,7 +1150,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
       const int le = sv.blo + (int)(pend - sv.gbeg);
       const int pt0 = max(sv.t0, lb * kBlk);
       const int pt1 = min(sv.n, le * kBlk);
-      const bool whole = (pos == sv.gbeg) && (pend == sv.gend);
+      // A cluster-merged launch always merges, even a piece that is the
+      // whole segment (its cluster peers then hold empty partials).
+      const bool whole = !clustered && (pos == sv.gbeg) && (pend == sv.gend);
       // CTAs sharing this segment, for the merge after the piece: computed
       // here, off the critical path at the piece's end, and parked in shared
       // memory (read after the finalize barriers) rather than in registers.
@@ -1221,17 +1344,19 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         if (whole) {
           put_out(a, out_seg + idx, acc / L);
         } else {
-          part[idx] = acc;
+          float* dst = clustered ? cbuf : part;
+          dst[idx] = acc;
           if (j == 0) {
-            part[G * D + hl] = M;
-            part[G * D + G + hl] = L;
+            dst[G * D + hl] = M;
+            dst[G * D + G + hl] = L;
           }
         }
       }
+      have_part = true;
       // Every partial (or output) write of this CTA is issued before the
       // barrier; the merge buffer is free again after it.
       ptx::named_bar_sync(1, kConsumerWarps * 32);
-      if (!whole) {
+      if (!whole && !clustered) {
         // One thread publishes the CTA's partial and takes a ticket; the CTA
         // that draws the last ticket of the segment merges all partials.
         const long long cf = seg_cta_sm[0];
@@ -1248,6 +1373,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     pos = pend > pos ? pend : pos;
     ++s;
   }
+  if (clustered) cluster_finish<D>(a, cta, cbuf, have_part, ctid, ticket_sm);
   if (a.npeer > 0) {
     // Peer gather: once every CTA's output stores are issued, the last CTA
     // to finish publishes this launch's epoch in every rank's buffer.  The

@@ -21,4 +21,50 @@ bool pick_decode_q8(int D, int G, KernelRef* k);
 // gqa_prefill_kernel for a head_dim and a storage type.
 bool pick_prefill_kv(int D, int kvt, KernelRef* k);
 
+// Thread-block clusters of this many CTAs that kernel k can keep resident
+// at once on device dev (cached; 0 when the query fails).
+int max_active_clusters(const KernelRef& k, int cluster, int dev);
+
+// Partition of a single-sequence (uniform) decode launch of S segments
+// (kv heads) of nblk 16-slot blocks each.
+struct UniformPlan {
+  int grid = 0;
+  int aligned = 0;     // one segment per CTA (DecodeArgs::aligned)
+  int cluster = 0;     // DecodeArgs::cluster
+  int cl_per_seg = 0;  // DecodeArgs::cl_per_seg
+};
+
+constexpr int kClusterCtas = 8;       // CTAs per cluster (portable size)
+constexpr int kClusterMinBlocks = 4;  // blocks per CTA below which no extra cluster is added
+
+// One CTA per SM at most.  Segment-aligned when there are at least as many
+// CTAs as segments.  Launches too small to give every SM two blocks (the
+// sliding-window layers) merge in thread-block clusters instead, when every
+// segment can have a whole cluster resident at once: clusters of
+// kClusterCtas CTAs merge the segment's partials in distributed shared
+// memory -- k clusters per segment, as many as fit (each CTA keeping
+// kClusterMinBlocks blocks or more).  On larger launches clusters measured
+// slower (cfg2 step 0.88 -> 1.43 ms): a cluster starts only once kClusterCtas
+// SMs of one GPC are free, which defeats the overlap of back-to-back
+// launches.
+inline UniformPlan plan_uniform(long long NB, int S, int nblk, int sms, int clusters_resident) {
+  UniformPlan p;
+  p.grid = (int)(NB < sms ? NB : sms);
+  p.aligned = p.grid >= S ? 1 : 0;
+  const int C = kClusterCtas;
+  if (NB < 2LL * sms && clusters_resident >= S && S * C <= sms && nblk >= C) {
+    int k = clusters_resident / S;
+    if (k > sms / (S * C)) k = sms / (S * C);
+    const int by_work = nblk / (C * kClusterMinBlocks);
+    if (k > by_work) k = by_work > 1 ? by_work : 1;
+    if (k >= 1 && nblk >= C * k) {
+      p.grid = S * k * C;
+      p.aligned = 1;
+      p.cluster = C;
+      p.cl_per_seg = k;
+    }
+  }
+  return p;
+}
+
 }  // namespace molot

@@ -164,10 +164,15 @@ extern "C" int molot_attn_decode_strided_noalloc(const float* Q, const float* K,
   const int blo = t0 / kBlk;
   const int nblk = (n + kBlk - 1) / kBlk - blo;
   const long long NB = (long long)nkv * nblk;
-  int grid = sms < kNoAllocMaxGrid ? sms : kNoAllocMaxGrid;
-  if (NB < grid) grid = (int)NB;
   if (partial_record_floats(G, d) > kNoAllocMaxRecord)
     return set_last_error(MOLOT_ERR_UNSUPPORTED, "partial record exceeds the no-alloc scratch");
+  e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
+  if (e != cudaSuccess) return cuda_err(e, "cudaFuncSetAttribute");
+  // The partition of molot_attn_decode_strided_dev (at most kNoAllocMaxGrid
+  // CTAs, which covers one per SM of a B200).
+  const UniformPlan up = plan_uniform(NB, nkv, nblk, sms < kNoAllocMaxGrid ? sms : kNoAllocMaxGrid,
+                                      max_active_clusters(k, kClusterCtas, dev));
+  const int grid = up.grid;
 
   float* partials = reinterpret_cast<float*>(scratch);
   int* counters = reinterpret_cast<int*>(scratch + kNoAllocPartialBytes);
@@ -177,10 +182,9 @@ extern "C" int molot_attn_decode_strided_noalloc(const float* Q, const float* K,
   // molot_noalloc_status to report.
   e = cudaMemsetAsync(counters, 0, kNoAllocCounterBytes, st);
   if (e != cudaSuccess) return cuda_err(e, "cudaMemsetAsync(no-alloc tickets)");
-  // The partition and kernel variant of molot_attn_decode_strided_dev: one
-  // segment per CTA when there are at least as many CTAs as kv heads, and
-  // the split K/V stage barriers for long FP32 launches at head_dim <= 128.
-  const int aligned = grid >= nkv ? 1 : 0;
+  // The kernel variant of molot_attn_decode_strided_dev: split K/V stage
+  // barriers for long FP32 launches at head_dim <= 128.
+  const int aligned = up.aligned;
   {
     const int tile_rows = d <= 64 ? TileShape<64, float>::T : TileShape<128, float>::T;
     const long long rows_per_cta = (long long)nblk * kBlk * nkv / grid;
@@ -215,18 +219,24 @@ extern "C" int molot_attn_decode_strided_noalloc(const float* Q, const float* K,
   a.timeout_ns = 2000000000ull;
   a.grid = grid;
   a.aligned = aligned;
+  a.cluster = up.cluster;
+  a.cl_per_seg = up.cl_per_seg;
   a.prefetch_old_rows = 0;  // the caller's K/V may come from the preceding launch
   take_withhold(a);
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = up.cluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kDecodeThreads);
   cfg.dynamicSmemBytes = k.smem;
   cfg.stream = st;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = up.cluster > 1 ? 2 : 1;
   void* args[] = {&a};
   e = cudaLaunchKernelExC(&cfg, k.fn, args);
   return e == cudaSuccess ? MOLOT_OK : cuda_err(e, "launch (no-alloc decode)");

@@ -33,7 +33,7 @@ struct molot_pager {
   size_t pool_bytes = 0;           // per K (or V) pool of one layer
   int kvt = MOLOT_KV_F32;
   int device = -1;
-  std::mutex mu;
+  mutable std::mutex mu;  // every call, queries included
 };
 
 namespace {
@@ -172,13 +172,16 @@ int molot_pager_free(molot_pager* p, int seq) {
 }
 
 int molot_pager_length(const molot_pager* p, int seq) {
-  if (!p || seq < 0 || seq >= p->max_seqs || !p->live[seq])
+  if (!p) return pager_fail(MOLOT_ERR_INVALID, "null pager");
+  std::lock_guard<std::mutex> lk(p->mu);
+  if (seq < 0 || seq >= p->max_seqs || !p->live[seq])
     return pager_fail(MOLOT_ERR_INVALID, "bad sequence");
   return p->len[seq];
 }
 
 int molot_pager_free_pages(const molot_pager* p) {
   if (!p) return pager_fail(MOLOT_ERR_INVALID, "null pager");
+  std::lock_guard<std::mutex> lk(p->mu);
   return (int)p->free_pages.size();
 }
 

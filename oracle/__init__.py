@@ -25,7 +25,35 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_SO = os.path.join(HERE, "_build", "libmolot_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libmolot_ref.so")
-REF_TREE = os.environ.get("MOLOT_REFERENCE_TREE", "/root/reference")
+
+
+def _reference_tree() -> str | None:
+    """Root of the reference's source tree: MOLOT_REFERENCE_TREE, else the
+    reference_path that BASELINE.json records for this repository; None
+    when neither names an existing tree (then only the port is built and
+    ref() is None)."""
+    cand = os.environ.get("MOLOT_REFERENCE_TREE")
+    if not cand:
+        try:
+            import json
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as fh:
+                cand = json.load(fh).get("reference_path")
+        except (OSError, ValueError):
+            cand = None
+    if cand and os.path.isfile(os.path.join(cand, "include", "molot", "attn.h")):
+        return cand
+    return None
+
+
+REF_TREE = _reference_tree()
+
+
+def require_reference_tree() -> str:
+    """The reference tree, or a clear error naming how to point at it."""
+    if REF_TREE is None:
+        raise RuntimeError("reference source tree not found: set MOLOT_REFERENCE_TREE to the "
+                           "directory holding include/molot/attn.h")
+    return REF_TREE
 
 _f = ctypes.c_float
 _i = ctypes.c_int
@@ -45,9 +73,11 @@ def build(with_ref: bool | None = None) -> None:
     # The image's default CC/CXX wrapper is fine for both targets; make them
     # explicit so a stray environment cannot change the flags' meaning.
     targets = ["port"]
-    if with_ref or (with_ref is None and os.path.isfile(os.path.join(REF_TREE, "include", "molot", "attn.h"))):
+    cmd = ["make", "-s", "-C", HERE]
+    if with_ref or (with_ref is None and REF_TREE is not None):
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", HERE, f"REF={REF_TREE}"] + targets, check=True, env=env)
+        cmd.append(f"REF={require_reference_tree()}")
+    subprocess.run(cmd + targets, check=True, env=env)
 
 
 def host_has_avx512() -> bool:
@@ -106,7 +136,7 @@ def ref():
     global _ref, _ref_checked
     if not _ref_checked:
         _ref_checked = True
-        if os.path.isfile(PORT_SO) and not os.path.isfile(REF_SO) and os.path.isdir(REF_TREE):
+        if os.path.isfile(PORT_SO) and not os.path.isfile(REF_SO) and REF_TREE is not None:
             try:
                 build(with_ref=True)
             except subprocess.CalledProcessError:
