@@ -193,7 +193,7 @@ def prefill_flops(cfg):
     return 4 * cfg["nq"] * cfg["d"] * pairs
 
 
-PREFILL_METRIC = "prefill attention TFLOP/s (FP32), 4096-token prompt"
+PREFILL_METRIC = "prefill attention TFLOP/s (FP32 results), 4096-token prompt"
 
 
 GEMV_METRIC = "Q4 projection GEMV GB/s (weights streamed per decode token)"
@@ -1033,9 +1033,25 @@ def run_prefill(args, cfg):
     del graph, agraph
     metric, unit, amount, div = step_work(cfg)
     flops_layer = prefill_flops(cfg)
-    # nominal FP32 CUDA-core peak (no measured FP32 figure exists for this pool)
+    # FP32 caches at head_dim 64/128 run the split-TF32 tensor-core kernel:
+    # its ceiling is the TF32 tensor rate (half the measured bf16 GEMM rate)
+    # over the three TF32 products each FP32 product takes.  Other caches
+    # run the FP32 CUDA-core kernel: nominal FP32 peak (no measured figure).
+    tc_path = args.kv == "f32" and cfg["d"] in (64, 128)
     sm_count = torch.cuda.get_device_properties(rt.dev).multi_processor_count
-    peak = sm_count * 128 * 2 * 1.965e9 / 1e12
+    if tc_path:
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+                bf16 = float(json.load(fh)["bf16_tflops"])
+            peak_src = (f"measured bf16_tflops {bf16:.1f} / 2 (TF32 rate) / 3 (TF32 products per "
+                        "FP32 product)")
+        except Exception:
+            bf16 = 1590.0
+            peak_src = "fallback bf16 1590 TFLOP/s / 2 (TF32 rate) / 3 (products per FP32 product)"
+        peak = bf16 / 2 / 3
+    else:
+        peak = sm_count * 128 * 2 * 1.965e9 / 1e12
+        peak_src = "nominal FP32 CUDA-core peak (SMs x 128 lanes x 2 x 1965 MHz); no measured FP32 figure"
     if rt.rank == 0:
         value = amount * rt.world / (ms * 1e-3) / div
         line = {
@@ -1053,12 +1069,14 @@ def run_prefill(args, cfg):
                     "h2d_bytes_per_step": int(4 * (q_raw.numel() + k_raw.numel() + v_raw.numel())),
                     "d2h_bytes_per_step": int(4 * out.numel()), "ms_per_step": round(e2e_ms, 3)},
             "gpu_launches": 2 * L * args.steps,
-            "roofline": {"bound": "fp32", "achieved": round(flops_layer / (attn_ms * 1e-3) / 1e12, 2),
+            "roofline": {"bound": "tensor" if tc_path else "fp32",
+                         "achieved": round(flops_layer / (attn_ms * 1e-3) / 1e12, 2),
                          "peak": round(peak, 1), "unit": "TFLOP/s",
                          "frac": round(flops_layer / (attn_ms * 1e-3) / 1e12 / peak, 4),
-                         "traffic": None, "kernel": "gqa_prefill_kernel<128>",
-                         "peak_source": "nominal FP32 CUDA-core peak (SMs x 128 lanes x 2 x "
-                                        "1965 MHz); no measured FP32 figure",
+                         "traffic": None,
+                         "kernel": ("gqa_prefill_tc_kernel<%d> (split TF32, tcgen05)" % cfg["d"]
+                                    if tc_path else "gqa_prefill_kernel<%d>" % cfg["d"]),
+                         "peak_source": peak_src,
                          "flops_per_launch": flops_layer, "avg_launch_ms": round(attn_ms, 4)},
             "clocks": clk,
             "path": "molot_attn_append_rope_tokens + molot_attn_prefill per layer",

@@ -18,6 +18,7 @@
 #include "gemv.cuh"
 #include "molot_b200.h"
 #include "prefill.cuh"
+#include "prefill_tc.cuh"
 
 namespace molot {
 
@@ -464,6 +465,11 @@ int prefill_strided(Workspace& ws, const float* Q, long long q_tstride, float* O
   int dev, rc;
   if ((rc = current_device(&dev))) return rc;
   if ((rc = ws.ensure(dev, 0, 0, 0))) return rc;
+  // FP32 caches at head_dim 64/128: the split-TF32 tensor-core kernel
+  // (128 query rows per CTA, so the group size must divide 128).
+  KernelRef ktc;
+  const bool tc = kvt == MOLOT_KV_F32 && kTcRows % G == 0 && pick_prefill_tc(d, &ktc);
+  if (tc) k = ktc;
   if ((rc = prepare_kernel(k, dev))) return rc;
   PrefillArgs a = {};
   a.Q = Q;
@@ -482,11 +488,12 @@ int prefill_strided(Workspace& ws, const float* Q, long long q_tstride, float* O
   a.pos0 = pos0;
   a.window = window;
   a.scale = scale;
-  a.BP = kPrefillRows / G;
+  a.BP = (tc ? kTcRows : kPrefillRows) / G;
   a.nblk_m = (M + a.BP - 1) / a.BP;
   a.status = ws.status;
   a.timeout_ns = kWaitLimitNs;
-  return launch(k.fn, dim3(a.nblk_m, nkv), dim3(kPrefillThreads), k.smem, st, &a);
+  return launch(k.fn, dim3(a.nblk_m, nkv), dim3(tc ? kTcThreads : kPrefillThreads), k.smem, st,
+                &a);
 }
 
 // Host drop-in: stage Qm / K / V, run, copy Om back.

@@ -20,6 +20,8 @@ bool pick_decode_bf16(int D, int G, KernelRef* k);
 bool pick_decode_q8(int D, int G, KernelRef* k);
 // gqa_prefill_kernel for a head_dim and a storage type.
 bool pick_prefill_kv(int D, int kvt, KernelRef* k);
+// gqa_prefill_tc_kernel (split-TF32 tcgen05; FP32 caches, head_dim 64/128).
+bool pick_prefill_tc(int D, KernelRef* k);
 
 // Thread-block clusters of this many CTAs that kernel k can keep resident
 // at once on device dev (cached; 0 when the query fails).

@@ -2,6 +2,7 @@
 #include "dispatch.cuh"
 #include "molot_b200.h"
 #include "prefill.cuh"
+#include "prefill_tc.cuh"
 
 namespace molot {
 namespace {
@@ -20,6 +21,18 @@ bool pick(int D, KernelRef* k) {
   return false;
 }
 }  // namespace
+
+bool pick_prefill_tc(int D, KernelRef* k) {
+  switch (D) {
+    case 64:
+      *k = {reinterpret_cast<const void*>(&gqa_prefill_tc_kernel<64>), TcShape<64>::kTotal};
+      return true;
+    case 128:
+      *k = {reinterpret_cast<const void*>(&gqa_prefill_tc_kernel<128>), TcShape<128>::kTotal};
+      return true;
+  }
+  return false;
+}
 
 bool pick_prefill_kv(int D, int kvt, KernelRef* k) {
   switch (kvt) {

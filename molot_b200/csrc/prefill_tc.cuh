@@ -1,0 +1,469 @@
+// Causal / sliding-window GQA prefill attention on the 5th-generation tensor
+// cores (tcgen05), for FP32 caches at head_dim 64 and 128: the same
+// contract as gqa_prefill_kernel (gemm.h:409-446, attn_prefill_gqa at
+// forward.h:396) within the 1e-5 bar.
+//
+// Precision: split TF32.  Every FP32 operand x is split into hi =
+// round-to-nearest TF32 of x and lo = x - hi (exact in FP32, |lo| <=
+// 2^-11 |x|), and each product is formed as hi*hi + hi*lo + lo*hi by three
+// TF32 MMAs accumulating in FP32 (the dropped lo*lo term is ~2^-22 of the
+// product).  S = Q K^T and O = P V both run this way.
+//
+// CTA: one kv head x 128 query rows (row r = position (r / G) of the block,
+// head (r % G) of the kv head's group), the MMA's M.  Tensor memory (512
+// columns, all of the SM's): Q hi / lo (the A operand of S, D columns each),
+// two S buffers (BN columns each), P hi / lo (the A operand of O), the O
+// accumulator (D columns); a thread of the softmax warpgroup owns its row's
+// lane, so row maxima and sums never leave the thread.
+// Warps:
+//   0-3  softmax: Q row -> TMEM (split), then per key tile: S row from TMEM,
+//        scale, causal / window mask, lazy online softmax in base 2 (the
+//        running max rises only when a score exceeds it by 2^8; O is then
+//        rescaled in TMEM), P -> TMEM (split); at the end O / l -> global.
+//   4-7  converters: per key tile, K and V rows from global (L2-resident
+//        across the query blocks), split, into shared memory in the
+//        no-swizzle K-major core-matrix layout the MMA reads (K as
+//        [key][dim], V transposed as [dim][key]); 3 stages.
+//   8    lane 0 issues every MMA and commit.
+// Barriers (all waits bounded; a wait that runs out records a status code,
+// raises the abort flag and the CTA winds down without further MMAs):
+//   kv_full / kv_empty per stage, s_full / s_free per S buffer, p_full,
+//   pv_done, q_ready, done (the last commit, before TMEM is freed).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <math_constants.h>
+
+#include <cstdint>
+
+#include "prefill.cuh"
+#include "ptx.cuh"
+
+namespace molot {
+
+constexpr int kTcRows = 128;   // query rows per CTA (MMA M)
+constexpr int kTcBN = 32;      // keys per tile
+constexpr int kTcStages = 3;   // K/V tile stages
+constexpr int kTcThreads = 9 * 32;
+constexpr int kTcTmemCols = 512;
+
+template <int D>
+struct TcShape {
+  static_assert(D == 64 || D == 128, "tensor-core prefill: head_dim 64 or 128");
+  static constexpr int kTile = kTcBN * D * 4;     // one hi or lo K tile (bytes)
+  // V tiles are transposed with a 16-byte gap after each 4-key chunk
+  // (leading byte offset D*16 + 16), so the 8 chunks a warp's stores span
+  // fall on different banks.
+  static constexpr int kVChunk = D * 16 + 16;
+  static constexpr int kVTile = (kTcBN / 4) * kVChunk;
+  static constexpr int kStage = 2 * kTile + 2 * kVTile;  // K hi, K lo, V hi, V lo
+  static constexpr int kBarOff = kTcStages * kStage;
+  static constexpr int kBars = 2 * kTcStages + 4 + 4;  // kv_full/empty, s_full/free x2, p, pv, q, done
+  // Over half of the SM's shared memory, so a second CTA (which would wait
+  // in tcgen05.alloc for the first one's 512 columns) never shares the SM.
+  static constexpr int kUsed = kBarOff + kBars * 8 + 32;
+  static constexpr int kTotal = kUsed > 116 * 1024 ? kUsed : 116 * 1024;
+  // tensor-memory columns
+  static constexpr uint32_t kQhi = 0, kQlo = D, kS = 2 * D, kPhi = 2 * D + 2 * kTcBN,
+                            kPlo = kPhi + kTcBN, kO = kPlo + kTcBN;
+  static_assert(kO + D <= kTcTmemCols, "tensor memory columns");
+  static_assert(kTotal <= 227 * 1024, "shared memory");
+  // K tile, K-major B of S (N = keys, K = dims): core matrix = 8 keys x 4 dims
+  __device__ static int k_off(int key, int dim) {
+    return (dim >> 2) * (kTcBN * 16) + (key >> 3) * 128 + (key & 7) * 16 + (dim & 3) * 4;
+  }
+  // V tile transposed, K-major B of O (N = dims, K = keys): 8 dims x 4 keys
+  __device__ static int v_off(int key, int dim) {
+    return (key >> 2) * kVChunk + (dim >> 3) * 128 + (dim & 7) * 16 + (key & 3) * 4;
+  }
+};
+
+namespace tc {
+
+__device__ __forceinline__ float tf32_hi(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// Shared-memory matrix descriptor, no swizzle (sm_100 layout: start, leading
+// and stride byte offsets in 16-byte units, version 1).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((addr >> 4) & 0x3fff) | ((uint64_t)((lbo >> 4) & 0x3fff) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3fff) << 32) | (1ull << 46);
+}
+// Instruction descriptor: TF32 x TF32 -> F32, both K-major, M = 128.
+__host__ __device__ constexpr uint32_t idesc(int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(kTcRows >> 4) << 24);
+}
+// D[tmem] (+)= A[tmem] * B[smem desc]
+__device__ __forceinline__ void mma(uint32_t d, uint32_t a, uint64_t b, uint32_t id, int acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(b), "r"(id), "r"(acc), "r"(0u));
+}
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   ptx::smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// 16 columns of this thread's lane, starting at addr.
+__device__ __forceinline__ void ld16(uint32_t addr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(addr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void st16(uint32_t addr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(addr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+__device__ __forceinline__ void wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+}  // namespace tc
+
+// Waits for `bar` to complete phase `par`, bounded by a.timeout_ns; on
+// timeout records `code` and raises the abort flag.  Skipped once aborted.
+__device__ __forceinline__ void tc_wait(uint64_t* bar, uint32_t par, const PrefillArgs& a,
+                                        volatile int* abort_flag, int code) {
+  if (*abort_flag) return;
+  if (!ptx::mbar_wait_bounded(bar, par, a.timeout_ns)) {
+    *abort_flag = 1;
+    atomicCAS(a.status, 0, code);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gqa_prefill_tc_kernel(const __grid_constant__ PrefillArgs a) {
+  using TS = TcShape<D>;
+  constexpr int BN = kTcBN;
+  constexpr float kLog2e = 1.4426950408889634f;
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TS::kBarOff);
+  uint64_t* kv_full = bars;
+  uint64_t* kv_empty = bars + kTcStages;
+  uint64_t* s_full = bars + 2 * kTcStages;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_full + 4;
+  uint64_t* pv_done = p_full + 1;
+  uint64_t* q_ready = p_full + 2;
+  uint64_t* done_bar = p_full + 3;
+  volatile uint32_t* tmem_sm = reinterpret_cast<volatile uint32_t*>(bars + TS::kBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + TS::kBars) + 1;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = blockIdx.y;
+  const int mb = a.nblk_m - 1 - blockIdx.x;  // latest (longest) query blocks first
+  const int G = a.G;
+  const int BP = kTcRows / G;  // query positions per CTA
+  const int m0 = mb * BP;
+  // Keys the CTA attends: from the first position's window start to the
+  // last position's causal end (capped at N).
+  const int m_last = min(m0 + BP, a.M) - 1;
+  const int pos_first = a.pos0 + m0, pos_last = a.pos0 + m_last;
+  const int lo_key = a.window > 0 ? max(0, pos_first - a.window + 1) : 0;
+  const int hi_key = min(pos_last + 1, a.N);
+  const int kt0 = (lo_key / BN) * BN;
+  const int ntiles = hi_key > kt0 ? (hi_key - kt0 + BN - 1) / BN : 0;
+
+  if (tid == 0) {
+    for (int i = 0; i < kTcStages; ++i) {
+      ptx::mbar_init(kv_full + i, 128);
+      ptx::mbar_init(kv_empty + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(s_full + i, 1);
+      ptx::mbar_init(s_free + i, 128);
+    }
+    ptx::mbar_init(p_full, 128);
+    ptx::mbar_init(pv_done, 1);
+    ptx::mbar_init(q_ready, 128);
+    ptx::mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     ptx::smem_u32(const_cast<uint32_t*>(tmem_sm))),
+                 "r"(kTcTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t T = *tmem_sm;
+  // Q and the cache rows may come from the preceding launch.
+  ptx::pdl_wait();
+  if (tid == 0) ptx::pdl_launch_dependents();
+
+  if (warp < 4) {
+    // ------------------------------------------------------------ softmax
+    const int r = tid;  // this thread's row == TMEM lane
+    const uint32_t lane_base = T + ((uint32_t)(warp * 32) << 16);
+    const int pl = r / G, h = r - pl * G;
+    const int m = m0 + pl;
+    const bool valid = pl < BP && m < a.M;
+    const int pos = a.pos0 + m;
+    const int t_hi = valid ? min(pos + 1, a.N) : 0;  // attended [t_lo, t_hi)
+    const int t_lo = a.window > 0 ? max(0, pos - a.window + 1) : 0;
+    const float* qrow = a.Q + (long long)m * a.q_tstride + (long long)(g * G + h) * D;
+    {
+      float hi[16], lo[16];
+#pragma unroll 1
+      for (int c = 0; c < D; c += 16) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const float4 x = valid ? *reinterpret_cast<const float4*>(qrow + c + i)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+          hi[i] = tc::tf32_hi(x.x);
+          hi[i + 1] = tc::tf32_hi(x.y);
+          hi[i + 2] = tc::tf32_hi(x.z);
+          hi[i + 3] = tc::tf32_hi(x.w);
+          lo[i] = x.x - hi[i];
+          lo[i + 1] = x.y - hi[i + 1];
+          lo[i + 2] = x.z - hi[i + 2];
+          lo[i + 3] = x.w - hi[i + 3];
+        }
+        tc::st16(lane_base + TS::kQhi + c, hi);
+        tc::st16(lane_base + TS::kQlo + c, lo);
+      }
+      tc::wait_st();
+      tc::fence_before();
+      ptx::mbar_arrive(q_ready);
+    }
+    const float sl2 = a.scale * kLog2e;
+    float mrow = -CUDART_INF_F, lrow = 0.f;
+#pragma unroll 1
+    for (int j = 0; j < ntiles; ++j) {
+      const int sb = j & 1;
+      tc_wait(s_full + sb, (j >> 1) & 1, a, abort_flag, 1);
+      __syncwarp();  // lanes leave the wait loop on their own; tcgen05.ld is warp-collective
+      tc::fence_after();
+      float s[BN];
+      tc::ld16(lane_base + TS::kS + sb * BN, s);
+      tc::ld16(lane_base + TS::kS + sb * BN + 16, s + 16);
+      tc::fence_before();
+      ptx::mbar_arrive(s_free + sb);
+      const int key0 = kt0 + j * BN;
+      float mc = -CUDART_INF_F;
+#pragma unroll
+      for (int i = 0; i < BN; ++i) {
+        const int t = key0 + i;
+        s[i] = (t >= t_lo && t < t_hi) ? s[i] * sl2 : -CUDART_INF_F;
+        mc = fmaxf(mc, s[i]);
+      }
+      // P and O may be touched once the previous tile's P V has completed.
+      if (j > 0) {
+        tc_wait(pv_done, (j - 1) & 1, a, abort_flag, 2);
+        __syncwarp();
+        tc::fence_after();
+      }
+      // Lazy rescale: the running max rises only when a score exceeds it
+      // by 2^8 (or is the row's first finite one).  tcgen05.ld / st are
+      // warp-collective, so when any row of the warp must rescale O the
+      // whole warp does it, the other rows with a factor of 1.
+      const bool raise = mc > mrow + 8.f;
+      const bool scale_o = raise && j > 0 && lrow > 0.f;
+      if (__any_sync(0xffffffffu, scale_o)) {
+        const float alpha = scale_o ? prefill_ex2(mrow - mc) : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < D; c += 16) {
+          float o[16];
+          tc::ld16(lane_base + TS::kO + c, o);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] *= alpha;
+          tc::st16(lane_base + TS::kO + c, o);
+        }
+        lrow *= alpha;
+      }
+      if (raise) mrow = mc;
+      float hi[BN], lo[BN];
+#pragma unroll
+      for (int i = 0; i < BN; ++i) {
+        const float p = (s[i] == -CUDART_INF_F) ? 0.f : prefill_ex2(s[i] - mrow);
+        lrow += p;
+        hi[i] = tc::tf32_hi(p);
+        lo[i] = p - hi[i];
+      }
+      tc::st16(lane_base + TS::kPhi, hi);
+      tc::st16(lane_base + TS::kPhi + 16, hi + 16);
+      tc::st16(lane_base + TS::kPlo, lo);
+      tc::st16(lane_base + TS::kPlo + 16, lo + 16);
+      tc::wait_st();
+      tc::fence_before();
+      ptx::mbar_arrive(p_full);
+    }
+    if (ntiles > 0) {
+      tc_wait(pv_done, (ntiles - 1) & 1, a, abort_flag, 2);
+      __syncwarp();
+      tc::fence_after();
+    }
+    // Every lane of the warp reads O (warp-collective); valid rows store.
+    float* orow = a.O + (long long)m * a.o_tstride + (long long)(g * G + h) * D;
+    const float inv = lrow > 0.f ? 1.f / lrow : 0.f;  // an empty range gives zeros
+#pragma unroll 1
+    for (int c = 0; c < D; c += 16) {
+      float o[16];
+      if (ntiles > 0) {
+        tc::ld16(lane_base + TS::kO + c, o);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = 0.f;
+      }
+      if (valid) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 4)
+          *reinterpret_cast<float4*>(orow + c + i) =
+              make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+      }
+    }
+  } else if (warp < 8) {
+    // ---------------------------------------------------------- converters
+    const int ct = tid - 128;
+    const float* Kb = static_cast<const float*>(a.K) + (long long)g * a.stride_h;
+    const float* Vb = static_cast<const float*>(a.V) + (long long)g * a.stride_h;
+    constexpr int NI = BN * D / 4 / 128;
+#pragma unroll 1
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j % kTcStages;
+      if (j >= kTcStages) tc_wait(kv_empty + st, ((j / kTcStages) - 1) & 1, a, abort_flag, 3);
+      if (!*abort_flag) {
+        unsigned char* base = smem + st * TS::kStage;
+        unsigned char* khi = base;
+        unsigned char* klo = base + TS::kTile;
+        unsigned char* vhi = base + 2 * TS::kTile;
+        unsigned char* vlo = base + 2 * TS::kTile + TS::kVTile;
+        const int key0 = kt0 + j * BN;
+        // Every load of the tile is issued before the first store: thread
+        // ct takes key (ct % 32) of the 4-dim chunks ct/32 + 4i, so a
+        // warp's K stores are one contiguous 512-byte run.
+        float4 kx[NI], vx[NI];
+#pragma unroll
+        for (int i = 0; i < NI; ++i) {
+          const int f = ct + i * 128;
+          const int t = key0 + f % BN;
+          const long long row = (long long)t * a.stride_t + 4 * (f / BN);
+          kx[i] = t < a.N ? *reinterpret_cast<const float4*>(Kb + row) : make_float4(0.f, 0.f, 0.f, 0.f);
+          vx[i] = t < a.N ? *reinterpret_cast<const float4*>(Vb + row) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int i = 0; i < NI; ++i) {
+          const int f = ct + i * 128;
+          const int key = f % BN, c4 = f / BN;
+          const float4 x = kx[i];
+          float4 h, l;
+          h.x = tc::tf32_hi(x.x);
+          h.y = tc::tf32_hi(x.y);
+          h.z = tc::tf32_hi(x.z);
+          h.w = tc::tf32_hi(x.w);
+          l.x = x.x - h.x;
+          l.y = x.y - h.y;
+          l.z = x.z - h.z;
+          l.w = x.w - h.w;
+          const int off = TS::k_off(key, 4 * c4);
+          *reinterpret_cast<float4*>(khi + off) = h;
+          *reinterpret_cast<float4*>(klo + off) = l;
+          const float v4[4] = {vx[i].x, vx[i].y, vx[i].z, vx[i].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float vh = tc::tf32_hi(v4[e]);
+            const int vo = TS::v_off(key, 4 * c4 + e);
+            *reinterpret_cast<float*>(vhi + vo) = vh;
+            *reinterpret_cast<float*>(vlo + vo) = v4[e] - vh;
+          }
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      ptx::mbar_arrive(kv_full + st);
+    }
+  } else if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t ids = tc::idesc(BN), ido = tc::idesc(D);
+    tc_wait(q_ready, 0, a, abort_flag, 4);
+    tc::fence_after();
+#pragma unroll 1
+    for (int j = 0; j <= ntiles; ++j) {
+      if (j < ntiles) {
+        const int st = j % kTcStages, sb = j & 1;
+        tc_wait(kv_full + st, (j / kTcStages) & 1, a, abort_flag, 4);
+        if (j >= 2) tc_wait(s_free + sb, ((j >> 1) - 1) & 1, a, abort_flag, 4);
+        tc::fence_after();
+        if (!*abort_flag) {
+          const uint32_t kb = ptx::smem_u32(smem + st * TS::kStage);
+          const uint32_t d = T + TS::kS + sb * BN;
+#pragma unroll 1
+          for (int s = 0; s < D / 8; ++s) {  // S = Qh Kh + Qh Kl + Ql Kh over dims 8s..8s+7
+            const uint32_t off = 2 * s * (BN * 16);
+            const uint64_t bh = tc::sdesc(kb + off, BN * 16, 128);
+            const uint64_t bl = tc::sdesc(kb + TS::kTile + off, BN * 16, 128);
+            tc::mma(d, T + TS::kQhi + 8 * s, bh, ids, s > 0);
+            tc::mma(d, T + TS::kQhi + 8 * s, bl, ids, 1);
+            tc::mma(d, T + TS::kQlo + 8 * s, bh, ids, 1);
+          }
+        }
+        tc::commit(s_full + sb);
+      }
+      if (j >= 1) {
+        const int jp = j - 1, st = jp % kTcStages;
+        tc_wait(p_full, jp & 1, a, abort_flag, 4);
+        tc::fence_after();
+        if (!*abort_flag) {
+          const uint32_t vb = ptx::smem_u32(smem + st * TS::kStage + 2 * TS::kTile);
+#pragma unroll 1
+          for (int s = 0; s < BN / 8; ++s) {  // O += Ph Vh + Ph Vl + Pl Vh over keys 8s..8s+7
+            const uint32_t off = 2 * s * TS::kVChunk;
+            const uint64_t bh = tc::sdesc(vb + off, TS::kVChunk, 128);
+            const uint64_t bl = tc::sdesc(vb + TS::kVTile + off, TS::kVChunk, 128);
+            tc::mma(T + TS::kO, T + TS::kPhi + 8 * s, bh, ido, (jp > 0 || s > 0) ? 1 : 0);
+            tc::mma(T + TS::kO, T + TS::kPhi + 8 * s, bl, ido, 1);
+            tc::mma(T + TS::kO, T + TS::kPlo + 8 * s, bh, ido, 1);
+          }
+        }
+        tc::commit(pv_done);
+        tc::commit(kv_empty + st);
+      }
+    }
+    tc::commit(done_bar);  // arrives once every MMA above has completed
+  }
+
+  // Tensor memory is freed by the warp that allocated it, after every MMA
+  // (done_bar) and every thread's tensor-memory access (the CTA barrier).
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    if (!ptx::mbar_wait_bounded(done_bar, 0, a.timeout_ns) && lane == 0)
+      atomicCAS(a.status, 0, 5);
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(T),
+                 "r"(kTcTmemCols));
+  }
+}
+
+}  // namespace molot

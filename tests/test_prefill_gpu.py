@@ -35,6 +35,8 @@ def test_prefill_host_dropin_against_reference_golden(mb, torch_cuda, orc):
     (64, 8, 128, 33, 20, 0, 0),       # G = 8 (Llama-70B shape)
     (8, 2, 128, 40, 30, -25, 0),      # cache shorter than the positions (nn = N)
     (8, 2, 128, 1, 63, 0, 0),         # one token
+    (32, 8, 128, 600, 200, 0, 256),   # many key tiles, window spanning tiles (tensor-core path)
+    (16, 4, 64, 257, 1000, -200, 0),  # head_dim 64, ragged last query block, nn = N
 ])
 def test_prefill_strided_against_oracle(mb, torch_cuda, orc, nq, nkv, d, M, pos0, N_extra,
                                         window):
