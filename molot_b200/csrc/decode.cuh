@@ -551,32 +551,22 @@ __device__ __forceinline__ void process_rows(const KT* kr, const KT* vr, int tok
 // Fused step, launch constants: cos/sin of the RoPE angles pos*freq[i]
 // (tab[i], tab[D/2+i]) and the q_norm / k_norm weights (tab[D+i],
 // tab[2D+i]), staged in shared memory once per CTA by the 256 consumer
-// threads (the caller's named barrier publishes them).  When `raw` is
-// non-null the raw k row `kx` ([D]) and all nkv*D raw v values are staged
-// there too (raw[0..D), raw[D..D+nkv*D)), for the new-row build.  Every
-// global load is issued before the first dependent operation, so the whole
-// prologue costs one memory round trip.  forward.h:562-575 computes the same
-// values per row.
+// threads (the caller's named barrier publishes them).  They depend only on
+// the launch's arguments and the layer's weights, never on the preceding
+// kernel, so the consumers build them before the dependency wait, while the
+// preceding launch drains.  forward.h:562-575 computes the same values per
+// row.
 template <int D>
-__device__ __forceinline__ void fused_fill_tables(const DecodeArgs& a, float* tab, int ctid,
-                                                  float* raw, const float* kx) {
+__device__ __forceinline__ void fused_fill_tables(const DecodeArgs& a, float* tab, int ctid) {
   constexpr int NT = kConsumerWarps * 32;
   constexpr int IT = (D + NT - 1) / NT;
-  constexpr int kMaxV = kMaxStagedV / NT;
-  float f[IT], wq[IT], wk[IT], kr[IT], vv[kMaxV];
-  const int nv = a.nkv * D;
+  float f[IT], wq[IT], wk[IT];
 #pragma unroll
   for (int r = 0; r < IT; ++r) {
     const int i = ctid + r * NT;
     f[r] = (i < D / 2 && a.freq) ? ptx::ld_nc_issue(a.freq + i) : 0.f;
     wq[r] = (i < D && a.q_norm) ? ptx::ld_nc_issue(a.q_norm + i) : 0.f;
     wk[r] = (i < D && a.k_norm) ? ptx::ld_nc_issue(a.k_norm + i) : 0.f;
-    kr[r] = (i < D && raw) ? ptx::ld_nc_issue(kx + i) : 0.f;
-  }
-#pragma unroll
-  for (int r = 0; r < kMaxV; ++r) {
-    const int j = ctid + r * NT;
-    vv[r] = (raw && j < nv) ? ptx::ld_nc_issue(a.v_raw + j) : 0.f;
   }
 #pragma unroll
   for (int r = 0; r < IT; ++r) {
@@ -590,15 +580,42 @@ __device__ __forceinline__ void fused_fill_tables(const DecodeArgs& a, float* ta
     if (i < D) {
       tab[D + i] = wq[r];
       tab[2 * D + i] = wk[r];
-      if (raw) raw[i] = kr[r];
     }
   }
-  if (raw) {
+}
+
+// Fused step, the new token's raw rows for the CTA that builds it: the raw
+// k row `kx` ([D]) and all nkv*D raw v values go to raw[0..D) and
+// raw[D..D+nkv*D) (the caller's named barrier publishes them).  They are
+// the preceding kernel's outputs, so this runs after the dependency wait;
+// every load is issued before the first store.
+template <int D>
+__device__ __forceinline__ void fused_stage_raw(const DecodeArgs& a, float* raw, int ctid,
+                                                const float* kx) {
+  constexpr int NT = kConsumerWarps * 32;
+  constexpr int IT = (D + NT - 1) / NT;
+  constexpr int kMaxV = kMaxStagedV / NT;
+  float kr[IT], vv[kMaxV];
+  const int nv = a.nkv * D;
 #pragma unroll
-    for (int r = 0; r < kMaxV; ++r) {
-      const int j = ctid + r * NT;
-      if (j < nv) raw[D + j] = vv[r];
-    }
+  for (int r = 0; r < IT; ++r) {
+    const int i = ctid + r * NT;
+    kr[r] = i < D ? ptx::ld_nc_issue(kx + i) : 0.f;
+  }
+#pragma unroll
+  for (int r = 0; r < kMaxV; ++r) {
+    const int j = ctid + r * NT;
+    vv[r] = j < nv ? ptx::ld_nc_issue(a.v_raw + j) : 0.f;
+  }
+#pragma unroll
+  for (int r = 0; r < IT; ++r) {
+    const int i = ctid + r * NT;
+    if (i < D) raw[i] = kr[r];
+  }
+#pragma unroll
+  for (int r = 0; r < kMaxV; ++r) {
+    const int j = ctid + r * NT;
+    if (j < nv) raw[D + j] = vv[r];
   }
 }
 
@@ -1116,6 +1133,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
 
   // -------------------------------------------------------------- consumers
   ptx::setmaxnreg_inc<kConsumerRegs>();
+  // Fused step: the launch constants, before the dependency wait.
+  if (a.fused) {
+    fused_fill_tables<D>(a, tab, threadIdx.x);
+    ptx::named_bar_sync(1, kConsumerWarps * 32);
+  }
   // q, the KV row appended just before and the scratch the previous
   // decode/combine pair used are only touched after the preceding launch
   // completed.  The trigger comes after that wait: when the next grids
@@ -1134,7 +1156,6 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
   float m[GS], l[GS];
 
   int it = 0;
-  bool tables_ready = false;
   const bool clustered = a.cluster > 1;
   // cluster merge: this CTA's partial, in the ring (idle once the CTA's
   // last tile is consumed; a cluster-merged CTA has one piece)
@@ -1182,18 +1203,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         const bool newrow = pend == sv.gend;
         const float* kx = a.k_raw + (long long)sv.g * D;  // raw k row of head g
         const float* vx = a.v_raw;                          // raw v, all heads
-        if (!tables_ready) {  // once per CTA; the q loads above are in flight
-          // merge_o is free until this piece's finalize: stage the raw rows
-          // there when this piece builds the new row.
-          const bool stage = newrow && a.nkv * D <= kMaxStagedV &&
-                             (D + a.nkv * D) * 4 <= SM::kMergeO;
-          fused_fill_tables<D>(a, tab, ctid, stage ? merge_o : nullptr, kx);
+        // merge_o is free until this piece's finalize: stage the raw rows
+        // there when this piece builds the new row (the q loads above are in
+        // flight meanwhile).
+        if (newrow && a.nkv * D <= kMaxStagedV && (D + a.nkv * D) * 4 <= SM::kMergeO) {
+          fused_stage_raw<D>(a, merge_o, ctid, kx);
           ptx::named_bar_sync(1, kConsumerWarps * 32);
-          tables_ready = true;
-          if (stage) {
-            kx = merge_o;
-            vx = merge_o + D;
-          }
+          kx = merge_o;
+          vx = merge_o + D;
         }
         fused_rotate_q<D, GS, KT>(a, q, l8, tab);
         if (newrow) {
