@@ -257,7 +257,11 @@ int molot_attn_decode(molot_kv_cache* kv, int src_layer, const float* q, float* 
  * attention over slots [max(0, pos-window+1), n] is written to o ([nq][hd]).
  * Same results as molot_attn_append_rope + molot_attn_decode(layer), without
  * the rotated-q round trip or a second launch.  MOLOT_ERR_CACHE_FULL when
- * n == cap (forward.h:570). */
+ * n == cap (forward.h:570).  The launch may start while the preceding
+ * kernel on the stream drains (programmatic dependent launch): q, k and v
+ * are read after it completes, but freq, q_norm and k_norm (the layer's
+ * constants) are read before, so they must not be written by the kernel
+ * immediately preceding this call. */
 int molot_attn_step(molot_kv_cache* kv, int layer, const float* q, const float* k,
                     const float* v, const float* q_norm, const float* k_norm, int v_norm,
                     float eps, const float* freq, int pos, float* o, int nq, float scale,
