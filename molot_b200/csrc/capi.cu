@@ -201,6 +201,8 @@ int prepare_kernel(const KernelRef& k, int dev) {
   for (auto& p : done)
     if (p.first == k.fn && p.second == dev) return MOLOT_OK;
   MOLOT_CUDA(cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem));
+  // 16-CTA clusters (plan_uniform) are a non-portable size.
+  MOLOT_CUDA(cudaFuncSetAttribute(k.fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   done.emplace_back(k.fn, dev);
   return MOLOT_OK;
 }
@@ -291,7 +293,8 @@ int decode_uniform(Workspace& ws, const float* Q, float* O, const void* K, const
   const long long NB = (long long)nkv * nblk;
   if ((rc = prepare_kernel(k, dev))) return rc;
   const UniformPlan up =
-      plan_uniform(NB, nkv, nblk, sm_count(dev), max_active_clusters(k, kClusterCtas, dev));
+      plan_uniform(NB, nkv, nblk, sm_count(dev), max_active_clusters(k, kClusterCtas, dev),
+                   max_active_clusters(k, kClusterCtasWide, dev));
   const int grid = up.grid;
   const int G = nq / nkv;
   if ((rc = ws.ensure(dev, (size_t)2 * grid * partial_record_floats(G, d), nkv, 0))) return rc;

@@ -872,7 +872,8 @@ __device__ __forceinline__ void cluster_finish(const DecodeArgs& a, int cta, flo
   float* rec = a.partials + (size_t)(s * a.cl_per_seg + ci) * psz;
   const uint32_t rank = ptx::cluster_ctarank();
   const int nchunk = GD / 4;
-  for (int chunk = (int)rank * NT + ctid; chunk < nchunk; chunk += C * NT) {
+  // chunks interleaved over the cluster's CTAs, so every CTA merges a few
+  for (int chunk = ctid * C + (int)rank; chunk < nchunk; chunk += C * NT) {
     const int hl = (chunk * 4) / D;
     float M = -CUDART_INF_F;
     for (int r = 0; r < C; ++r) M = fmaxf(M, ptx::ld_dsmem(ptx::dsmem_addr(cbuf + GD + hl, r)));

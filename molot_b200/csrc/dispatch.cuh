@@ -37,6 +37,7 @@ struct UniformPlan {
 };
 
 constexpr int kClusterCtas = 8;       // CTAs per cluster (portable size)
+constexpr int kClusterCtasWide = 16;  // one cluster per segment (non-portable size)
 constexpr int kClusterMinBlocks = 4;  // blocks per CTA below which no extra cluster is added
 
 // One CTA per SM at most.  Segment-aligned when there are at least as many
@@ -49,10 +50,23 @@ constexpr int kClusterMinBlocks = 4;  // blocks per CTA below which no extra clu
 // slower (cfg2 step 0.88 -> 1.43 ms): a cluster starts only once kClusterCtas
 // SMs of one GPC are free, which defeats the overlap of back-to-back
 // launches.
-inline UniformPlan plan_uniform(long long NB, int S, int nblk, int sms, int clusters_resident) {
+//
+// When a whole segment fits one 16-CTA cluster at once (wide_resident >= S),
+// that form is taken: the merge then stays in distributed shared memory,
+// with no ticket and no global record.
+inline UniformPlan plan_uniform(long long NB, int S, int nblk, int sms, int clusters_resident,
+                                int wide_resident = 0) {
   UniformPlan p;
   p.grid = (int)(NB < sms ? NB : sms);
   p.aligned = p.grid >= S ? 1 : 0;
+  if (NB < 2LL * sms && wide_resident >= S && S * kClusterCtasWide <= sms &&
+      nblk >= kClusterCtasWide) {
+    p.grid = S * kClusterCtasWide;
+    p.aligned = 1;
+    p.cluster = kClusterCtasWide;
+    p.cl_per_seg = 1;
+    return p;
+  }
   const int C = kClusterCtas;
   if (NB < 2LL * sms && clusters_resident >= S && S * C <= sms && nblk >= C) {
     int k = clusters_resident / S;

@@ -167,11 +167,13 @@ extern "C" int molot_attn_decode_strided_noalloc(const float* Q, const float* K,
   if (partial_record_floats(G, d) > kNoAllocMaxRecord)
     return set_last_error(MOLOT_ERR_UNSUPPORTED, "partial record exceeds the no-alloc scratch");
   e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e != cudaSuccess) return cuda_err(e, "cudaFuncSetAttribute");
   // The partition of molot_attn_decode_strided_dev (at most kNoAllocMaxGrid
   // CTAs, which covers one per SM of a B200).
   const UniformPlan up = plan_uniform(NB, nkv, nblk, sms < kNoAllocMaxGrid ? sms : kNoAllocMaxGrid,
-                                      max_active_clusters(k, kClusterCtas, dev));
+                                      max_active_clusters(k, kClusterCtas, dev),
+                                      max_active_clusters(k, kClusterCtasWide, dev));
   const int grid = up.grid;
 
   float* partials = reinterpret_cast<float*>(scratch);
@@ -192,6 +194,7 @@ extern "C" int molot_attn_decode_strided_noalloc(const float* Q, const float* K,
     if (d <= 128 && aligned && rows_per_cta >= 8LL * tile_rows && pick(d, G, true, &ks)) k = ks;
   }
   e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e != cudaSuccess) return cuda_err(e, "cudaFuncSetAttribute");
 
   DecodeArgs a = {};
