@@ -24,7 +24,8 @@
 //        across the query blocks), split, into shared memory in the
 //        no-swizzle K-major core-matrix layout the MMA reads (K as
 //        [key][dim], V transposed as [dim][key]); 3 stages.
-//   8    lane 0 issues every MMA and commit.
+//   8    lane 0 issues the S MMAs (Q K^T) and their commits;
+//   9    lane 0 issues the P V MMAs and theirs, in parallel with warp 8's.
 // Barriers (all waits bounded; a wait that runs out records a status code,
 // raises the abort flag and the CTA winds down without further MMAs):
 //   kv_full / kv_empty per stage, s_full / s_free per S buffer, p_full,
@@ -44,7 +45,7 @@ namespace molot {
 constexpr int kTcRows = 128;   // query rows per CTA (MMA M)
 constexpr int kTcBN = 32;      // keys per tile
 constexpr int kTcStages = 3;   // K/V tile stages
-constexpr int kTcThreads = 9 * 32;
+constexpr int kTcThreads = 10 * 32;
 constexpr int kTcTmemCols = 512;
 
 template <int D>
@@ -204,7 +205,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     ptx::mbar_init(p_full, 128);
     ptx::mbar_init(pv_done, 1);
     ptx::mbar_init(q_ready, 128);
-    ptx::mbar_init(done_bar, 1);
+    ptx::mbar_init(done_bar, 2);  // one commit per issuing thread
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -402,54 +403,63 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       ptx::mbar_arrive(kv_full + st);
     }
-  } else if (lane == 0) {
-    // ------------------------------------------------------------ MMA issuer
-    const uint32_t ids = tc::idesc(BN), ido = tc::idesc(D);
+  } else if (warp == 8 && lane == 0) {
+    // ------------------------------------------------------- S = Q K^T issuer
+    // Fully unrolled: the descriptors advance by constant offsets (their
+    // start-address field never carries: shared-memory offsets stay below
+    // 2^18 bytes), so the thread issues at the tensor pipe's rate.
+    const uint32_t ids = tc::idesc(BN);
     tc_wait(q_ready, 0, a, abort_flag, 4);
     tc::fence_after();
 #pragma unroll 1
-    for (int j = 0; j <= ntiles; ++j) {
-      if (j < ntiles) {
-        const int st = j % kTcStages, sb = j & 1;
-        tc_wait(kv_full + st, (j / kTcStages) & 1, a, abort_flag, 4);
-        if (j >= 2) tc_wait(s_free + sb, ((j >> 1) - 1) & 1, a, abort_flag, 4);
-        tc::fence_after();
-        if (!*abort_flag) {
-          const uint32_t kb = ptx::smem_u32(smem + st * TS::kStage);
-          const uint32_t d = T + TS::kS + sb * BN;
-#pragma unroll 1
-          for (int s = 0; s < D / 8; ++s) {  // S = Qh Kh + Qh Kl + Ql Kh over dims 8s..8s+7
-            const uint32_t off = 2 * s * (BN * 16);
-            const uint64_t bh = tc::sdesc(kb + off, BN * 16, 128);
-            const uint64_t bl = tc::sdesc(kb + TS::kTile + off, BN * 16, 128);
-            tc::mma(d, T + TS::kQhi + 8 * s, bh, ids, s > 0);
-            tc::mma(d, T + TS::kQhi + 8 * s, bl, ids, 1);
-            tc::mma(d, T + TS::kQlo + 8 * s, bh, ids, 1);
-          }
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j % kTcStages, sb = j & 1;
+      tc_wait(kv_full + st, (j / kTcStages) & 1, a, abort_flag, 4);
+      if (j >= 2) tc_wait(s_free + sb, ((j >> 1) - 1) & 1, a, abort_flag, 4);
+      tc::fence_after();
+      if (!*abort_flag) {
+        const uint32_t kb = ptx::smem_u32(smem + st * TS::kStage);
+        const uint32_t d = T + TS::kS + sb * BN;
+        const uint64_t bh0 = tc::sdesc(kb, BN * 16, 128);
+        const uint64_t bl0 = tc::sdesc(kb + TS::kTile, BN * 16, 128);
+#pragma unroll
+        for (int k = 0; k < D / 8; ++k) {  // S = Qh Kh + Qh Kl + Ql Kh over dims 8k..8k+7
+          const uint64_t step = (uint64_t)((2 * k * (BN * 16)) >> 4);
+          tc::mma(d, T + TS::kQhi + 8 * k, bh0 + step, ids, k > 0);
+          tc::mma(d, T + TS::kQhi + 8 * k, bl0 + step, ids, 1);
+          tc::mma(d, T + TS::kQlo + 8 * k, bh0 + step, ids, 1);
         }
-        tc::commit(s_full + sb);
       }
-      if (j >= 1) {
-        const int jp = j - 1, st = jp % kTcStages;
-        tc_wait(p_full, jp & 1, a, abort_flag, 4);
-        tc::fence_after();
-        if (!*abort_flag) {
-          const uint32_t vb = ptx::smem_u32(smem + st * TS::kStage + 2 * TS::kTile);
-#pragma unroll 1
-          for (int s = 0; s < BN / 8; ++s) {  // O += Ph Vh + Ph Vl + Pl Vh over keys 8s..8s+7
-            const uint32_t off = 2 * s * TS::kVChunk;
-            const uint64_t bh = tc::sdesc(vb + off, TS::kVChunk, 128);
-            const uint64_t bl = tc::sdesc(vb + TS::kVTile + off, TS::kVChunk, 128);
-            tc::mma(T + TS::kO, T + TS::kPhi + 8 * s, bh, ido, (jp > 0 || s > 0) ? 1 : 0);
-            tc::mma(T + TS::kO, T + TS::kPhi + 8 * s, bl, ido, 1);
-            tc::mma(T + TS::kO, T + TS::kPlo + 8 * s, bh, ido, 1);
-          }
-        }
-        tc::commit(pv_done);
-        tc::commit(kv_empty + st);
-      }
+      tc::commit(s_full + sb);
     }
-    tc::commit(done_bar);  // arrives once every MMA above has completed
+    tc::commit(done_bar);  // arrives once every MMA this thread issued has completed
+  } else if (warp == 9 && lane == 0) {
+    // ------------------------------------------------------- O += P V issuer
+    // A thread of its own, so tile j's P V is issued while the other thread
+    // issues tile j+1's S.  kv_empty may follow P V(j) alone: S(j) completed
+    // before the softmax released P(j).
+    const uint32_t ido = tc::idesc(D);
+#pragma unroll 1
+    for (int jp = 0; jp < ntiles; ++jp) {
+      const int st = jp % kTcStages;
+      tc_wait(p_full, jp & 1, a, abort_flag, 4);
+      tc::fence_after();
+      if (!*abort_flag) {
+        const uint32_t vb = ptx::smem_u32(smem + st * TS::kStage + 2 * TS::kTile);
+        const uint64_t bh0 = tc::sdesc(vb, TS::kVChunk, 128);
+        const uint64_t bl0 = tc::sdesc(vb + TS::kVTile, TS::kVChunk, 128);
+#pragma unroll
+        for (int k = 0; k < BN / 8; ++k) {  // O += Ph Vh + Ph Vl + Pl Vh over keys 8k..8k+7
+          const uint64_t step = (uint64_t)((2 * k * TS::kVChunk) >> 4);
+          tc::mma(T + TS::kO, T + TS::kPhi + 8 * k, bh0 + step, ido, (jp > 0 || k > 0) ? 1 : 0);
+          tc::mma(T + TS::kO, T + TS::kPhi + 8 * k, bl0 + step, ido, 1);
+          tc::mma(T + TS::kO, T + TS::kPlo + 8 * k, bh0 + step, ido, 1);
+        }
+      }
+      tc::commit(pv_done);
+      tc::commit(kv_empty + st);
+    }
+    tc::commit(done_bar);
   }
 
   // Tensor memory is freed by the warp that allocated it, after every MMA
