@@ -20,12 +20,12 @@
 //        scale, causal / window mask, lazy online softmax in base 2 (the
 //        running max rises only when a score exceeds it by 2^8; O is then
 //        rescaled in TMEM), P -> TMEM (split); at the end O / l -> global.
-//   4-7  converters: per key tile, K and V rows from global (L2-resident
+//   4-11 converters: per key tile, K and V rows from global (L2-resident
 //        across the query blocks), split, into shared memory in the
 //        no-swizzle K-major core-matrix layout the MMA reads (K as
 //        [key][dim], V transposed as [dim][key]); 3 stages.
-//   8    lane 0 issues the S MMAs (Q K^T) and their commits;
-//   9    lane 0 issues the P V MMAs and theirs, in parallel with warp 8's.
+//   12   lane 0 issues the S MMAs (Q K^T) and their commits;
+//   13   lane 0 issues the P V MMAs and theirs, in parallel with warp 12's.
 // Barriers (all waits bounded; a wait that runs out records a status code,
 // raises the abort flag and the CTA winds down without further MMAs):
 //   kv_full / kv_empty per stage, s_full / s_free per S buffer, p_full,
@@ -45,7 +45,8 @@ namespace molot {
 constexpr int kTcRows = 128;   // query rows per CTA (MMA M)
 constexpr int kTcBN = 32;      // keys per tile
 constexpr int kTcStages = 3;   // K/V tile stages
-constexpr int kTcThreads = 10 * 32;
+constexpr int kTcConvWarps = 8;  // converter warps (4..11)
+constexpr int kTcThreads = (4 + kTcConvWarps + 2) * 32;
 constexpr int kTcTmemCols = 512;
 
 template <int D>
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (tid == 0) {
     for (int i = 0; i < kTcStages; ++i) {
-      ptx::mbar_init(kv_full + i, 128);
+      ptx::mbar_init(kv_full + i, kTcConvWarps * 32);
       ptx::mbar_init(kv_empty + i, 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -344,12 +345,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
       }
     }
-  } else if (warp < 8) {
+  } else if (warp < 4 + kTcConvWarps) {
     // ---------------------------------------------------------- converters
+    constexpr int NC = kTcConvWarps * 32;
     const int ct = tid - 128;
     const float* Kb = static_cast<const float*>(a.K) + (long long)g * a.stride_h;
     const float* Vb = static_cast<const float*>(a.V) + (long long)g * a.stride_h;
-    constexpr int NI = BN * D / 4 / 128;
+    constexpr int NI = BN * D / 4 / NC;
 #pragma unroll 1
     for (int j = 0; j < ntiles; ++j) {
       const int st = j % kTcStages;
@@ -362,12 +364,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         unsigned char* vlo = base + 2 * TS::kTile + TS::kVTile;
         const int key0 = kt0 + j * BN;
         // Every load of the tile is issued before the first store: thread
-        // ct takes key (ct % 32) of the 4-dim chunks ct/32 + 4i, so a
+        // ct takes key (ct % 32) of the 4-dim chunks ct/32 + (NC/32)i, so a
         // warp's K stores are one contiguous 512-byte run.
         float4 kx[NI], vx[NI];
 #pragma unroll
         for (int i = 0; i < NI; ++i) {
-          const int f = ct + i * 128;
+          const int f = ct + i * NC;
           const int t = key0 + f % BN;
           const long long row = (long long)t * a.stride_t + 4 * (f / BN);
           kx[i] = t < a.N ? *reinterpret_cast<const float4*>(Kb + row) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -375,7 +377,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
 #pragma unroll
         for (int i = 0; i < NI; ++i) {
-          const int f = ct + i * 128;
+          const int f = ct + i * NC;
           const int key = f % BN, c4 = f / BN;
           const float4 x = kx[i];
           float4 h, l;
@@ -403,7 +405,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       ptx::mbar_arrive(kv_full + st);
     }
-  } else if (warp == 8 && lane == 0) {
+  } else if (warp == 4 + kTcConvWarps && lane == 0) {
     // ------------------------------------------------------- S = Q K^T issuer
     // Fully unrolled: the descriptors advance by constant offsets (their
     // start-address field never carries: shared-memory offsets stay below
@@ -433,7 +435,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc::commit(s_full + sb);
     }
     tc::commit(done_bar);  // arrives once every MMA this thread issued has completed
-  } else if (warp == 9 && lane == 0) {
+  } else if (warp == 5 + kTcConvWarps && lane == 0) {
     // ------------------------------------------------------- O += P V issuer
     // A thread of its own, so tile j's P V is issued while the other thread
     // issues tile j+1's S.  kv_empty may follow P V(j) alone: S(j) completed
