@@ -48,6 +48,10 @@ def test_step_against_reference_golden(mb, torch_cuda, orc):
     (32, 8, 128, 300, True, 0),       # ~1 block per CTA: the shortened last share
     (64, 8, 128, 2500, False, 0),     # G = 8
     (8, 8, 128, 40000, True, 0),      # G = 1, long
+    # long enough for the split-barrier kernels
+    (64, 8, 128, 20000, True, 0),     # G = 8: two head sets
+    (32, 8, 64, 40000, False, 0),     # head_dim 64
+    (32, 8, 128, 30000, True, 20000), # window start inside a tile
 ])
 def test_step_matches_oracle_and_two_launch_path(mb, torch_cuda, orc, nq, nkv, hd, n0, norms,
                                                   window):
