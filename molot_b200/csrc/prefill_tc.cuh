@@ -3,27 +3,42 @@
 // contract as gqa_prefill_kernel (gemm.h:409-446, attn_prefill_gqa at
 // forward.h:396) within the 1e-5 bar.
 //
-// Precision: split TF32.  Every FP32 operand x is split into hi =
-// round-to-nearest TF32 of x and lo = x - hi (exact in FP32, |lo| <=
-// 2^-11 |x|), and each product is formed as hi*hi + hi*lo + lo*hi by three
-// TF32 MMAs accumulating in FP32 (the dropped lo*lo term is ~2^-22 of the
-// product).  S = Q K^T and O = P V both run this way.
+// Precision.  Both products keep FP32 accuracy by splitting operands:
+//   S = Q K^T in split FP16.  Every query row and every key row is scaled
+//     by a power of two (exact) so that its largest magnitude lies in
+//     [2^14, 2^15); a scaled value x becomes h0 = fp16(x) and h1 = fp16(x -
+//     h0) (x - h0 is exact in FP32), and S is formed as h0.h0 + h0.h1 +
+//     h1.h0 by three kind::f16 MMAs accumulating in FP32.  The dropped h1.h1
+//     term is ~2^-22 of the product; values below 2^-17 of their row's
+//     largest keep an absolute error under 2^-39 of it.  The softmax undoes
+//     both scales exactly before it applies the attention scale.
+//   O += P V in split TF32: hi = round-to-nearest TF32 of x, lo = x - hi,
+//     hi.hi + hi.lo + lo.hi by three kind::tf32 MMAs (P <= 2^8 and V are
+//     used unscaled).
+// FP16 pairs pack two K elements per 32-bit tensor-memory column, so Q's
+// two halves take D columns in all and 64-key tiles fit: an S MMA costs the
+// same issue time at N = 64 as at N = 32, so a key costs half the S issue
+// time of 32-key tiles.
 //
 // CTA: one kv head x 128 query rows (row r = position (r / G) of the block,
 // head (r % G) of the kv head's group), the MMA's M.  Tensor memory (512
-// columns, all of the SM's): Q hi / lo (the A operand of S, D columns each),
-// two S buffers (BN columns each), P hi / lo (the A operand of O), the O
-// accumulator (D columns); a thread of the softmax warpgroup owns its row's
-// lane, so row maxima and sums never leave the thread.
+// columns, all of the SM's): Q h0 / h1 (the A operand of S, D/2 columns
+// each), two S buffers (BN columns each), P hi / lo (the A operand of O),
+// the O accumulator (D columns); a thread of the softmax warpgroup owns its
+// row's lane, so row maxima and sums never leave the thread.
 // Warps:
-//   0-3  softmax: Q row -> TMEM (split), then per key tile: S row from TMEM,
-//        scale, causal / window mask, lazy online softmax in base 2 (the
-//        running max rises only when a score exceeds it by 2^8; O is then
-//        rescaled in TMEM), P -> TMEM (split); at the end O / l -> global.
+//   0-3  softmax: Q row -> TMEM (scaled, split), then per key tile: S row
+//        from TMEM, both scales and the attention scale, causal / window
+//        mask, lazy online softmax in base 2 (the running max rises only
+//        when a score exceeds it by 2^8; O is then rescaled in TMEM), P ->
+//        TMEM (split); at the end O / l -> global.
 //   4-11 converters: per key tile, K and V rows from global (L2-resident
-//        across the query blocks), split, into shared memory in the
-//        no-swizzle K-major core-matrix layout the MMA reads (K as
-//        [key][dim], V transposed as [dim][key]); 3 stages.
+//        across the query blocks; issued before the stage is free), each
+//        key's scale (its largest magnitude, reduced over the four lanes
+//        holding the key), K split in FP16 and V in TF32, into shared
+//        memory in the no-swizzle K-major core-matrix layouts the MMAs read
+//        (K as [key][dim], V transposed as [dim][key]), plus the keys'
+//        inverse scales; 2 stages.
 //   12   lane 0 issues the S MMAs (Q K^T) and their commits;
 //   13   lane 0 issues the P V MMAs and theirs, in parallel with warp 12's.
 // Barriers (all waits bounded; a wait that runs out records a status code,
@@ -32,6 +47,7 @@
 //   pv_done, q_ready, done (the last commit, before TMEM is freed).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math_constants.h>
 
@@ -42,9 +58,9 @@
 
 namespace molot {
 
-constexpr int kTcRows = 128;   // query rows per CTA (MMA M)
-constexpr int kTcBN = 32;      // keys per tile
-constexpr int kTcStages = 3;   // K/V tile stages
+constexpr int kTcRows = 128;     // query rows per CTA (MMA M)
+constexpr int kTcBN = 64;        // keys per tile (the S MMA's N)
+constexpr int kTcStages = 2;     // K/V tile stages
 constexpr int kTcConvWarps = 8;  // converter warps (4..11)
 constexpr int kTcThreads = (4 + kTcConvWarps + 2) * 32;
 constexpr int kTcTmemCols = 512;
@@ -52,13 +68,15 @@ constexpr int kTcTmemCols = 512;
 template <int D>
 struct TcShape {
   static_assert(D == 64 || D == 128, "tensor-core prefill: head_dim 64 or 128");
-  static constexpr int kTile = kTcBN * D * 4;     // one hi or lo K tile (bytes)
+  static constexpr int BN = kTcBN;
+  static constexpr int kKTile = BN * D * 2;  // one FP16 half (h0 or h1) of a K tile (bytes)
   // V tiles are transposed with a 16-byte gap after each 4-key chunk
-  // (leading byte offset D*16 + 16), so the 8 chunks a warp's stores span
-  // fall on different banks.
+  // (leading byte offset D*16 + 16), so the chunks a warp's stores span fall
+  // on different banks.
   static constexpr int kVChunk = D * 16 + 16;
-  static constexpr int kVTile = (kTcBN / 4) * kVChunk;
-  static constexpr int kStage = 2 * kTile + 2 * kVTile;  // K hi, K lo, V hi, V lo
+  static constexpr int kVTile = (BN / 4) * kVChunk;  // one TF32 half of a V tile
+  static constexpr int kKInv = BN * 4;               // the keys' inverse scales (floats)
+  static constexpr int kStage = 2 * kKTile + 2 * kVTile + kKInv;
   static constexpr int kBarOff = kTcStages * kStage;
   static constexpr int kBars = 2 * kTcStages + 4 + 4;  // kv_full/empty, s_full/free x2, p, pv, q, done
   // Over half of the SM's shared memory, so a second CTA (which would wait
@@ -66,26 +84,49 @@ struct TcShape {
   static constexpr int kUsed = kBarOff + kBars * 8 + 32;
   static constexpr int kTotal = kUsed > 116 * 1024 ? kUsed : 116 * 1024;
   // tensor-memory columns
-  static constexpr uint32_t kQhi = 0, kQlo = D, kS = 2 * D, kPhi = 2 * D + 2 * kTcBN,
-                            kPlo = kPhi + kTcBN, kO = kPlo + kTcBN;
+  static constexpr uint32_t kQ0 = 0, kQ1 = D / 2, kS = D, kPhi = D + 2 * BN, kPlo = kPhi + BN,
+                            kO = kPlo + BN;
   static_assert(kO + D <= kTcTmemCols, "tensor memory columns");
   static_assert(kTotal <= 227 * 1024, "shared memory");
-  // K tile, K-major B of S (N = keys, K = dims): core matrix = 8 keys x 4 dims
+  static_assert(kStage % 16 == 0 && kKTile % 16 == 0 && kVTile % 16 == 0, "16-byte operands");
+  // K tile half, K-major B of S (N = keys, K = dims): core matrix = 8 keys x
+  // 8 FP16 dims (16-byte rows)
   __device__ static int k_off(int key, int dim) {
-    return (dim >> 2) * (kTcBN * 16) + (key >> 3) * 128 + (key & 7) * 16 + (dim & 3) * 4;
+    return (dim >> 3) * (BN * 16) + (key >> 3) * 128 + (key & 7) * 16 + (dim & 7) * 2;
   }
-  // V tile transposed, K-major B of O (N = dims, K = keys): 8 dims x 4 keys
+  // V tile half transposed, K-major B of O (N = dims, K = keys): 8 dims x 4 keys
   __device__ static int v_off(int key, int dim) {
     return (key >> 2) * kVChunk + (dim >> 3) * 128 + (dim & 7) * 16 + (key & 3) * 4;
   }
 };
 
+// Power-of-two exponent e that brings a largest magnitude m into [2^14,
+// 2^15) (0 for m == 0), kept within the range where 2^e and 2^-e are normal.
+__device__ __forceinline__ int fp16_split_exp(float m) {
+  const int ex = (int)((__float_as_uint(m) >> 23) & 0xff);
+  if (ex == 0) return m == 0.f ? 0 : 126;
+  const int e = 141 - ex;
+  return e > 126 ? 126 : (e < -126 ? -126 : e);
+}
+__device__ __forceinline__ float exp2i(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
+// Two scaled values y -> their FP16 high parts h0 (packed, y.x in the low
+// half) and residual parts h1 = fp16(y - h0) (y - h0 exact in FP32).
+__device__ __forceinline__ void fp16_split2(float2 y, uint32_t& h0, uint32_t& h1) {
+  const __half2 a = __float22half2_rn(y);
+  const float2 af = __half22float2(a);
+  const __half2 b = __float22half2_rn(make_float2(y.x - af.x, y.y - af.y));
+  h0 = *reinterpret_cast<const uint32_t*>(&a);
+  h1 = *reinterpret_cast<const uint32_t*>(&b);
+}
+
 namespace tc {
 
+// Round to nearest TF32, ties away from zero (cvt.rna.tf32.f32), in integer
+// arithmetic on the bit pattern: add half of the dropped 13 bits' weight to
+// the magnitude, then clear them (a carry moves into the exponent, as the
+// rounding does).  Finite inputs only.
 __device__ __forceinline__ float tf32_hi(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xffffe000u);
 }
 
 // Shared-memory matrix descriptor, no swizzle (sm_100 layout: start, leading
@@ -99,7 +140,18 @@ __host__ __device__ constexpr uint32_t idesc(int n) {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) |
          ((uint32_t)(kTcRows >> 4) << 24);
 }
-// D[tmem] (+)= A[tmem] * B[smem desc]
+// Instruction descriptor: F16 x F16 -> F32, both K-major, M = 128.
+__host__ __device__ constexpr uint32_t idesc16(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
+}
+// D[tmem] (+)= A[tmem] * B[smem desc], FP16 operands (A: two per column)
+__device__ __forceinline__ void mma16(uint32_t d, uint32_t a, uint64_t b, uint32_t id, int acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(b), "r"(id), "r"(acc), "r"(0u));
+}
+// D[tmem] (+)= A[tmem] * B[smem desc], TF32 operands
 __device__ __forceinline__ void mma(uint32_t d, uint32_t a, uint64_t b, uint32_t id, int acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -235,65 +287,115 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int t_hi = valid ? min(pos + 1, a.N) : 0;  // attended [t_lo, t_hi)
     const int t_lo = a.window > 0 ? max(0, pos - a.window + 1) : 0;
     const float* qrow = a.Q + (long long)m * a.q_tstride + (long long)(g * G + h) * D;
+    // The row's scale 2^eq (its largest magnitude into [2^14, 2^15)), then
+    // h0 / h1 into columns kQ0 / kQ1, two dims per column.
+    int eq;
     {
-      float hi[16], lo[16];
+      float amax = 0.f;
 #pragma unroll 1
-      for (int c = 0; c < D; c += 16) {
+      for (int c = 0; c < D; c += 4) {
+        const float4 x = valid ? *reinterpret_cast<const float4*>(qrow + c)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+      }
+      eq = fp16_split_exp(amax);
+      const float sq = exp2i(eq);
+#pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        float w0[16], w1[16];
 #pragma unroll
-        for (int i = 0; i < 16; i += 4) {
+        for (int i = 0; i < 32; i += 4) {
           const float4 x = valid ? *reinterpret_cast<const float4*>(qrow + c + i)
                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-          hi[i] = tc::tf32_hi(x.x);
-          hi[i + 1] = tc::tf32_hi(x.y);
-          hi[i + 2] = tc::tf32_hi(x.z);
-          hi[i + 3] = tc::tf32_hi(x.w);
-          lo[i] = x.x - hi[i];
-          lo[i + 1] = x.y - hi[i + 1];
-          lo[i + 2] = x.z - hi[i + 2];
-          lo[i + 3] = x.w - hi[i + 3];
+          uint32_t a0, a1, b0, b1;
+          fp16_split2(make_float2(x.x * sq, x.y * sq), a0, b0);
+          fp16_split2(make_float2(x.z * sq, x.w * sq), a1, b1);
+          w0[i / 2] = __uint_as_float(a0);
+          w0[i / 2 + 1] = __uint_as_float(a1);
+          w1[i / 2] = __uint_as_float(b0);
+          w1[i / 2 + 1] = __uint_as_float(b1);
         }
-        tc::st16(lane_base + TS::kQhi + c, hi);
-        tc::st16(lane_base + TS::kQlo + c, lo);
+        tc::st16(lane_base + TS::kQ0 + c / 2, w0);
+        tc::st16(lane_base + TS::kQ1 + c / 2, w1);
       }
       tc::wait_st();
       tc::fence_before();
       ptx::mbar_arrive(q_ready);
     }
-    const float sl2 = a.scale * kLog2e;
+    // S * 2^-eq * 2^-ek[key] is the exact FP32 score; sl2 applies the
+    // attention scale in base 2 with the single rounding of s * scale.
+    const float sl2 = a.scale * kLog2e * exp2i(-eq);
     float mrow = -CUDART_INF_F, lrow = 0.f;
 #pragma unroll 1
     for (int j = 0; j < ntiles; ++j) {
       const int sb = j & 1;
+      const int st = j % kTcStages;
       tc_wait(s_full + sb, (j >> 1) & 1, a, abort_flag, 1);
       __syncwarp();  // lanes leave the wait loop on their own; tcgen05.ld is warp-collective
       tc::fence_after();
       float s[BN];
-      tc::ld16(lane_base + TS::kS + sb * BN, s);
-      tc::ld16(lane_base + TS::kS + sb * BN + 16, s + 16);
+#pragma unroll
+      for (int c = 0; c < BN; c += 16) tc::ld16(lane_base + TS::kS + sb * BN + c, s + c);
       tc::fence_before();
       ptx::mbar_arrive(s_free + sb);
+      // The keys' inverse scales, written by the converters before they
+      // released the stage (waited on here for ordering; it cannot refill
+      // before this tile's P V completes).
+      tc_wait(kv_full + st, (j / kTcStages) & 1, a, abort_flag, 1);
+      const float* kinv = reinterpret_cast<const float*>(smem + st * TS::kStage + 2 * TS::kKTile +
+                                                         2 * TS::kVTile);
       const int key0 = kt0 + j * BN;
-      float mc = -CUDART_INF_F;
+      // s * 2^-ek (exact) then * sl2 (one rounding), two keys per packed
+      // multiply; keys outside [t_lo, t_hi) only on the tiles that hold some.
+#pragma unroll
+      for (int i = 0; i < BN; i += 4) {
+        const float4 ki = *reinterpret_cast<const float4*>(kinv + i);
+        const float2 a0 = __fmul2_rn(__fmul2_rn(make_float2(s[i], s[i + 1]), make_float2(ki.x, ki.y)),
+                                     make_float2(sl2, sl2));
+        const float2 a1 = __fmul2_rn(__fmul2_rn(make_float2(s[i + 2], s[i + 3]), make_float2(ki.z, ki.w)),
+                                     make_float2(sl2, sl2));
+        s[i] = a0.x;
+        s[i + 1] = a0.y;
+        s[i + 2] = a1.x;
+        s[i + 3] = a1.y;
+      }
+      if (key0 < t_lo || key0 + BN > t_hi) {
+#pragma unroll
+        for (int i = 0; i < BN; ++i) {
+          const int t = key0 + i;
+          if (t < t_lo || t >= t_hi) s[i] = -CUDART_INF_F;
+        }
+      }
+      float mc4[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
+#pragma unroll
+      for (int i = 0; i < BN; ++i) mc4[i & 3] = fmaxf(mc4[i & 3], s[i]);
+      const float mc = fmaxf(fmaxf(mc4[0], mc4[1]), fmaxf(mc4[2], mc4[3]));
+      // Lazy rescale: the running max rises only when a score exceeds it
+      // by 2^8 (or is the row's first finite one).  The weights are formed
+      // before the wait for the previous tile's P V (they depend on the
+      // scores alone); O's rescale and the P stores come after it.
+      const bool raise = mc > mrow + 8.f;
+      const bool scale_o = raise && j > 0 && lrow > 0.f;
+      const float alpha = scale_o ? prefill_ex2(mrow - mc) : 1.f;
+      if (raise) mrow = mc;
+      if (scale_o) lrow *= alpha;
+      float l4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < BN; ++i) {
-        const int t = key0 + i;
-        s[i] = (t >= t_lo && t < t_hi) ? s[i] * sl2 : -CUDART_INF_F;
-        mc = fmaxf(mc, s[i]);
+        s[i] = (s[i] == -CUDART_INF_F) ? 0.f : prefill_ex2(s[i] - mrow);
+        l4[i & 3] += s[i];
       }
+      lrow += (l4[0] + l4[1]) + (l4[2] + l4[3]);
       // P and O may be touched once the previous tile's P V has completed.
       if (j > 0) {
         tc_wait(pv_done, (j - 1) & 1, a, abort_flag, 2);
         __syncwarp();
         tc::fence_after();
       }
-      // Lazy rescale: the running max rises only when a score exceeds it
-      // by 2^8 (or is the row's first finite one).  tcgen05.ld / st are
-      // warp-collective, so when any row of the warp must rescale O the
-      // whole warp does it, the other rows with a factor of 1.
-      const bool raise = mc > mrow + 8.f;
-      const bool scale_o = raise && j > 0 && lrow > 0.f;
+      // tcgen05.ld / st are warp-collective, so when any row of the warp
+      // must rescale O the whole warp does it, the other rows with a factor
+      // of 1.
       if (__any_sync(0xffffffffu, scale_o)) {
-        const float alpha = scale_o ? prefill_ex2(mrow - mc) : 1.f;
 #pragma unroll 1
         for (int c = 0; c < D; c += 16) {
           float o[16];
@@ -302,21 +404,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int i = 0; i < 16; ++i) o[i] *= alpha;
           tc::st16(lane_base + TS::kO + c, o);
         }
-        lrow *= alpha;
       }
-      if (raise) mrow = mc;
-      float hi[BN], lo[BN];
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        const float p = (s[i] == -CUDART_INF_F) ? 0.f : prefill_ex2(s[i] - mrow);
-        lrow += p;
-        hi[i] = tc::tf32_hi(p);
-        lo[i] = p - hi[i];
+      for (int c = 0; c < BN; c += 16) {
+        float hi[16], lo[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          hi[i] = tc::tf32_hi(s[c + i]);
+          lo[i] = s[c + i] - hi[i];
+        }
+        tc::st16(lane_base + TS::kPhi + c, hi);
+        tc::st16(lane_base + TS::kPlo + c, lo);
       }
-      tc::st16(lane_base + TS::kPhi, hi);
-      tc::st16(lane_base + TS::kPhi + 16, hi + 16);
-      tc::st16(lane_base + TS::kPlo, lo);
-      tc::st16(lane_base + TS::kPlo + 16, lo + 16);
       tc::wait_st();
       tc::fence_before();
       ptx::mbar_arrive(p_full);
@@ -347,56 +446,60 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else if (warp < 4 + kTcConvWarps) {
     // ---------------------------------------------------------- converters
-    constexpr int NC = kTcConvWarps * 32;
-    const int ct = tid - 128;
+    // Converter warp cw takes keys 8cw..8cw+7 of a tile, four lanes per key:
+    // lane l holds dims 4(l%4) + 16i of key 8cw + l/4, so a warp's loads
+    // read 64 contiguous bytes of each of its 8 rows and a key's largest
+    // magnitude is reduced over its four lanes with two shuffles.  A tile's
+    // loads and scales are done before its stage is free.
+    constexpr int NI = D / 16;  // float4 chunks of K (and of V) per thread
+    static_assert(kTcConvWarps * 8 == BN, "eight keys per converter warp");
+    const int key = 8 * (warp - 4) + (lane >> 2);
+    const int dq = 4 * (lane & 3);
     const float* Kb = static_cast<const float*>(a.K) + (long long)g * a.stride_h;
     const float* Vb = static_cast<const float*>(a.V) + (long long)g * a.stride_h;
-    constexpr int NI = BN * D / 4 / NC;
 #pragma unroll 1
     for (int j = 0; j < ntiles; ++j) {
       const int st = j % kTcStages;
+      const int t = kt0 + j * BN + key;
+      float4 kx[NI], vx[NI];
+#pragma unroll
+      for (int i = 0; i < NI; ++i) {
+        const long long row = (long long)t * a.stride_t + dq + 16 * i;
+        kx[i] = t < a.N ? *reinterpret_cast<const float4*>(Kb + row) : make_float4(0.f, 0.f, 0.f, 0.f);
+        vx[i] = t < a.N ? *reinterpret_cast<const float4*>(Vb + row) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      float am = 0.f;
+#pragma unroll
+      for (int i = 0; i < NI; ++i)
+        am = fmaxf(am, fmaxf(fmaxf(fabsf(kx[i].x), fabsf(kx[i].y)),
+                             fmaxf(fabsf(kx[i].z), fabsf(kx[i].w))));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+      const int ek = fp16_split_exp(am);
+      const float sk = exp2i(ek);
       if (j >= kTcStages) tc_wait(kv_empty + st, ((j / kTcStages) - 1) & 1, a, abort_flag, 3);
+      unsigned char* base = smem + st * TS::kStage;
+      unsigned char* kh0 = base;
+      unsigned char* kh1 = base + TS::kKTile;
+      unsigned char* vhi = base + 2 * TS::kKTile;
+      unsigned char* vlo = vhi + TS::kVTile;
+      float* kinv = reinterpret_cast<float*>(vlo + TS::kVTile);
       if (!*abort_flag) {
-        unsigned char* base = smem + st * TS::kStage;
-        unsigned char* khi = base;
-        unsigned char* klo = base + TS::kTile;
-        unsigned char* vhi = base + 2 * TS::kTile;
-        unsigned char* vlo = base + 2 * TS::kTile + TS::kVTile;
-        const int key0 = kt0 + j * BN;
-        // Every load of the tile is issued before the first store: thread
-        // ct takes key (ct % 32) of the 4-dim chunks ct/32 + (NC/32)i, so a
-        // warp's K stores are one contiguous 512-byte run.
-        float4 kx[NI], vx[NI];
+        if ((lane & 3) == 0) kinv[key] = exp2i(-ek);
 #pragma unroll
         for (int i = 0; i < NI; ++i) {
-          const int f = ct + i * NC;
-          const int t = key0 + f % BN;
-          const long long row = (long long)t * a.stride_t + 4 * (f / BN);
-          kx[i] = t < a.N ? *reinterpret_cast<const float4*>(Kb + row) : make_float4(0.f, 0.f, 0.f, 0.f);
-          vx[i] = t < a.N ? *reinterpret_cast<const float4*>(Vb + row) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int i = 0; i < NI; ++i) {
-          const int f = ct + i * NC;
-          const int key = f % BN, c4 = f / BN;
-          const float4 x = kx[i];
-          float4 h, l;
-          h.x = tc::tf32_hi(x.x);
-          h.y = tc::tf32_hi(x.y);
-          h.z = tc::tf32_hi(x.z);
-          h.w = tc::tf32_hi(x.w);
-          l.x = x.x - h.x;
-          l.y = x.y - h.y;
-          l.z = x.z - h.z;
-          l.w = x.w - h.w;
-          const int off = TS::k_off(key, 4 * c4);
-          *reinterpret_cast<float4*>(khi + off) = h;
-          *reinterpret_cast<float4*>(klo + off) = l;
+          const int d0 = dq + 16 * i;
+          uint32_t a0, a1, b0, b1;
+          fp16_split2(make_float2(kx[i].x * sk, kx[i].y * sk), a0, b0);
+          fp16_split2(make_float2(kx[i].z * sk, kx[i].w * sk), a1, b1);
+          const int off = TS::k_off(key, d0);
+          *reinterpret_cast<uint2*>(kh0 + off) = make_uint2(a0, a1);
+          *reinterpret_cast<uint2*>(kh1 + off) = make_uint2(b0, b1);
           const float v4[4] = {vx[i].x, vx[i].y, vx[i].z, vx[i].w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float vh = tc::tf32_hi(v4[e]);
-            const int vo = TS::v_off(key, 4 * c4 + e);
+            const int vo = TS::v_off(key, d0 + e);
             *reinterpret_cast<float*>(vhi + vo) = vh;
             *reinterpret_cast<float*>(vlo + vo) = v4[e] - vh;
           }
@@ -406,11 +509,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       ptx::mbar_arrive(kv_full + st);
     }
   } else if (warp == 4 + kTcConvWarps && lane == 0) {
-    // ------------------------------------------------------- S = Q K^T issuer
+    // --------------------------------------------------- S = Q K^T issuer
     // Fully unrolled: the descriptors advance by constant offsets (their
     // start-address field never carries: shared-memory offsets stay below
     // 2^18 bytes), so the thread issues at the tensor pipe's rate.
-    const uint32_t ids = tc::idesc(BN);
+    const uint32_t ids = tc::idesc16(BN);
     tc_wait(q_ready, 0, a, abort_flag, 4);
     tc::fence_after();
 #pragma unroll 1
@@ -422,14 +525,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (!*abort_flag) {
         const uint32_t kb = ptx::smem_u32(smem + st * TS::kStage);
         const uint32_t d = T + TS::kS + sb * BN;
-        const uint64_t bh0 = tc::sdesc(kb, BN * 16, 128);
-        const uint64_t bl0 = tc::sdesc(kb + TS::kTile, BN * 16, 128);
+        const uint64_t b0 = tc::sdesc(kb, BN * 16, 128);
+        const uint64_t b1 = tc::sdesc(kb + TS::kKTile, BN * 16, 128);
 #pragma unroll
-        for (int k = 0; k < D / 8; ++k) {  // S = Qh Kh + Qh Kl + Ql Kh over dims 8k..8k+7
+        for (int k = 0; k < D / 16; ++k) {  // S = Q0 K0 + Q0 K1 + Q1 K0 over dims 16k..16k+15
           const uint64_t step = (uint64_t)((2 * k * (BN * 16)) >> 4);
-          tc::mma(d, T + TS::kQhi + 8 * k, bh0 + step, ids, k > 0);
-          tc::mma(d, T + TS::kQhi + 8 * k, bl0 + step, ids, 1);
-          tc::mma(d, T + TS::kQlo + 8 * k, bh0 + step, ids, 1);
+          tc::mma16(d, T + TS::kQ0 + 8 * k, b0 + step, ids, k > 0);
+          tc::mma16(d, T + TS::kQ0 + 8 * k, b1 + step, ids, 1);
+          tc::mma16(d, T + TS::kQ1 + 8 * k, b0 + step, ids, 1);
         }
       }
       tc::commit(s_full + sb);
@@ -447,7 +550,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_wait(p_full, jp & 1, a, abort_flag, 4);
       tc::fence_after();
       if (!*abort_flag) {
-        const uint32_t vb = ptx::smem_u32(smem + st * TS::kStage + 2 * TS::kTile);
+        const uint32_t vb = ptx::smem_u32(smem + st * TS::kStage + 2 * TS::kKTile);
         const uint64_t bh0 = tc::sdesc(vb, TS::kVChunk, 128);
         const uint64_t bl0 = tc::sdesc(vb + TS::kVTile, TS::kVChunk, 128);
 #pragma unroll
