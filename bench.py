@@ -1033,22 +1033,24 @@ def run_prefill(args, cfg):
     del graph, agraph
     metric, unit, amount, div = step_work(cfg)
     flops_layer = prefill_flops(cfg)
-    # FP32 caches at head_dim 64/128 run the split-TF32 tensor-core kernel:
-    # its ceiling is the TF32 tensor rate (half the measured bf16 GEMM rate)
-    # over the three TF32 products each FP32 product takes.  Other caches
-    # run the FP32 CUDA-core kernel: nominal FP32 peak (no measured figure).
+    # FP32 caches at head_dim 64/128 run the tensor-core kernel: half the
+    # useful FLOPs (S = QK^T) as three FP16 products at the measured bf16
+    # GEMM rate R, half (O = PV) as three TF32 products at R / 2, so a
+    # useful FLOP costs 0.5*3/R + 0.5*3/(R/2) = 4.5/R and the ceiling is
+    # R / 4.5.  Other caches run the FP32 CUDA-core kernel: nominal FP32
+    # peak (no measured figure).
     tc_path = args.kv == "f32" and cfg["d"] in (64, 128)
     sm_count = torch.cuda.get_device_properties(rt.dev).multi_processor_count
     if tc_path:
         try:
             with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
                 bf16 = float(json.load(fh)["bf16_tflops"])
-            peak_src = (f"measured bf16_tflops {bf16:.1f} / 2 (TF32 rate) / 3 (TF32 products per "
-                        "FP32 product)")
+            peak_src = (f"measured bf16_tflops {bf16:.1f} / 4.5 (S: 3 FP16 products at the bf16 "
+                        "rate; PV: 3 TF32 products at half of it; half the FLOPs each)")
         except Exception:
             bf16 = 1590.0
-            peak_src = "fallback bf16 1590 TFLOP/s / 2 (TF32 rate) / 3 (products per FP32 product)"
-        peak = bf16 / 2 / 3
+            peak_src = "fallback bf16 1590 TFLOP/s / 4.5 (3 FP16 S products, 3 TF32 PV products)"
+        peak = bf16 / 4.5
     else:
         peak = sm_count * 128 * 2 * 1.965e9 / 1e12
         peak_src = "nominal FP32 CUDA-core peak (SMs x 128 lanes x 2 x 1965 MHz); no measured FP32 figure"
@@ -1074,7 +1076,7 @@ def run_prefill(args, cfg):
                          "peak": round(peak, 1), "unit": "TFLOP/s",
                          "frac": round(flops_layer / (attn_ms * 1e-3) / 1e12 / peak, 4),
                          "traffic": None,
-                         "kernel": ("gqa_prefill_tc_kernel<%d> (split TF32, tcgen05)" % cfg["d"]
+                         "kernel": ("gqa_prefill_tc_kernel<%d> (split FP16 S, split TF32 PV, tcgen05)" % cfg["d"]
                                     if tc_path else "gqa_prefill_kernel<%d>" % cfg["d"]),
                          "peak_source": peak_src,
                          "flops_per_launch": flops_layer, "avg_launch_ms": round(attn_ms, 4)},
