@@ -70,10 +70,12 @@ struct TcShape {
   static_assert(D == 64 || D == 128, "tensor-core prefill: head_dim 64 or 128");
   static constexpr int BN = kTcBN;
   static constexpr int kKTile = BN * D * 2;  // one FP16 half (h0 or h1) of a K tile (bytes)
-  // V tiles are transposed with a 16-byte gap after each 4-key chunk
-  // (leading byte offset D*16 + 16), so the chunks a warp's stores span fall
-  // on different banks.
-  static constexpr int kVChunk = D * 16 + 16;
+  // V tiles are transposed: 4-key chunks (leading byte offset kVChunk) of
+  // 8-dim core matrices 160 bytes apart (stride byte offset), with a
+  // 16-byte gap after each chunk, so the 32 lanes of a converter warp's
+  // scalar stores (8 keys x 4 dim groups) fall on 32 different banks.
+  static constexpr int kVSbo = 160;  // bytes between 8-dim core matrices of a 4-key chunk
+  static constexpr int kVChunk = (D / 8) * kVSbo + 16;
   static constexpr int kVTile = (BN / 4) * kVChunk;  // one TF32 half of a V tile
   static constexpr int kKInv = BN * 4;               // the keys' inverse scales (floats)
   static constexpr int kStage = 2 * kKTile + 2 * kVTile + kKInv;
@@ -96,7 +98,7 @@ struct TcShape {
   }
   // V tile half transposed, K-major B of O (N = dims, K = keys): 8 dims x 4 keys
   __device__ static int v_off(int key, int dim) {
-    return (key >> 2) * kVChunk + (dim >> 3) * 128 + (dim & 7) * 16 + (key & 3) * 4;
+    return (key >> 2) * kVChunk + (dim >> 3) * kVSbo + (dim & 7) * 16 + (key & 3) * 4;
   }
 };
 
@@ -551,8 +553,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc::fence_after();
       if (!*abort_flag) {
         const uint32_t vb = ptx::smem_u32(smem + st * TS::kStage + 2 * TS::kKTile);
-        const uint64_t bh0 = tc::sdesc(vb, TS::kVChunk, 128);
-        const uint64_t bl0 = tc::sdesc(vb + TS::kVTile, TS::kVChunk, 128);
+        const uint64_t bh0 = tc::sdesc(vb, TS::kVChunk, TS::kVSbo);
+        const uint64_t bl0 = tc::sdesc(vb + TS::kVTile, TS::kVChunk, TS::kVSbo);
 #pragma unroll
         for (int k = 0; k < BN / 8; ++k) {  // O += Ph Vh + Ph Vl + Pl Vh over keys 8k..8k+7
           const uint64_t step = (uint64_t)((2 * k * TS::kVChunk) >> 4);
