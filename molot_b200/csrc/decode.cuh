@@ -747,15 +747,21 @@ __device__ __forceinline__ void fused_new_row(const DecodeArgs& a, const SegView
 // float4 chunk of o[G][D] and a share (csplit) of the partials, issuing up
 // to 16 partials' loads before merging them with online rescaling; shares
 // are folded through `red` ([256][6] floats of shared memory).
+// Slot of the first CTA's partial record: its second piece unless its own
+// range starts in the segment.  Computed before the ticket, off the path.
+__device__ __forceinline__ int combine_slot_first(const DecodeArgs& a, const SegView& sv,
+                                                  long long cf) {
+  return 2 * (int)cf + (range_begin(a, (int)cf) >= sv.gbeg ? 0 : 1);
+}
+
 template <int D>
-__device__ __forceinline__ void combine_segment(const DecodeArgs& a, int s, const SegView& sv,
-                                                long long cf, long long cl, float* red, int ctid,
+__device__ __forceinline__ void combine_segment(const DecodeArgs& a, int slot_first, long long cf,
+                                                long long cl, float* red, int ctid,
                                                 float* out_seg) {
   constexpr int kBatch = 16;
   const int G = a.G;
   const int psz = partial_record_floats(G, D);
   const int nc = (int)(cl - cf + 1);
-  const int slot_first = 2 * (int)cf + (range_begin(a, (int)cf) >= sv.gbeg ? 0 : 1);
   const int nchunk = G * D / 4;
   const int csplit = max(1, (kConsumerWarps * 32) / nchunk);
   for (int task = ctid; task < nchunk * csplit; task += kConsumerWarps * 32) {
@@ -806,10 +812,11 @@ __device__ __forceinline__ void combine_segment(const DecodeArgs& a, int s, cons
     }
     if (csplit == 1) {
       float* dst = out_seg + chunk * 4;
-      put_out(a, dst + 0, acc.x / L);
-      put_out(a, dst + 1, acc.y / L);
-      put_out(a, dst + 2, acc.z / L);
-      put_out(a, dst + 3, acc.w / L);
+      const float inv = 1.f / L;  // one division per chunk
+      put_out(a, dst + 0, acc.x * inv);
+      put_out(a, dst + 1, acc.y * inv);
+      put_out(a, dst + 2, acc.z * inv);
+      put_out(a, dst + 3, acc.w * inv);
     } else {
       // csplit > 1 implies nchunk * csplit <= 256: the task fits `red`.
       float* r = red + (size_t)task * 6;
@@ -837,10 +844,11 @@ __device__ __forceinline__ void combine_segment(const DecodeArgs& a, int s, cons
       acc.w += r[5] * f;
     }
     float* dst = out_seg + chunk * 4;
-    put_out(a, dst + 0, acc.x / L);
-    put_out(a, dst + 1, acc.y / L);
-    put_out(a, dst + 2, acc.z / L);
-    put_out(a, dst + 3, acc.w / L);
+    const float inv = 1.f / L;
+    put_out(a, dst + 0, acc.x * inv);
+    put_out(a, dst + 1, acc.y * inv);
+    put_out(a, dst + 2, acc.z * inv);
+    put_out(a, dst + 3, acc.w * inv);
   }
 }
 
@@ -1380,9 +1388,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
         const long long cf = seg_cta_sm[0];
         const long long cl = seg_cta_sm[1];
         if (ctid == 0) *ticket_sm = ptx::atom_add_acq_rel_gpu(a.counters + s, 1);
+        const int slot_first = combine_slot_first(a, sv, cf);  // while the ticket is out
         ptx::named_bar_sync(1, kConsumerWarps * 32);
         if (*ticket_sm == (int)(cl - cf)) {
-          combine_segment<D>(a, s, sv, cf, cl, merge_o, ctid, out_seg);
+          combine_segment<D>(a, slot_first, cf, cl, merge_o, ctid, out_seg);
           if (ctid == 0) a.counters[s] = 0;
         }
         ptx::named_bar_sync(1, kConsumerWarps * 32);
