@@ -295,16 +295,7 @@ int decode_uniform(Workspace& ws, const float* Q, float* O, const void* K, const
   UniformPlan up =
       plan_uniform(NB, nkv, nblk, sm_count(dev), max_active_clusters(k, kClusterCtas, dev),
                    max_active_clusters(k, kClusterCtasWide, dev));
-  {
-    // Launches of under 8 FP32-sized tiles per CTA (cfg1's 4096 slots): every
-    // segment the same number of CTAs, the grid rounded down to a multiple
-    // of nkv, measured faster there (cfg1 0.425 -> 0.417 ms per token); the
-    // longer launches keep every SM (cfg2 measured 0.3 % slower rounded).
-    const long long rows_full = (long long)nblk * kBlk * nkv / up.grid;
-    if (up.cluster < 2 && up.aligned && up.grid >= 2 * nkv &&
-        rows_full < 8LL * TileShape<128, float>::T)
-      up.grid -= up.grid % nkv;
-  }
+  balance_uniform_grid(up, nkv, nblk);
   const int grid = up.grid;
   const int G = nq / nkv;
   if ((rc = ws.ensure(dev, (size_t)2 * grid * partial_record_floats(G, d), nkv, 0))) return rc;

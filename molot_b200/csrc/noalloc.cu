@@ -171,9 +171,10 @@ extern "C" int molot_attn_decode_strided_noalloc(const float* Q, const float* K,
   if (e != cudaSuccess) return cuda_err(e, "cudaFuncSetAttribute");
   // The partition of molot_attn_decode_strided_dev (at most kNoAllocMaxGrid
   // CTAs, which covers one per SM of a B200).
-  const UniformPlan up = plan_uniform(NB, nkv, nblk, sms < kNoAllocMaxGrid ? sms : kNoAllocMaxGrid,
-                                      max_active_clusters(k, kClusterCtas, dev),
-                                      max_active_clusters(k, kClusterCtasWide, dev));
+  UniformPlan up = plan_uniform(NB, nkv, nblk, sms < kNoAllocMaxGrid ? sms : kNoAllocMaxGrid,
+                                max_active_clusters(k, kClusterCtas, dev),
+                                max_active_clusters(k, kClusterCtasWide, dev));
+  balance_uniform_grid(up, nkv, nblk);
   const int grid = up.grid;
 
   float* partials = reinterpret_cast<float*>(scratch);
