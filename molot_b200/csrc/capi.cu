@@ -308,11 +308,11 @@ int decode_uniform(Workspace& ws, const float* Q, float* O, const void* K, const
   // builds that row, in a decode right after the append that wrote it, it
   // can only stream that row once the append has completed.  Half a share
   // of slots for it measured best (cfg2 fused step, FP32 and BF16 caches),
-  // a quarter on unclustered launches of under 8 tiles per CTA (cfg1 0.4167
-  // -> 0.4135 ms per token); the two forms keep one partition, so their
-  // results stay bit-identical.
-  const bool short_launch =
-      up.cluster < 2 && (long long)nblk * kBlk * nkv / grid < 8LL * 64;
+  // a quarter on launches of under 8 tiles per CTA (cfg1 0.4167 -> 0.4135
+  // ms per token; cfg3's clustered sliding-window layers 0.549 -> 0.533 ms
+  // per token); the two forms keep one partition, so their results stay
+  // bit-identical.
+  const bool short_launch = (long long)nblk * kBlk * nkv / grid < 8LL * 64;
   a.tail_w = (fused || prefetch_old_rows) ? (short_launch ? kShareW * 3 / 4 : kShareW / 2) : 0;
   {
     // Split K/V stage barriers where they measured faster (see the kernel).
